@@ -1,0 +1,450 @@
+"""Benchmark of the B200 TensorRegion engine (one JSON line on rank 0).
+
+Default workload: the i64 elementwise region out = (a + b) * a - b on
+[8192, 8192] i64 with a, b uniform integers in [-1000, 1000] (seed 1), checked
+for overflow, row-sharded over the ranks (8192 / N rows each, no collective).
+A step is one pass of the fused region kernel over the rank's shard.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+                    [--workload i64_region|f32_chain|softmax]
+
+value     device-timed aggregate GB/s (algorithmic bytes: 24 B per element,
+          a and b read, out written), inputs resident in HBM; max over ranks.
+e2e       the same metric through the public host API (thb_region_execute):
+          every step copies the inputs host->device from pinned memory, runs
+          the region, reads the result back and checks the error word.
+roofline  the fused kernel's achieved GB/s vs the measured HBM copy peak.
+The working set (1.5 GiB per step at N=1) is far above the 126 MB L2, so no
+L2 flush is needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "fused-region GB/s and % HBM peak (device-timed) at 1/2/4/8 B200; MLP TFLOP/s"
+REF_REGION = {"i64_region": os.path.join(ROOT, "oracle", "_ref", "region_i64_region.so"),
+              "f32_chain": os.path.join(ROOT, "oracle", "_ref", "region_f32_chain.so")}
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic(name):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", f"{name}.ncu.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f).get("dram_bytes_per_launch")
+    return None
+
+
+# ---- workloads ---------------------------------------------------------------------
+
+class Workload:
+    name = ""
+    bytes_per_element = 0
+    dtype = ""
+    ncu_name = ""
+
+    def config(self, world):
+        raise NotImplementedError
+
+
+class I64Region(Workload):
+    name = "i64_region"
+    bytes_per_element = 24
+    dtype = "int64"
+    rows, cols = 8192, 8192
+    ncu_name = "i64_region_8192x8192"
+
+    def build(self, torch, rank, world):
+        from thiran_b200 import regions
+        rows = self.rows // world
+        g = torch.Generator(device="cuda").manual_seed(1 + 1000 * rank)
+        a = torch.randint(-1000, 1001, (rows, self.cols), dtype=torch.int64, device="cuda", generator=g)
+        b = torch.randint(-1000, 1001, (rows, self.cols), dtype=torch.int64, device="cuda", generator=g)
+        out = torch.empty_like(a)
+        return regions.i64_region(), [a, b], out
+
+    def config(self, world):
+        return {"workload": "i64 region (a+b)*a-b, [8192,8192] i64, uniform ints [-1000,1000] seed 1, overflow-checked",
+                "global_shape": [self.rows, self.cols], "shard": f"rows/{world} per rank",
+                "parallelism": f"row-sharded x{world}, no collective",
+                "l2": "working set 1.5 GiB/step >> 126 MB L2 (no flush needed)"}
+
+
+class F32Chain(Workload):
+    name = "f32_chain"
+    bytes_per_element = 8
+    dtype = "f32"
+    n = 1 << 28
+    ncu_name = "f32_chain_2p28"
+
+    def build(self, torch, rank, world):
+        from thiran_b200 import regions
+        g = torch.Generator(device="cuda").manual_seed(2 + 1000 * rank)
+        x = torch.rand(self.n // world, device="cuda", generator=g) * 2 - 1
+        return regions.f32_chain(), [x], torch.empty_like(x)
+
+    def config(self, world):
+        return {"workload": "f32 chain ((x*1.5+0.25)*x-x)*0.5+x on 2^28 f32, uniform[-1,1] seed 2",
+                "global_shape": [self.n], "shard": f"elements/{world} per rank",
+                "parallelism": f"sharded x{world}, no collective", "l2": "2 GiB/step >> L2"}
+
+
+class Softmax(Workload):
+    name = "softmax"
+    bytes_per_element = 8
+    dtype = "f32"
+    rows, cols = 65536, 4096
+    ncu_name = "softmax_65536x4096"
+
+    def build(self, torch, rank, world):
+        from thiran_b200 import regions
+        g = torch.Generator(device="cuda").manual_seed(3 + 1000 * rank)
+        x = torch.randn((self.rows // world, self.cols), device="cuda", generator=g)
+        return regions.softmax_rows(), [x], torch.empty_like(x)
+
+    def config(self, world):
+        return {"workload": "row softmax on [65536,4096] f32 ~ N(0,1) seed 3",
+                "global_shape": [self.rows, self.cols], "shard": f"rows/{world} per rank",
+                "parallelism": f"row-sharded x{world}, no collective", "l2": "2 GiB/step >> L2"}
+
+
+WORKLOADS = {w.name: w for w in (I64Region(), F32Chain(), Softmax())}
+
+
+# ---- clocks ------------------------------------------------------------------------
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.1)
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        self.file.seek(0)
+        rows = [r.split(", ") for r in self.file.read().strip().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in rows if len(r) >= 9 for k in range(4) if r[5 + k].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows), "window": "warm-up + timed region, 50 ms sampling"}
+
+
+# ---- CPU baseline (reference CPU path) ----------------------------------------------
+
+class RefArg(C.Structure):
+    _fields_ = [("kind", C.c_uint32), ("dtype", C.c_uint32), ("rank", C.c_uint32), ("reserved", C.c_uint32),
+                ("shape", C.POINTER(C.c_uint64)), ("data", C.c_void_p), ("count", C.c_uint64)]
+
+
+def reference_entry(workload):
+    """The reference's native CPU region (emitted by its NativeCpu emitter and
+    compiled like its JIT, built by oracle/Makefile), or None."""
+    path = REF_REGION.get(workload.name)
+    if not path or not os.path.exists(path):
+        return None
+    lib = C.CDLL(path)
+    fn = lib.thiran_ref_entry
+    fn.restype = C.c_int
+    fn.argtypes = [C.POINTER(RefArg), C.c_uint64, C.c_void_p, C.c_uint64, C.c_char_p, C.c_uint64]
+    return fn
+
+
+def cpu_inputs(workload, rows):
+    rng = np.random.default_rng(1)
+    if workload.name == "i64_region":
+        a = rng.integers(-1000, 1001, (rows, workload.cols), dtype=np.int64)
+        b = rng.integers(-1000, 1001, (rows, workload.cols), dtype=np.int64)
+        return [a, b], np.empty_like(a)
+    if workload.name == "f32_chain":
+        x = rng.uniform(-1, 1, rows * 8192).astype(np.float32)
+        return [x], np.empty_like(x)
+    x = rng.standard_normal((rows, workload.cols)).astype(np.float32)
+    return [x], np.empty_like(x)
+
+
+def call_reference(fn, inputs, out):
+    keep = []
+    args = (RefArg * len(inputs))()
+    for k, a in enumerate(inputs):
+        shape = (C.c_uint64 * a.ndim)(*a.shape)
+        keep.append(shape)
+        args[k] = RefArg(2, 1 if a.dtype == np.int64 else 2, a.ndim, 0, shape, a.ctypes.data, a.size)
+    fail = C.create_string_buffer(256)
+    status = fn(args, len(inputs), out.ctypes.data, out.size, fail, 256)
+    if status != 0:
+        raise RuntimeError(f"reference CPU path failed: {status} {fail.value.decode()}")
+
+
+def time_cpu(workload, threads, rows_per_thread, repeats):
+    """Times the reference CPU path (or the oracle port) over `threads` host
+    threads, each on its own `rows_per_thread` rows; returns (GB/s, kind, sample)."""
+    fn = reference_entry(workload)
+    kind = "reference"
+    if fn is None:
+        sys.path.insert(0, os.path.join(ROOT, "tests"))
+        import oracle_lib
+        from thiran_b200 import regions
+        spec = regions.i64_region() if workload.name == "i64_region" else regions.f32_chain() \
+            if workload.name == "f32_chain" else regions.softmax_rows()
+        kind = "port"
+
+        def fn_port(inputs, out):
+            out[...] = oracle_lib.region_eval(spec, inputs)
+    work = [cpu_inputs(workload, rows_per_thread) for _ in range(threads)]
+    elements = sum(o.size for _, o in work)
+
+    def run(k):
+        inputs, out = work[k]
+        for _ in range(repeats):
+            if kind == "reference":
+                call_reference(fn, inputs, out)
+            else:
+                fn_port(inputs, out)
+
+    start = time.perf_counter()
+    pool = [threading.Thread(target=run, args=(k,)) for k in range(threads)]
+    for t in pool:
+        t.start()
+    for t in pool:
+        t.join()
+    elapsed = time.perf_counter() - start
+    gbs = elements * repeats * workload.bytes_per_element / elapsed / 1e9
+    sample = (f"{threads} thread(s) x {rows_per_thread} rows x {repeats} call(s) "
+              f"({elements * repeats} elements) of the same region, {elapsed:.2f} s")
+    return gbs, kind, sample, elapsed
+
+
+def _reference_worker(name, rows, calls, start, done):
+    """One host process of the reference arm: its own inputs, `calls` calls."""
+    workload = WORKLOADS[name]
+    fn = reference_entry(workload)
+    inputs, out = cpu_inputs(workload, rows)
+    call_reference(fn, inputs, out)  # warm (page-in, allocator)
+    for _ in range(calls):
+        start.wait()
+        call_reference(fn, inputs, out)
+        done.wait()
+
+
+def reference_arm(args, workload):
+    """Times the reference's own CPU path (emitCpp20 output compiled like its
+    JIT) on all host cores: one process per core (the reference's per-call
+    path is single-threaded and serialises on process-global runtime state),
+    each step every process runs the region once on its own sample rows."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import multiprocessing as mp
+    procs_n = os.cpu_count() or 1
+    rows = 16 if workload.name == "i64_region" else 8
+    kind = "reference"
+    if reference_entry(workload) is None:
+        gbs, kind, sample, _ = time_cpu(workload, 1, rows, args.steps)
+        values = [gbs]
+        cores = 1
+    else:
+        ctx = mp.get_context("spawn")
+        calls = args.warmup + args.steps
+        start, done = ctx.Barrier(procs_n + 1), ctx.Barrier(procs_n + 1)
+        procs = [ctx.Process(target=_reference_worker, args=(workload.name, rows, calls, start, done))
+                 for _ in range(procs_n)]
+        for p in procs:
+            p.start()
+        values = []
+        for step in range(calls):
+            start.wait()
+            t0 = time.perf_counter()
+            done.wait()
+            elapsed = time.perf_counter() - t0
+            if step >= args.warmup:
+                values.append(procs_n * rows * 8192 * workload.bytes_per_element / elapsed / 1e9)
+        for p in procs:
+            p.join()
+        cores = procs_n
+        sample = (f"{procs_n} process(es) x {rows} rows x 8192 of the workload per step, "
+                  f"one reference region call each")
+    value = statistics.median(values)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": workload.dtype, "data": "synthetic",
+            "config": workload.config(1),
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": kind,
+                             "sample": f"per step: {sample}"},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---- GPU arm -------------------------------------------------------------------------
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="engine", choices=["engine", "reference"])
+    p.add_argument("--workload", default="i64_region", choices=sorted(WORKLOADS))
+    p.add_argument("--e2e-steps", type=int, default=None)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    args = p.parse_args()
+    workload = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        return reference_arm(args, workload)
+
+    import torch
+    import torch.distributed as dist
+    import datetime
+    import thiran_b200 as thb
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    spec, inputs, out = workload.build(torch, rank, world)
+    region = spec.compile(local)
+    stream = torch.cuda.Stream()
+    s = stream.cuda_stream
+    elements = out.numel()
+    bytes_per_step_rank = elements * workload.bytes_per_element
+
+    # Warm-up (also JIT/module load and slot allocation).
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            region.launch(inputs, out, s)
+    region.check_errors(s)
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for k in range(args.steps):
+            starts[k].record(stream)
+            region.launch(inputs, out, s)
+            ends[k].record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    region.check_errors(s)
+    per_launch_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    total_ms = starts[0].elapsed_time(ends[-1])
+    total_ms = max_over_ranks(total_ms)
+    ms_per_step = total_ms / args.steps
+    value = bytes_per_step_rank * world * args.steps / (total_ms / 1e3) / 1e9
+
+    # Roofline of the dominant (only) kernel.
+    peak, peak_kind = measured_peaks()
+    launch_ms = statistics.mean(per_launch_ms)
+    achieved = bytes_per_step_rank / (launch_ms / 1e3) / 1e9
+    traffic = ncu_traffic(workload.ncu_name) if world == 1 else None
+
+    # End to end through the public host API, pinned host buffers.
+    host_inputs = [t.cpu().pin_memory() for t in inputs]
+    host_np = [t.numpy() for t in host_inputs]
+    host_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    host_out_np = host_out.numpy()
+    e2e_steps = args.e2e_steps or max(3, min(args.steps, 20))
+    region_host = spec.compile(local)
+    region_host.execute(host_np, out=host_out_np)  # warm
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        region_host.execute(host_np, out=host_out_np)
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    e2e_value = bytes_per_step_rank * world * e2e_steps / e2e_s / 1e9
+    h2d = sum(t.numel() * t.element_size() for t in inputs)
+    d2h = out.numel() * out.element_size()
+
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rows = 1024 if workload.name == "i64_region" else 128
+        gbs, kind, sample, _ = time_cpu(workload, 1, rows, 2)
+        cpu_baseline = {"value": gbs, "unit": "GB/s", "cores": 1, "kind": kind,
+                        "sample": f"{sample}; the reference CPU path is single-threaded"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": workload.dtype, "data": "synthetic (torch.Generator on device, seeded)",
+            "config": workload.config(world),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "kernel": "generated fused elementwise group (NVRTC, sm_100a)",
+                         "algorithmic_bytes_per_launch": bytes_per_step_rank,
+                         "avg_launch_ms": launch_ms, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
+            "cpu_baseline": cpu_baseline,
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "steps": e2e_steps, "api": "thb_region_execute (host buffers, pinned)"},
+            "gpu_launches": args.steps * 1,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    del region, region_host
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

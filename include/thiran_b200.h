@@ -1,0 +1,329 @@
+/*
+ * thiran_b200.h — C ABI of the B200-native execution engine for Thiran's
+ * TensorRegion hot path.
+ *
+ * Every entry point is extern "C", takes plain pointers and sizes, and
+ * returns one of the THB_STATUS_* codes below. Failures write a NUL-terminated
+ * text into the caller's (failure, failure_cap) buffer; for a checked semantic
+ * failure that text is exactly the failure id (for example
+ * "TH-SPEC-I64-OVERFLOW"), for every other failure it is "CODE: message".
+ * This is the convention of the reference's native CPU artifact entry
+ * `thiran_v0_entry` (src/artifact/v0/NativeArtifacts.cpp:631-700).
+ *
+ * Nothing here ever falls back to a CPU implementation: when the CUDA driver
+ * or device is missing the call fails with GPU-DRIVER-NOT-FOUND /
+ * GPU-INVALID-DEVICE.
+ */
+#ifndef THIRAN_B200_H
+#define THIRAN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define THB_ABI_VERSION 1u
+
+/* Return codes. 0..4 keep the meaning of thiran_v0_entry's return values
+ * (src/artifact/v0/NativeArtifacts.cpp:693-697). */
+enum {
+    THB_STATUS_OK = 0,
+    THB_STATUS_ABI = 1,      /* arity / type / shape / layout / malformed region */
+    THB_STATUS_SEMANTIC = 2, /* checked failure; the failure id is in the buffer */
+    THB_STATUS_BACKEND = 3,  /* driver / device / launch failure */
+    THB_STATUS_UNKNOWN = 4
+};
+
+/* Element dtypes. I64 and F32 use the artifact ABI codes
+ * (src/artifact/v0/NativeArtifacts.cpp:130-134); BF16 is an engine addition
+ * used only for tensor-core GEMM operands. */
+enum { THB_DTYPE_I64 = 1, THB_DTYPE_F32 = 2, THB_DTYPE_BF16 = 3 };
+
+/* Value kinds (include/artifact/v0/NativeArtifacts.hpp:22). */
+enum { THB_KIND_SCALAR = 1, THB_KIND_TENSOR = 2 };
+
+/* RegionOp, numbered exactly as include/backend/v0/TensorRegion.hpp:14-28. */
+enum {
+    THB_OP_INPUT = 0,
+    THB_OP_INTEGER = 1,
+    THB_OP_FLOAT = 2,
+    THB_OP_TENSOR_LITERAL = 3,
+    THB_OP_ALIAS = 4,
+    THB_OP_COPY = 5,
+    THB_OP_NEGATE = 6,
+    THB_OP_ADD = 7,
+    THB_OP_SUBTRACT = 8,
+    THB_OP_ELEMENT_MULTIPLY = 9,
+    THB_OP_EXTENSION = 10,
+    THB_OP_INDEX = 11,
+    THB_OP_UNSUPPORTED = 12,
+    /* Engine additions. The reference executes these only in its Evaluator
+     * (src/semantic/v0/Evaluator.cpp) and rejects them natively
+     * (src/backend/v0/TensorRegion.cpp:424-431). */
+    THB_OP_SUM = 32,     /* sum(A, axis): Evaluator.cpp:214-251; axis in node.axis */
+    THB_OP_ROW_MAX = 33, /* max over the last axis */
+    THB_OP_SOFTMAX = 34, /* softmax over the last axis (RegionPythonEmitter.cpp:293-294) */
+    THB_OP_RELU = 35     /* max(x, 0) (PythonExecutorEmitter.cpp:94) */
+};
+
+/* Scalar recipe opcodes (include/extension/v0/Extension.hpp:16-17). */
+enum {
+    THB_SCALAR_INPUT = 1,
+    THB_SCALAR_CONSTANT_F32 = 2,
+    THB_SCALAR_ADD = 3,
+    THB_SCALAR_SUBTRACT = 4,
+    THB_SCALAR_MULTIPLY = 5,
+    THB_SCALAR_DIVIDE = 6,
+    THB_SCALAR_NEGATE = 7
+};
+
+/* Operation effects and backend mask (include/extension/v0/Extension.hpp:31-32). */
+enum { THB_EFFECT_PURE = 0, THB_EFFECT_MAY_TRAP = 1 };
+enum { THB_BACKEND_REFERENCE = 1, THB_BACKEND_CPU = 2, THB_BACKEND_GPU = 4 };
+
+/* Layout-compatible with ScalarNodeV0 / ScalarRecipeV0 / DerivativeV0 /
+ * OperationDescriptorV0 (include/extension/v0/Extension.hpp:18-53), so the
+ * descriptor an extension plugin returns from thiran_extension_v0() can be
+ * passed here unchanged. C++ bool is one byte; uint8_t stands in for it. */
+typedef struct thb_scalar_node {
+    uint8_t opcode;
+    uint32_t left;
+    uint32_t right;
+    uint32_t input;
+    float constant;
+} thb_scalar_node;
+
+typedef struct thb_scalar_recipe {
+    const thb_scalar_node* nodes;
+    size_t node_count;
+    uint32_t root;
+    uint32_t input_count;
+} thb_scalar_recipe;
+
+typedef struct thb_derivative {
+    uint64_t differentiable_inputs;
+    uint64_t saved_inputs;
+    uint8_t saves_output;
+    const thb_scalar_recipe* gradients;
+    size_t gradient_count;
+} thb_derivative;
+
+typedef struct thb_operation {
+    const char* name;
+    const char* semantic_version;
+    uint32_t arity;
+    uint32_t minimum_rank;
+    uint32_t maximum_rank;
+    uint32_t result_like_input;
+    uint8_t same_shape;
+    uint8_t effect;
+    uint32_t backends;
+    uint8_t fusible;
+    thb_scalar_recipe forward;
+    const thb_derivative* derivative;
+} thb_operation;
+
+/* One TensorRegion node (RegionNode, include/backend/v0/TensorRegion.hpp:30-47).
+ * rank 0 is a scalar of `dtype`; rank 1..2 is a contiguous row-major tensor.
+ * An extent of -1 is unknown until execution. */
+typedef struct thb_region_node {
+    uint32_t id;
+    uint32_t op;
+    uint32_t dtype;
+    uint32_t rank;
+    int64_t extent[2];
+    const uint32_t* dependencies;
+    uint32_t dependency_count;
+    const uint32_t* indices;
+    uint32_t index_count;
+    int64_t integer;
+    float floating;
+    int32_t axis;
+    const thb_operation* extension;
+} thb_region_node;
+
+/* TensorRegion (TensorRegion.hpp:49-57). */
+typedef struct thb_region_desc {
+    uint32_t function;
+    const char* name;
+    const thb_region_node* nodes;
+    uint32_t node_count;
+    const uint32_t* inputs;
+    uint32_t input_count;
+    uint32_t output;
+} thb_region_desc;
+
+/* PhysicalPlanOptions (include/backend/v0/PhysicalPlan.hpp:37-41). */
+typedef struct thb_plan_options {
+    uint32_t enable_reuse;
+    uint32_t enable_fusion;
+} thb_plan_options;
+
+/* Argument record, layout-identical to ThiranAbiArg
+ * (src/artifact/v0/NativeArtifacts.cpp:702-708). For tensors `data` is a host
+ * pointer in thb_region_execute / thb_region_submit and a device pointer in
+ * thb_region_launch. Bit 0 of `reserved` marks a view / non-contiguous /
+ * offset tensor, which is rejected with GPU-UNSUPPORTED-LAYOUT
+ * (src/backend/v0/NativeGpu.cpp:94-96). */
+typedef struct thb_abi_arg {
+    uint32_t kind;
+    uint32_t dtype;
+    uint32_t rank;
+    uint32_t reserved;
+    const uint64_t* shape;
+    const void* data;
+    uint64_t count;
+} thb_abi_arg;
+
+/* GpuExecutionEvidence (include/backend/v0/NativeGpu.hpp:52-87), same
+ * fields in the same order. Under the persistent runtime moduleLoads and
+ * driverJitLoads count cache misses, allocationCount counts pool misses. */
+typedef struct thb_evidence {
+    uint64_t allocation_count;
+    uint64_t allocation_bytes_requested;
+    uint64_t host_to_device_copies;
+    uint64_t host_to_device_bytes;
+    uint64_t device_to_host_copies;
+    uint64_t device_to_host_bytes;
+    uint64_t device_to_device_copies;
+    uint64_t device_to_device_bytes;
+    uint64_t module_loads;
+    uint64_t driver_jit_loads;
+    uint64_t input_storage_uploads;
+    uint64_t result_downloads;
+    uint64_t kernel_launches;
+    uint64_t synchronizations;
+    uint64_t submitted_operations;
+    uint64_t pending_operations;
+    uint64_t active_read_reservations;
+    uint64_t active_write_reservations;
+    uint64_t stream_submissions;
+    uint64_t event_records;
+    uint64_t observations;
+    uint64_t dropped_drains;
+    uint64_t released_reservations;
+    uint64_t logical_tensor_values;
+    uint64_t logical_intermediates;
+    uint64_t materialized_intermediates;
+    uint64_t physical_slots;
+    uint64_t physical_temporary_slots;
+    uint64_t reused_slot_assignments;
+    uint64_t fusion_groups;
+    uint64_t fused_kernel_groups;
+    uint64_t planner_owned_allocations;
+    uint64_t retained_planner_allocations;
+} thb_evidence;
+
+/* GpuDeviceInfo (include/backend/v0/NativeGpu.hpp:37-48). */
+typedef struct thb_device_info {
+    int32_t backend_built;
+    int32_t driver_loaded;
+    int32_t device_available;
+    int32_t device_count;
+    int32_t selected_device;
+    int32_t driver_version;
+    int32_t compute_major;
+    int32_t compute_minor;
+    int32_t sm_count;
+    int32_t reserved;
+    char name[256];
+    char error_code[64];
+} thb_device_info;
+
+typedef struct thb_region thb_region;
+typedef struct thb_pending thb_pending;
+
+/* ---- backend identity (include/backend/v0/NativeGpu.hpp:96-102) ------ */
+
+/* nativeGpuBackendBuilt() (NativeGpu.hpp:96). Always 1 for this library. */
+int thb_backend_built(void);
+/* ABI version of this header. */
+uint32_t thb_abi_version(void);
+/* probeNativeGpu(int) (NativeGpu.hpp:102). Never throws; fills `out`. */
+int thb_probe(int device, thb_device_info* out);
+
+/* ---- regions (include/backend/v0/NativeGpu.hpp:200-226) ------------- */
+
+/* Verifies the region (TensorRegion.cpp:103-228 rules), builds the physical
+ * plan (PhysicalPlan.cpp:366-482: fusion groups, slots), generates one CUDA
+ * kernel per elementwise fusion group and compiles it for sm_100a through
+ * NVRTC (cached by digest). Replaces buildPhysicalPlan + plannedPtx + the
+ * per-call cuModuleLoadDataEx of submitNativeGpuAsync (NativeGpu.cpp:1524,
+ * :590, :602). Failure: THB_STATUS_ABI with GPU-INVALID-REGION etc. */
+int thb_region_compile(const thb_region_desc* region, thb_plan_options options, int device,
+                       thb_region** out, char* failure, uint64_t failure_cap);
+void thb_region_release(thb_region* region);
+
+/* executeNativeGpu(region, inputs, device, options) (NativeGpu.hpp:219-222):
+ * host inputs are uploaded, the plan runs on the region's stream, the result
+ * (output_count elements of the output dtype) is downloaded and the call
+ * synchronises. `evidence` may be NULL. */
+int thb_region_execute(thb_region* region, const thb_abi_arg* args, uint64_t argc,
+                       void* output, uint64_t output_count, thb_evidence* evidence,
+                       char* failure, uint64_t failure_cap);
+
+/* submitNativeGpuAsync (NativeGpu.hpp:200-203): preflight, upload and launch,
+ * then return a pending handle without synchronising. The host input buffers
+ * must stay unchanged until the handle is observed or released. */
+int thb_region_submit(thb_region* region, const thb_abi_arg* args, uint64_t argc,
+                      thb_pending** out, thb_evidence* evidence,
+                      char* failure, uint64_t failure_cap);
+/* PendingGpuExecution::state(): 0 pending, 1 complete. */
+int thb_pending_state(const thb_pending* pending);
+/* PendingGpuExecution::observe() (NativeGpu.hpp:122): waits (bounded by
+ * `timeout_ms`, 0 = wait without limit), checks the error words, copies the
+ * value out. May be called again; later calls return the same outcome. */
+int thb_pending_observe(thb_pending* pending, void* output, uint64_t output_count,
+                        uint64_t timeout_ms, thb_evidence* evidence,
+                        char* failure, uint64_t failure_cap);
+/* Dropping a PendingGpuExecution: an unobserved handle is drained and its
+ * failure, if any, is queued for thb_take_unobserved_errors. */
+void thb_pending_release(thb_pending* pending);
+/* runtime::takeUnobservedAsyncErrors() (include/runtime/v0/Async.hpp:165):
+ * writes the queued failure ids, newline separated, and clears the queue.
+ * Returns the number of ids. */
+uint64_t thb_take_unobserved_errors(char* buffer, uint64_t capacity);
+
+/* Device-resident, stream-ordered launch: tensors in `args` and `output` are
+ * device pointers on the region's device; nothing is copied and nothing
+ * synchronises. Checked failures latch into the region's error words until
+ * thb_region_check_errors reads and clears them. `stream` is a cudaStream_t
+ * (NULL = legacy default stream). This is the hot path the benchmark times. */
+int thb_region_launch(thb_region* region, const thb_abi_arg* args, uint64_t argc,
+                      void* output, uint64_t output_count, void* stream,
+                      char* failure, uint64_t failure_cap);
+/* Synchronises `stream`, reads and clears the latched error words; returns
+ * THB_STATUS_SEMANTIC with the failure id of the first failing fusion group
+ * in region order, else THB_STATUS_OK. */
+int thb_region_check_errors(thb_region* region, void* stream, char* failure, uint64_t failure_cap);
+
+/* emitNativeGpuPtx(region, options) (NativeGpu.hpp:101): the generated CUDA
+ * source of all fusion groups (this engine's payload text). Writes up to
+ * `capacity` bytes including the NUL; `needed` receives the full size. */
+int thb_region_emit_source(const thb_region* region, char* buffer, uint64_t capacity, uint64_t* needed);
+/* PhysicalPlan::dump() (include/backend/v0/PhysicalPlan.hpp:125). */
+int thb_region_dump_plan(const thb_region* region, char* buffer, uint64_t capacity, uint64_t* needed);
+/* Plan structure: number of fusion groups and how many of them fused >1 node. */
+int thb_region_plan_counts(const thb_region* region, uint64_t* fusion_groups, uint64_t* fused_groups,
+                           uint64_t* kernels);
+
+/* Device-free planning, as emitNativeGpuPtx(region, options) is in the
+ * reference (NativeGpu.hpp:101): verifies and plans the region without
+ * touching the driver and writes `what` into `buffer`:
+ *   THB_DESCRIBE_PLAN   region dump + physical plan dump,
+ *   THB_DESCRIBE_SOURCE generated CUDA source,
+ *   THB_DESCRIBE_CUBIN  compiles the source with NVRTC for sm_100a and writes
+ *                       the cubin size in bytes as decimal text.
+ * counts (optional, 3 entries): fusion groups, fused groups, kernel groups. */
+enum { THB_DESCRIBE_PLAN = 0, THB_DESCRIBE_SOURCE = 1, THB_DESCRIBE_CUBIN = 2 };
+int thb_region_describe(const thb_region_desc* region, thb_plan_options options, uint32_t what,
+                        char* buffer, uint64_t capacity, uint64_t* needed, uint64_t* counts,
+                        char* failure, uint64_t failure_cap);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* THIRAN_B200_H */

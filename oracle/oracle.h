@@ -1,0 +1,82 @@
+/*
+ * oracle.h — CPU restatement of the reference's TensorRegion semantics.
+ *
+ * TEST INFRASTRUCTURE ONLY. The engine (thiran_b200/) never links, loads or
+ * calls anything in oracle/; only tests/, __graft_entry__.smoke() and the
+ * cpu_baseline / reference legs of bench.py do, and only as the checker or
+ * the timed CPU baseline.
+ *
+ * Pinning: oracle/ref_driver.cpp compiles the reference's own Evaluator and
+ * NativeCpu emitter from its sources (oracle/Makefile) and
+ * tests/golden/make_golden.py records their outputs as fixtures; the CPU test
+ * suite checks this restatement against those fixtures and against the
+ * known-answer vectors of the reference's tests.
+ */
+#ifndef THIRAN_ORACLE_H
+#define THIRAN_ORACLE_H
+
+#include <stdint.h>
+
+#include "../include/thiran_b200.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Evaluates a region on host values (same thb_abi_arg records the engine's
+ * thb_region_execute takes, host pointers) following the reference's native
+ * CPU semantics: IR-ordered, separately rounded f32 operations
+ * (src/backend/v0/NativeCpu.cpp:251-316), checked i64 arithmetic
+ * (NativeCpu.cpp:116-132), recipe evaluation (src/extension/v0/
+ * Extension.cpp:151-169), checked index (NativeCpu.cpp:133-148). Engine ops:
+ * Relu (torch.relu), Softmax / RowMax / Sum with f64 accumulation.
+ * Returns 0, or 2 with the failure id (TH-SPEC-I64-OVERFLOW, TH-SPEC-BOUNDS,
+ * TH021-DIVIDE-BY-ZERO) in `failure`, or 1 for a malformed call. */
+int orc_region_eval(const thb_region_desc* region, const thb_abi_arg* args, uint64_t argc, void* output,
+                    uint64_t output_count, char* failure, uint64_t failure_cap);
+
+/* Scalar recipe evaluation (Extension.cpp:151-169). Returns 0 or 2
+ * (divide by zero). */
+int orc_recipe_eval(const thb_scalar_recipe* recipe, const float* inputs, float* result);
+
+/* Row softmax over the last axis: m = max, e = exp(x - m) in f64, y = e / sum. */
+void orc_softmax_rows(const float* x, float* y, uint64_t rows, uint64_t cols);
+void orc_max_rows(const float* x, float* y, uint64_t rows, uint64_t cols);
+/* Row sums accumulated in f64 and rounded once. */
+void orc_sum_rows(const float* x, float* y, uint64_t rows, uint64_t cols);
+void orc_sum_cols(const float* x, float* y, uint64_t rows, uint64_t cols);
+/* Full sum: f64 accumulation (the 1e-5 gate) and the reference Evaluator's
+ * sequential f32 order (Evaluator.cpp:221-226). */
+double orc_sum_all_f64(const float* x, uint64_t n);
+float orc_sum_all_sequential_f32(const float* x, uint64_t n);
+
+/* Evaluator matmul order (src/semantic/v0/Evaluator.cpp:125-154): for each
+ * (i, j), acc = 0.0f; acc = acc + a[i,k] * b[k,j] over k in order, every
+ * product and sum rounded to f32. a: [m,k] row-major, b: [k,n] row-major. */
+void orc_matmul_f32(const float* a, const float* b, float* c, uint64_t m, uint64_t k, uint64_t n);
+/* Same product accumulated in f64 and rounded once (used at sizes where the
+ * sequential f32 order itself carries more error than the gate). */
+void orc_matmul_f64acc(const float* a, const float* b, float* c, uint64_t m, uint64_t k, uint64_t n);
+
+/* Rounds f32 values to bf16 (round to nearest even) and back to f32. */
+void orc_round_bf16(const float* x, float* y, uint64_t n);
+
+/* Two-layer MLP step restated from the reference's reverse-AD rules
+ * (src/autodiff/v0/Autodiff.cpp:195-231) and SGD (src/training/v0/
+ * Training.cpp:343-381), with the engine's precision contract: GEMM operands
+ * are rounded to bf16 (X, W1, H, W2, dY, dH), products accumulate in f64.
+ *   H = relu(X W1)          X [b,i], W1 [i,h]
+ *   Y = H W2                W2 [h,o]
+ *   L = mean((Y - T)^2)
+ *   dY = 2 (Y - T) / (b*o)
+ *   dW2 = H^T dY ; dH = (dY W2^T) * [H > 0] ; dW1 = X^T dH
+ *   W1 -= lr dW1 ; W2 -= lr dW2
+ * Outputs: loss, dW1 [i,h], dW2 [h,o], updated W1/W2 in place. */
+double orc_mlp_step(const float* x, const float* t, float* w1, float* w2, uint64_t b, uint64_t i, uint64_t h,
+                    uint64_t o, float lr, float* dw1, float* dw2, float* hidden, float* y);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

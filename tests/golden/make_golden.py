@@ -1,0 +1,222 @@
+"""Generates tests/golden/ fixtures by running the REFERENCE implementation.
+
+Runs only where the reference sources are present: `make -C oracle ref` first
+builds oracle/_ref/ref_driver from them. Each fixture records inputs and the
+reference's output (its Evaluator, src/semantic/v0/Evaluator.cpp, and its
+native CPU path, src/backend/v0/NativeCpu.cpp), plus the reference planner's
+fusion groups. The CPU tests check the oracle against these files and the GPU
+tests check the engine against them.
+
+    python tests/golden/make_golden.py
+"""
+from __future__ import annotations
+
+import ctypes as C
+import json
+import os
+import struct
+import subprocess
+import sys
+import tempfile
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+DRIVER = os.path.join(ROOT, "oracle", "_ref", "ref_driver")
+
+
+def write_thb(path, value):
+    arr = np.asarray(value)
+    dtype = 1 if arr.dtype == np.int64 else 2
+    with open(path, "wb") as f:
+        f.write(b"THB1" + struct.pack("<II", dtype, arr.ndim))
+        for e in arr.shape:
+            f.write(struct.pack("<Q", e))
+        f.write(np.ascontiguousarray(arr).tobytes())
+
+
+def read_thb(path):
+    with open(path, "rb") as f:
+        data = f.read()
+    assert data[:4] == b"THB1"
+    dtype, rank = struct.unpack("<II", data[4:12])
+    shape = struct.unpack("<" + "Q" * rank, data[12:12 + 8 * rank])
+    arr = np.frombuffer(data[12 + 8 * rank:], dtype=np.int64 if dtype == 1 else np.float32)
+    return arr.reshape(shape) if rank else arr[0]
+
+
+def evaluate(program: str, function: str, inputs):
+    """Runs semantic::evaluateCall on the reference; returns (status, value)."""
+    with tempfile.TemporaryDirectory() as tmp:
+        src = os.path.join(tmp, "p.th")
+        with open(src, "w") as f:
+            f.write(program)
+        paths = []
+        for k, v in enumerate(inputs):
+            p = os.path.join(tmp, f"in{k}.bin")
+            write_thb(p, v)
+            paths.append(p)
+        out = os.path.join(tmp, "out.bin")
+        res = subprocess.run([DRIVER, "eval", src, function, out] + paths, capture_output=True, text=True, check=True)
+        status = json.loads(res.stdout.strip().splitlines()[-1])
+        if status["status"] != "ok":
+            return status.get("error_id", "error"), None
+        return "ok", read_thb(out)
+
+
+def plan(program: str, function: str, fusion=True):
+    with tempfile.TemporaryDirectory() as tmp:
+        src = os.path.join(tmp, "p.th")
+        with open(src, "w") as f:
+            f.write(program)
+        args = [DRIVER, "plan", src, function] + ([] if fusion else ["nofusion"])
+        return subprocess.run(args, capture_output=True, text=True, check=True).stdout
+
+
+def groups_of(dump: str):
+    out = []
+    for line in dump.splitlines():
+        line = line.strip()
+        if line.startswith("group g"):
+            nodes = line.split("nodes=")[1].split()[0]
+            out.append([int(v[1:]) for v in nodes.split(",")])
+    return out
+
+
+class RefRegion:
+    """The reference's native CPU region object (emitCpp20 + host compile)."""
+
+    class Arg(C.Structure):
+        _fields_ = [("kind", C.c_uint32), ("dtype", C.c_uint32), ("rank", C.c_uint32), ("reserved", C.c_uint32),
+                    ("shape", C.POINTER(C.c_uint64)), ("data", C.c_void_p), ("count", C.c_uint64)]
+
+    def __init__(self, path):
+        self.lib = C.CDLL(path)
+        self.fn = self.lib.thiran_ref_entry
+        self.fn.restype = C.c_int
+        self.fn.argtypes = [C.POINTER(self.Arg), C.c_uint64, C.c_void_p, C.c_uint64, C.c_char_p, C.c_uint64]
+
+    def __call__(self, inputs, out_shape, out_dtype):
+        args = (self.Arg * len(inputs))()
+        keep = []
+        for k, a in enumerate(inputs):
+            shape = (C.c_uint64 * a.ndim)(*a.shape)
+            keep.append(shape)
+            args[k] = self.Arg(2, 1 if a.dtype == np.int64 else 2, a.ndim, 0, shape, a.ctypes.data, a.size)
+        out = np.empty(out_shape, dtype=out_dtype)
+        fail = C.create_string_buffer(256)
+        status = self.fn(args, len(inputs), out.ctypes.data, out.size, fail, 256)
+        return status, fail.value.decode(), out
+
+
+F32_CHAIN_4 = """fn f(A:Tensor<f32,1>,B:Tensor<f32,1>) -> Tensor<f32,1> {
+let C=A+B
+let D=C.*B
+let E=D-A
+return E+B
+}"""
+I64_DYN = """fn f(x: Tensor<i64,1>, y: Tensor<i64,1>) -> Tensor<i64,1> {
+let z=x+y
+return z.*y
+}"""
+PICK = "fn pick(x: Tensor<i64,1>, i:i64)->i64{return x[i]}"
+CHAIN = open(os.path.join(ROOT, "oracle", "programs", "f32_chain.th")).read()
+I64_REGION = open(os.path.join(ROOT, "oracle", "programs", "i64_region.th")).read()
+SQUARE_LINEAR = "fn f(x: Tensor<f32,1>) -> Tensor<f32,1> {\nreturn research_square_linear(x)\n}"
+SUMS = """fn rows(A: Tensor<f32,2>) -> Tensor<f32,1> { return sum(A, 1) }
+fn cols(A: Tensor<f32,2>) -> Tensor<f32,1> { return sum(A, 0) }
+fn total(A: Tensor<f32,2>) -> f32 { return sum(sum(A, 1), 0) }
+"""
+MATMUL = "fn mm(A: Tensor<f32,2>, B: Tensor<f32,2>) -> Tensor<f32,2> { return A * B }"
+
+
+def main():
+    if not os.path.exists(DRIVER):
+        sys.exit(f"{DRIVER} missing: run `make -C oracle ref` (needs the reference sources)")
+    fixtures = {}
+    arrays = {}
+
+    # Known-answer vectors of the reference's GPU integration test
+    # (tests/backend/v0/NativeGpuIntegrationTests.cpp:72-112, :139-163, :165-189).
+    a = np.array([1.0, 2.0, 0.0, 3.5, 7.0], np.float32)
+    b = np.array([2.0, 4.0, 3.0, 0.5, 1.0], np.float32)
+    status, value = evaluate(F32_CHAIN_4, "f", [a, b])
+    arrays["kat_f32_a"], arrays["kat_f32_b"], arrays["kat_f32_out"] = a, b, value
+    fixtures["kat_f32_chain"] = {"status": status, "groups_fused": groups_of(plan(F32_CHAIN_4, "f")),
+                                 "groups_unfused": groups_of(plan(F32_CHAIN_4, "f", fusion=False))}
+
+    x = np.full(257, 3, np.int64)
+    status, value = evaluate(I64_DYN, "f", [x, x])
+    arrays["kat_i64_257_out"] = value
+    fixtures["kat_i64_257"] = {"status": status, "groups_fused": groups_of(plan(I64_DYN, "f"))}
+
+    lefts, rights, outs = [], [], []
+    for case in range(100):
+        left = np.array([(case * 37 + e * 19) % 257 - 128 for e in range(17)], np.int64)
+        right = np.array([(case * 29 + e * 31) % 129 - 64 for e in range(17)], np.int64)
+        status, value = evaluate(I64_DYN, "f", [left, right])
+        assert status == "ok"
+        lefts.append(left); rights.append(right); outs.append(value)
+    arrays["kat_i64_diff_left"] = np.stack(lefts)
+    arrays["kat_i64_diff_right"] = np.stack(rights)
+    arrays["kat_i64_diff_out"] = np.stack(outs)
+
+    status, _ = evaluate(I64_DYN, "f", [np.array([2**63 - 1], np.int64), np.array([1], np.int64)])
+    fixtures["kat_i64_overflow"] = {"status": status}
+    for idx in (256, 257, -1):
+        status, value = evaluate(PICK, "pick", [x, np.int64(idx)])
+        fixtures[f"kat_pick_{idx}"] = {"status": status, "value": None if value is None else int(value)}
+
+    xs = np.array([-2.0, -0.5, 0.0, 1.5, 3.0, 7.25, -9.0], np.float32)
+    status, value = evaluate(SQUARE_LINEAR, "f", [xs])
+    arrays["kat_square_linear_in"], arrays["kat_square_linear_out"] = xs, value
+
+    # Benchmark-shaped regions at fixture sizes, through the reference
+    # Evaluator AND its native CPU path (emitCpp20 + host compile).
+    rng = np.random.default_rng(0)
+    chain_x = rng.uniform(-1, 1, 1 << 14).astype(np.float32)
+    status, value = evaluate(CHAIN, "f", [chain_x])
+    arrays["chain_x"], arrays["chain_eval"] = chain_x, value
+    ref = RefRegion(os.path.join(ROOT, "oracle", "_ref", "region_f32_chain.so"))
+    s, _, out = ref([chain_x], chain_x.shape, np.float32)
+    assert s == 0
+    arrays["chain_native_cpu"] = out
+    fixtures["chain"] = {"groups_fused": groups_of(plan(CHAIN, "f"))}
+
+    rng = np.random.default_rng(1)
+    ia = rng.integers(-1000, 1001, (64, 96), dtype=np.int64)
+    ib = rng.integers(-1000, 1001, (64, 96), dtype=np.int64)
+    status, value = evaluate(I64_REGION, "f", [ia, ib])
+    arrays["i64_a"], arrays["i64_b"], arrays["i64_eval"] = ia, ib, value
+    ref = RefRegion(os.path.join(ROOT, "oracle", "_ref", "region_i64_region.so"))
+    s, _, out = ref([ia, ib], ia.shape, np.int64)
+    assert s == 0
+    arrays["i64_native_cpu"] = out
+    big = np.array([[3037000500, 1]], np.int64)
+    s, fail, _ = ref([big, np.zeros_like(big)], big.shape, np.int64)
+    fixtures["i64_region"] = {"groups_fused": groups_of(plan(I64_REGION, "f")),
+                              "groups_unfused": groups_of(plan(I64_REGION, "f", fusion=False)),
+                              "overflow_status": s, "overflow_id": fail}
+
+    # Reductions and matmul (Evaluator only; the reference has no native path).
+    rng = np.random.default_rng(3)
+    m = rng.standard_normal((64, 128)).astype(np.float32)
+    arrays["sum_in"] = m
+    for fn in ("rows", "cols", "total"):
+        status, value = evaluate(SUMS, fn, [m])
+        arrays[f"sum_{fn}"] = np.asarray(value, np.float32)
+    rng = np.random.default_rng(4)
+    ma = rng.standard_normal((16, 32)).astype(np.float32)
+    mb = rng.standard_normal((32, 24)).astype(np.float32)
+    status, value = evaluate(MATMUL, "mm", [ma, mb])
+    arrays["mm_a"], arrays["mm_b"], arrays["mm_out"] = ma, mb, value
+
+    np.savez_compressed(os.path.join(HERE, "reference_outputs.npz"), **arrays)
+    with open(os.path.join(HERE, "reference_fixtures.json"), "w") as f:
+        json.dump(fixtures, f, indent=1, sort_keys=True)
+    print("wrote", len(arrays), "arrays and", len(fixtures), "fixtures")
+
+
+if __name__ == "__main__":
+    main()

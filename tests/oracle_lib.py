@@ -1,0 +1,119 @@
+"""ctypes binding of oracle/liboracle.so — the CPU restatement used as checker."""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+import thiran_b200 as thb
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+_lib = C.CDLL(os.path.join(ROOT, "oracle", "liboracle.so"))
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_lib.orc_region_eval.restype = C.c_int
+_lib.orc_region_eval.argtypes = [C.POINTER(thb.RegionDesc), C.POINTER(thb.AbiArg), C.c_uint64, C.c_void_p, C.c_uint64,
+                                 C.c_char_p, C.c_uint64]
+for name in ("orc_softmax_rows", "orc_max_rows", "orc_sum_rows", "orc_sum_cols"):
+    fn = getattr(_lib, name)
+    fn.restype = None
+    fn.argtypes = [_f32p, _f32p, C.c_uint64, C.c_uint64]
+_lib.orc_sum_all_f64.restype = C.c_double
+_lib.orc_sum_all_f64.argtypes = [_f32p, C.c_uint64]
+_lib.orc_sum_all_sequential_f32.restype = C.c_float
+_lib.orc_sum_all_sequential_f32.argtypes = [_f32p, C.c_uint64]
+for name in ("orc_matmul_f32", "orc_matmul_f64acc"):
+    fn = getattr(_lib, name)
+    fn.restype = None
+    fn.argtypes = [_f32p, _f32p, _f32p, C.c_uint64, C.c_uint64, C.c_uint64]
+_lib.orc_round_bf16.restype = None
+_lib.orc_round_bf16.argtypes = [_f32p, _f32p, C.c_uint64]
+_lib.orc_mlp_step.restype = C.c_double
+_lib.orc_mlp_step.argtypes = [_f32p, _f32p, _f32p, _f32p, C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64, C.c_float,
+                              _f32p, _f32p, _f32p, _f32p]
+
+
+class OracleFailure(RuntimeError):
+    def __init__(self, status, code):
+        super().__init__(code)
+        self.status, self.code = status, code
+
+
+def region_eval(spec: "thb.RegionSpec", inputs, output_shape=None):
+    """Evaluates a region on the CPU restatement; raises OracleFailure."""
+    args, keep = thb._host_args(inputs)
+    shape = spec.infer_output_shape(inputs) if output_shape is None else list(output_shape)
+    out = np.empty(shape, dtype=thb._NP[spec.output_dtype])
+    fail = C.create_string_buffer(256)
+    status = _lib.orc_region_eval(C.byref(spec.desc), args, len(inputs), out.ctypes.data if out.size else None,
+                                  out.size, fail, 256)
+    if status:
+        raise OracleFailure(status, fail.value.decode())
+    return out if shape else out.reshape(()).item()
+
+
+def softmax_rows(x):
+    y = np.empty_like(x)
+    _lib.orc_softmax_rows(x, y, x.shape[0], x.shape[1])
+    return y
+
+
+def max_rows(x):
+    y = np.empty(x.shape[0], np.float32)
+    _lib.orc_max_rows(x, y, x.shape[0], x.shape[1])
+    return y
+
+
+def sum_rows(x):
+    y = np.empty(x.shape[0], np.float32)
+    _lib.orc_sum_rows(x, y, x.shape[0], x.shape[1])
+    return y
+
+
+def sum_cols(x):
+    y = np.empty(x.shape[1], np.float32)
+    _lib.orc_sum_cols(x, y, x.shape[0], x.shape[1])
+    return y
+
+
+def sum_all_f64(x):
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    return _lib.orc_sum_all_f64(x, x.size)
+
+
+def sum_all_sequential_f32(x):
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    return _lib.orc_sum_all_sequential_f32(x, x.size)
+
+
+def matmul_f32(a, b):
+    c = np.empty((a.shape[0], b.shape[1]), np.float32)
+    _lib.orc_matmul_f32(np.ascontiguousarray(a), np.ascontiguousarray(b), c, a.shape[0], a.shape[1], b.shape[1])
+    return c
+
+
+def matmul_f64acc(a, b):
+    c = np.empty((a.shape[0], b.shape[1]), np.float32)
+    _lib.orc_matmul_f64acc(np.ascontiguousarray(a), np.ascontiguousarray(b), c, a.shape[0], a.shape[1], b.shape[1])
+    return c
+
+
+def round_bf16(x):
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    _lib.orc_round_bf16(x.reshape(-1), y.reshape(-1), x.size)
+    return y
+
+
+def mlp_step(x, t, w1, w2, lr):
+    """Returns (loss, dW1, dW2, hidden, y); updates w1/w2 in place."""
+    b, i = x.shape
+    h = w1.shape[1]
+    o = w2.shape[1]
+    dw1 = np.empty((i, h), np.float32)
+    dw2 = np.empty((h, o), np.float32)
+    hidden = np.empty((b, h), np.float32)
+    y = np.empty((b, o), np.float32)
+    loss = _lib.orc_mlp_step(x, t, w1, w2, b, i, h, o, lr, dw1, dw2, hidden, y)
+    return loss, dw1, dw2, hidden, y

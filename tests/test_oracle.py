@@ -1,0 +1,146 @@
+"""Pins the CPU oracle against the reference's own outputs (tests/golden/,
+produced by tests/golden/make_golden.py from the reference's Evaluator and
+native CPU path) and the known-answer vectors of the reference's tests."""
+import numpy as np
+import pytest
+
+import thiran_b200 as thb
+from thiran_b200 import regions
+import oracle_lib as orc
+
+
+def test_kat_f32_chain(golden):
+    # tests/backend/v0/NativeGpuIntegrationTests.cpp:72-112
+    out = orc.region_eval(regions.f32_chain4(), [golden["kat_f32_a"], golden["kat_f32_b"]])
+    np.testing.assert_array_equal(out, golden["kat_f32_out"])
+
+
+def test_kat_i64_odd_size(golden):
+    # NativeGpuIntegrationTests.cpp:139-163: n=257, all 3 -> 18
+    x = np.full(257, 3, np.int64)
+    out = orc.region_eval(regions.i64_dynamic(), [x, x])
+    np.testing.assert_array_equal(out, golden["kat_i64_257_out"])
+    assert out[0] == 18 and out[-1] == 18
+
+
+def test_kat_i64_differential(golden):
+    # NativeGpuIntegrationTests.cpp:165-189: 100 generated cases, exact
+    spec = regions.i64_dynamic()
+    for case in range(100):
+        out = orc.region_eval(spec, [golden["kat_i64_diff_left"][case], golden["kat_i64_diff_right"][case]])
+        np.testing.assert_array_equal(out, golden["kat_i64_diff_out"][case])
+
+
+def test_kat_overflow(fixtures):
+    # NativeGpuIntegrationTests.cpp:277-283
+    with pytest.raises(orc.OracleFailure) as err:
+        orc.region_eval(regions.i64_dynamic(), [np.array([2**63 - 1], np.int64), np.array([1], np.int64)])
+    assert err.value.code == fixtures["kat_i64_overflow"]["status"] == "TH-SPEC-I64-OVERFLOW"
+
+
+@pytest.mark.parametrize("index", [256, 257, -1])
+def test_kat_index_bounds(fixtures, index):
+    b = thb.RegionBuilder("pick")
+    x = b.input(thb.I64, [None])
+    i = b.input(thb.I64, [])
+    spec = b.build(b.index(b.alias(x), b.alias(i)))
+    expected = fixtures[f"kat_pick_{index}"]
+    try:
+        value = orc.region_eval(spec, [np.full(257, 3, np.int64), index])
+        assert expected["status"] == "ok" and value == expected["value"]
+    except orc.OracleFailure as err:
+        assert err.code == expected["status"] == "TH-SPEC-BOUNDS"
+
+
+def test_kat_square_linear(golden):
+    # examples/research_extension: x*x + x
+    op = thb.Operation("research_square_linear",
+                       [(thb.SCALAR_INPUT, 0, 0, 0, 0.0), (thb.SCALAR_MULTIPLY, 0, 0, 0, 0.0),
+                        (thb.SCALAR_ADD, 1, 0, 0, 0.0)], root=2)
+    b = thb.RegionBuilder("f")
+    x = b.input(thb.F32, [None])
+    spec = b.build(b.extension(op, b.alias(x)))
+    out = orc.region_eval(spec, [golden["kat_square_linear_in"]])
+    np.testing.assert_array_equal(out, golden["kat_square_linear_out"])
+    np.testing.assert_array_equal(out, np.array([2.0, -0.25, 0.0, 3.75, 12.0, 59.8125, 72.0], np.float32))
+
+
+def test_chain_matches_reference_native_cpu_bitwise(golden):
+    out = orc.region_eval(regions.f32_chain(), [golden["chain_x"]])
+    assert out.view(np.uint32).tolist() == golden["chain_native_cpu"].view(np.uint32).tolist()
+    assert out.view(np.uint32).tolist() == golden["chain_eval"].view(np.uint32).tolist()
+
+
+def test_i64_region_matches_reference_native_cpu(golden, fixtures):
+    out = orc.region_eval(regions.i64_region(), [golden["i64_a"], golden["i64_b"]])
+    np.testing.assert_array_equal(out, golden["i64_native_cpu"])
+    np.testing.assert_array_equal(out, golden["i64_eval"])
+    big = np.array([[3037000500, 1]], np.int64)
+    with pytest.raises(orc.OracleFailure) as err:
+        orc.region_eval(regions.i64_region(), [big, np.zeros_like(big)])
+    assert err.value.code == fixtures["i64_region"]["overflow_id"]
+
+
+def test_sums_against_reference_evaluator(golden):
+    m = golden["sum_in"]
+    # The reference sums sequentially in f32 (Evaluator.cpp:221-226); the
+    # oracle accumulates in f64. They agree to the f32 ordering error.
+    np.testing.assert_allclose(orc.sum_rows(m), golden["sum_rows"], rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(orc.sum_cols(m), golden["sum_cols"], rtol=1e-5, atol=1e-5)
+    total = orc.sum_all_f64(m)
+    assert abs(total - float(golden["sum_total"])) <= 1e-4 * max(1.0, abs(total))
+    # The sequential-f32 restatement reproduces the reference exactly for a
+    # row-major flat sum of one row (same order).
+    row = np.ascontiguousarray(m[0])
+    assert orc.sum_all_sequential_f32(row) == np.float32(golden["sum_rows"][0]) or \
+        abs(orc.sum_all_sequential_f32(row) - golden["sum_rows"][0]) == 0
+
+
+def test_matmul_evaluator_order_bitwise(golden):
+    out = orc.matmul_f32(golden["mm_a"], golden["mm_b"])
+    assert out.view(np.uint32).tolist() == golden["mm_out"].view(np.uint32).tolist()
+
+
+def test_softmax_restatement_against_numpy():
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((33, 257)).astype(np.float32)
+    y = orc.softmax_rows(x)
+    xd = x.astype(np.float64)
+    e = np.exp(xd - xd.max(axis=1, keepdims=True))
+    np.testing.assert_allclose(y, e / e.sum(axis=1, keepdims=True), rtol=1e-6, atol=0)
+
+
+def test_softmax_restatement_against_torch_cpu():
+    # The legacy stack lowers softmax to torch.softmax(x, dim=-1)
+    # (src/region/RegionPythonEmitter.cpp:293-294).
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(8)
+    x = rng.standard_normal((16, 4096)).astype(np.float32)
+    ref = torch.softmax(torch.from_numpy(x), dim=-1).numpy()
+    np.testing.assert_allclose(orc.softmax_rows(x), ref, rtol=1e-5, atol=1e-9)
+
+
+def test_relu_restatement_against_torch_cpu():
+    torch = pytest.importorskip("torch")
+    x = np.array([-2.0, -0.0, 0.0, 1.5, np.inf, -np.inf, np.nan], np.float32)
+    b = thb.RegionBuilder("r")
+    v = b.input(thb.F32, [None])
+    out = orc.region_eval(b.build(b.relu(v)), [x])
+    ref = torch.relu(torch.from_numpy(x)).numpy()
+    np.testing.assert_array_equal(np.isnan(out), np.isnan(ref))
+    np.testing.assert_array_equal(out[~np.isnan(out)], ref[~np.isnan(ref)])
+
+
+def test_bf16_rounding_matches_torch():
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(9)
+    x = (rng.standard_normal(4096) * 10).astype(np.float32)
+    ref = torch.from_numpy(x).to(torch.bfloat16).to(torch.float32).numpy()
+    np.testing.assert_array_equal(orc.round_bf16(x), ref)
+
+
+def test_planted_mistake_is_caught(golden):
+    """A wrong oracle must fail the fixture comparison (harness is not blind)."""
+    out = orc.region_eval(regions.f32_chain(), [golden["chain_x"]])
+    out[123] = np.nextafter(out[123], np.float32(2))
+    assert out.view(np.uint32).tolist() != golden["chain_native_cpu"].view(np.uint32).tolist()

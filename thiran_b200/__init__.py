@@ -1,0 +1,550 @@
+"""Python binding of libthiran_b200.so, the B200-native TensorRegion engine.
+
+Everything here is a thin ctypes layer over the C ABI in include/thiran_b200.h;
+all planning, code generation and execution happens in the native library.
+There is no CPU execution path: if the library is missing, importing the
+binding raises, and without a CUDA device every execution call raises
+GpuError("GPU-DRIVER-NOT-FOUND"), exactly like the reference's
+`--backend gpu` (src/tooling/v0/Cli.cpp:150-156, no fallback).
+
+The region builder mirrors the reference's TensorRegion
+(include/backend/v0/TensorRegion.hpp:14-57): nodes are added in program order,
+each gets a nonzero value id, and the region is compiled with
+PhysicalPlanOptions(enable_reuse, enable_fusion)
+(include/backend/v0/PhysicalPlan.hpp:37-41).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass, field
+from typing import Sequence
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIBRARY_PATH = os.path.join(_HERE, "libthiran_b200.so")
+
+# ---- constants (include/thiran_b200.h) ------------------------------------------------
+STATUS_OK, STATUS_ABI, STATUS_SEMANTIC, STATUS_BACKEND, STATUS_UNKNOWN = 0, 1, 2, 3, 4
+I64, F32, BF16 = 1, 2, 3
+KIND_SCALAR, KIND_TENSOR = 1, 2
+(OP_INPUT, OP_INTEGER, OP_FLOAT, OP_TENSOR_LITERAL, OP_ALIAS, OP_COPY, OP_NEGATE, OP_ADD, OP_SUBTRACT,
+ OP_ELEMENT_MULTIPLY, OP_EXTENSION, OP_INDEX, OP_UNSUPPORTED) = range(13)
+OP_SUM, OP_ROW_MAX, OP_SOFTMAX, OP_RELU = 32, 33, 34, 35
+(SCALAR_INPUT, SCALAR_CONSTANT_F32, SCALAR_ADD, SCALAR_SUBTRACT, SCALAR_MULTIPLY, SCALAR_DIVIDE,
+ SCALAR_NEGATE) = range(1, 8)
+EFFECT_PURE, EFFECT_MAY_TRAP = 0, 1
+BACKEND_REFERENCE, BACKEND_CPU, BACKEND_GPU = 1, 2, 4
+DESCRIBE_PLAN, DESCRIBE_SOURCE, DESCRIBE_CUBIN = 0, 1, 2
+
+_NP = {I64: np.int64, F32: np.float32}
+
+
+class ScalarNode(C.Structure):
+    _fields_ = [("opcode", C.c_uint8), ("left", C.c_uint32), ("right", C.c_uint32), ("input", C.c_uint32),
+                ("constant", C.c_float)]
+
+
+class ScalarRecipe(C.Structure):
+    _fields_ = [("nodes", C.POINTER(ScalarNode)), ("node_count", C.c_size_t), ("root", C.c_uint32),
+                ("input_count", C.c_uint32)]
+
+
+class Derivative(C.Structure):
+    _fields_ = [("differentiable_inputs", C.c_uint64), ("saved_inputs", C.c_uint64), ("saves_output", C.c_uint8),
+                ("gradients", C.POINTER(ScalarRecipe)), ("gradient_count", C.c_size_t)]
+
+
+class OperationDesc(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("semantic_version", C.c_char_p), ("arity", C.c_uint32),
+                ("minimum_rank", C.c_uint32), ("maximum_rank", C.c_uint32), ("result_like_input", C.c_uint32),
+                ("same_shape", C.c_uint8), ("effect", C.c_uint8), ("backends", C.c_uint32), ("fusible", C.c_uint8),
+                ("forward", ScalarRecipe), ("derivative", C.POINTER(Derivative))]
+
+
+class RegionNode(C.Structure):
+    _fields_ = [("id", C.c_uint32), ("op", C.c_uint32), ("dtype", C.c_uint32), ("rank", C.c_uint32),
+                ("extent", C.c_int64 * 2), ("dependencies", C.POINTER(C.c_uint32)), ("dependency_count", C.c_uint32),
+                ("indices", C.POINTER(C.c_uint32)), ("index_count", C.c_uint32), ("integer", C.c_int64),
+                ("floating", C.c_float), ("axis", C.c_int32), ("extension", C.POINTER(OperationDesc))]
+
+
+class RegionDesc(C.Structure):
+    _fields_ = [("function", C.c_uint32), ("name", C.c_char_p), ("nodes", C.POINTER(RegionNode)),
+                ("node_count", C.c_uint32), ("inputs", C.POINTER(C.c_uint32)), ("input_count", C.c_uint32),
+                ("output", C.c_uint32)]
+
+
+class PlanOptions(C.Structure):
+    _fields_ = [("enable_reuse", C.c_uint32), ("enable_fusion", C.c_uint32)]
+
+
+class AbiArg(C.Structure):
+    _fields_ = [("kind", C.c_uint32), ("dtype", C.c_uint32), ("rank", C.c_uint32), ("reserved", C.c_uint32),
+                ("shape", C.POINTER(C.c_uint64)), ("data", C.c_void_p), ("count", C.c_uint64)]
+
+
+EVIDENCE_FIELDS = [
+    "allocation_count", "allocation_bytes_requested", "host_to_device_copies", "host_to_device_bytes",
+    "device_to_host_copies", "device_to_host_bytes", "device_to_device_copies", "device_to_device_bytes",
+    "module_loads", "driver_jit_loads", "input_storage_uploads", "result_downloads", "kernel_launches",
+    "synchronizations", "submitted_operations", "pending_operations", "active_read_reservations",
+    "active_write_reservations", "stream_submissions", "event_records", "observations", "dropped_drains",
+    "released_reservations", "logical_tensor_values", "logical_intermediates", "materialized_intermediates",
+    "physical_slots", "physical_temporary_slots", "reused_slot_assignments", "fusion_groups", "fused_kernel_groups",
+    "planner_owned_allocations", "retained_planner_allocations",
+]
+
+
+class Evidence(C.Structure):
+    _fields_ = [(name, C.c_uint64) for name in EVIDENCE_FIELDS]
+
+    def as_dict(self) -> dict:
+        return {name: int(getattr(self, name)) for name in EVIDENCE_FIELDS}
+
+
+class DeviceInfo(C.Structure):
+    _fields_ = [("backend_built", C.c_int32), ("driver_loaded", C.c_int32), ("device_available", C.c_int32),
+                ("device_count", C.c_int32), ("selected_device", C.c_int32), ("driver_version", C.c_int32),
+                ("compute_major", C.c_int32), ("compute_minor", C.c_int32), ("sm_count", C.c_int32),
+                ("reserved", C.c_int32), ("name", C.c_char * 256), ("error_code", C.c_char * 64)]
+
+
+# ---- library --------------------------------------------------------------------------
+
+_lib = None
+
+# Every symbol include/thiran_b200.h declares, with its ctypes signature.
+SIGNATURES = {
+    "thb_backend_built": (C.c_int, []),
+    "thb_abi_version": (C.c_uint32, []),
+    "thb_probe": (C.c_int, [C.c_int, C.POINTER(DeviceInfo)]),
+    "thb_region_compile": (C.c_int, [C.POINTER(RegionDesc), PlanOptions, C.c_int, C.POINTER(C.c_void_p),
+                                     C.c_char_p, C.c_uint64]),
+    "thb_region_release": (None, [C.c_void_p]),
+    "thb_region_execute": (C.c_int, [C.c_void_p, C.POINTER(AbiArg), C.c_uint64, C.c_void_p, C.c_uint64,
+                                     C.POINTER(Evidence), C.c_char_p, C.c_uint64]),
+    "thb_region_submit": (C.c_int, [C.c_void_p, C.POINTER(AbiArg), C.c_uint64, C.POINTER(C.c_void_p),
+                                    C.POINTER(Evidence), C.c_char_p, C.c_uint64]),
+    "thb_pending_state": (C.c_int, [C.c_void_p]),
+    "thb_pending_observe": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_uint64, C.POINTER(Evidence),
+                                      C.c_char_p, C.c_uint64]),
+    "thb_pending_release": (None, [C.c_void_p]),
+    "thb_take_unobserved_errors": (C.c_uint64, [C.c_char_p, C.c_uint64]),
+    "thb_region_launch": (C.c_int, [C.c_void_p, C.POINTER(AbiArg), C.c_uint64, C.c_void_p, C.c_uint64,
+                                    C.c_void_p, C.c_char_p, C.c_uint64]),
+    "thb_region_check_errors": (C.c_int, [C.c_void_p, C.c_void_p, C.c_char_p, C.c_uint64]),
+    "thb_region_emit_source": (C.c_int, [C.c_void_p, C.c_char_p, C.c_uint64, C.POINTER(C.c_uint64)]),
+    "thb_region_dump_plan": (C.c_int, [C.c_void_p, C.c_char_p, C.c_uint64, C.POINTER(C.c_uint64)]),
+    "thb_region_plan_counts": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64),
+                                         C.POINTER(C.c_uint64)]),
+    "thb_region_describe": (C.c_int, [C.POINTER(RegionDesc), PlanOptions, C.c_uint32, C.c_char_p, C.c_uint64,
+                                      C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.c_char_p, C.c_uint64]),
+}
+
+
+def lib() -> C.CDLL:
+    """Loads libthiran_b200.so from this package directory (raises if absent)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIBRARY_PATH):
+            raise ImportError(f"{LIBRARY_PATH} is missing: build it with `make -C thiran_b200` "
+                              "(there is no fallback implementation)")
+        handle = C.CDLL(LIBRARY_PATH)
+        for name, (restype, argtypes) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        _lib = handle
+    return _lib
+
+
+class GpuError(RuntimeError):
+    """A failed engine call: `status` is the C-ABI status, `code` the failure id."""
+
+    def __init__(self, status: int, text: str):
+        code, _, message = text.partition(": ")
+        super().__init__(text)
+        self.status = status
+        self.code = code
+        self.message = message or code
+
+
+def _failure():
+    return C.create_string_buffer(1024)
+
+
+def _raise(status: int, buf) -> None:
+    if status != STATUS_OK:
+        raise GpuError(status, buf.value.decode(errors="replace"))
+
+
+def probe(device: int = 0) -> DeviceInfo:
+    info = DeviceInfo()
+    lib().thb_probe(device, C.byref(info))
+    return info
+
+
+def take_unobserved_errors() -> list[str]:
+    buf = C.create_string_buffer(65536)
+    count = lib().thb_take_unobserved_errors(buf, len(buf))
+    text = buf.value.decode()
+    return text.split("\n") if count else []
+
+
+# ---- operations and regions ----------------------------------------------------------
+
+@dataclass
+class Operation:
+    """An extension operation descriptor (OperationDescriptorV0,
+    include/extension/v0/Extension.hpp:40-53) with its scalar forward recipe:
+    a list of (opcode, left, right, input, constant) tuples."""
+    name: str
+    recipe: Sequence[tuple]
+    root: int
+    arity: int = 1
+    semantic_version: str = "1.0.0"
+    effect: int = EFFECT_PURE
+    fusible: bool = True
+    backends: int = BACKEND_REFERENCE | BACKEND_CPU | BACKEND_GPU
+    minimum_rank: int = 1
+    maximum_rank: int = 2
+    _keep: list = field(default_factory=list, repr=False)
+
+    def descriptor(self) -> OperationDesc:
+        nodes = (ScalarNode * len(self.recipe))(*[ScalarNode(*t) for t in self.recipe])
+        name = self.name.encode()
+        version = self.semantic_version.encode()
+        self._keep[:] = [nodes, name, version]
+        return OperationDesc(name, version, self.arity, self.minimum_rank, self.maximum_rank, 0, 1, self.effect,
+                             self.backends, 1 if self.fusible else 0,
+                             ScalarRecipe(nodes, len(self.recipe), self.root, self.arity), None)
+
+
+def recipe_from_expression(ops: Sequence[tuple]) -> list[tuple]:
+    """Builds a recipe from (opcode, a, b) / ('c', value) / ('x', input) steps."""
+    out = []
+    for step in ops:
+        kind = step[0]
+        if kind == "x":
+            out.append((SCALAR_INPUT, 0, 0, step[1], 0.0))
+        elif kind == "c":
+            out.append((SCALAR_CONSTANT_F32, 0, 0, 0, float(step[1])))
+        elif kind == SCALAR_NEGATE:
+            out.append((SCALAR_NEGATE, step[1], 0, 0, 0.0))
+        else:
+            out.append((kind, step[1], step[2], 0, 0.0))
+    return out
+
+
+class RegionBuilder:
+    """Builds a TensorRegion description node by node (ids start at 1)."""
+
+    def __init__(self, name: str = "main", function: int = 1):
+        self.name = name
+        self.function = function
+        self.nodes: list[dict] = []
+        self.inputs: list[int] = []
+        self.output = 0
+
+    def _add(self, op, dtype, shape=(), deps=(), indices=(), integer=0, floating=0.0, axis=0, extension=None):
+        node_id = len(self.nodes) + 1
+        self.nodes.append(dict(id=node_id, op=op, dtype=dtype, shape=list(shape), deps=list(deps),
+                               indices=list(indices), integer=integer, floating=floating, axis=axis,
+                               extension=extension))
+        return node_id
+
+    def _like(self, v):
+        n = self.nodes[v - 1]
+        return n["dtype"], n["shape"]
+
+    # reference RegionOps
+    def input(self, dtype, shape=()):
+        v = self._add(OP_INPUT, dtype, shape)
+        self.inputs.append(v)
+        return v
+
+    def integer(self, value):
+        return self._add(OP_INTEGER, I64, integer=int(value))
+
+    def float(self, value):
+        return self._add(OP_FLOAT, F32, floating=float(value))
+
+    def literal(self, dtype, shape, elements):
+        return self._add(OP_TENSOR_LITERAL, dtype, shape, deps=elements)
+
+    def alias(self, a):
+        return self._add(OP_ALIAS, *self._like(a), deps=[a])
+
+    def copy(self, a):
+        return self._add(OP_COPY, *self._like(a), deps=[a])
+
+    def neg(self, a):
+        return self._add(OP_NEGATE, *self._like(a), deps=[a])
+
+    def add(self, a, b):
+        return self._add(OP_ADD, *self._like(a), deps=[a, b])
+
+    def sub(self, a, b):
+        return self._add(OP_SUBTRACT, *self._like(a), deps=[a, b])
+
+    def mul(self, a, b):
+        return self._add(OP_ELEMENT_MULTIPLY, *self._like(a), deps=[a, b])
+
+    def extension(self, operation: Operation, *args):
+        return self._add(OP_EXTENSION, *self._like(args[0]), deps=list(args), extension=operation)
+
+    def index(self, a, *coords):
+        return self._add(OP_INDEX, self._like(a)[0], (), deps=[a], indices=list(coords))
+
+    # engine additions
+    def relu(self, a):
+        return self._add(OP_RELU, *self._like(a), deps=[a])
+
+    def softmax(self, a):
+        dtype, shape = self._like(a)
+        return self._add(OP_SOFTMAX, dtype, shape, deps=[a], axis=len(shape) - 1)
+
+    def row_max(self, a):
+        dtype, shape = self._like(a)
+        return self._add(OP_ROW_MAX, dtype, [shape[0]], deps=[a], axis=1)
+
+    def sum(self, a, axis):
+        dtype, shape = self._like(a)
+        kept = [e for i, e in enumerate(shape) if i != axis]
+        return self._add(OP_SUM, dtype, kept, deps=[a], axis=axis)
+
+    def build(self, output: int) -> "RegionSpec":
+        self.output = output
+        return RegionSpec(self)
+
+
+class RegionSpec:
+    """A region description laid out in C structs (kept alive by this object)."""
+
+    def __init__(self, builder: RegionBuilder):
+        self._keep = []
+        nodes = (RegionNode * len(builder.nodes))()
+        for i, n in enumerate(builder.nodes):
+            deps = (C.c_uint32 * max(1, len(n["deps"])))(*n["deps"])
+            idx = (C.c_uint32 * max(1, len(n["indices"])))(*n["indices"])
+            self._keep += [deps, idx]
+            node = nodes[i]
+            node.id, node.op, node.dtype, node.rank = n["id"], n["op"], n["dtype"], len(n["shape"])
+            for a, e in enumerate(n["shape"]):
+                node.extent[a] = -1 if e is None else int(e)
+            for a in range(len(n["shape"]), 2):
+                node.extent[a] = -1
+            node.dependencies, node.dependency_count = deps, len(n["deps"])
+            node.indices, node.index_count = idx, len(n["indices"])
+            node.integer, node.floating, node.axis = n["integer"], n["floating"], n["axis"]
+            if n["extension"] is not None:
+                d = n["extension"].descriptor()
+                self._keep += [d, n["extension"]]
+                node.extension = C.pointer(d)
+        inputs = (C.c_uint32 * max(1, len(builder.inputs)))(*builder.inputs)
+        name = builder.name.encode()
+        self._keep += [nodes, inputs, name]
+        self.desc = RegionDesc(builder.function, name, nodes, len(builder.nodes), inputs, len(builder.inputs),
+                               builder.output)
+        self.input_types = [(builder.nodes[v - 1]["dtype"], builder.nodes[v - 1]["shape"]) for v in builder.inputs]
+        out = builder.nodes[builder.output - 1] if 0 < builder.output <= len(builder.nodes) else None
+        self.output_dtype = out["dtype"] if out else F32
+        self.output_shape = out["shape"] if out else []
+        self._nodes = builder.nodes
+        self._inputs = builder.inputs
+        self._output = builder.output
+
+    def infer_output_shape(self, inputs) -> list:
+        """Runtime output shape from the input shapes (for regions whose
+        extents are unknown until execution)."""
+        shapes = {}
+        for v, value in zip(self._inputs, inputs):
+            shapes[v] = list(np.shape(value)) if hasattr(value, "shape") else []
+        for n in self._nodes:
+            if n["id"] in shapes:
+                continue
+            deps = [shapes.get(d, []) for d in n["deps"]]
+            op = n["op"]
+            if op in (OP_INTEGER, OP_FLOAT, OP_INDEX):
+                s = []
+            elif op == OP_TENSOR_LITERAL:
+                s = list(n["shape"])
+            elif op == OP_SUM:
+                s = [e for i, e in enumerate(deps[0]) if i != n["axis"]]
+            elif op == OP_ROW_MAX:
+                s = [deps[0][0]]
+            else:
+                s = list(deps[0]) if deps else list(n["shape"])
+            shapes[n["id"]] = s
+        return [int(e) for e in shapes[self._output]]
+
+    def describe(self, what: int = DESCRIBE_PLAN, reuse=True, fusion=True) -> tuple[str, list[int]]:
+        counts = (C.c_uint64 * 3)()
+        needed = C.c_uint64(0)
+        fail = _failure()
+        status = lib().thb_region_describe(C.byref(self.desc), PlanOptions(int(reuse), int(fusion)), what, None, 0,
+                                           C.byref(needed), counts, fail, len(fail))
+        _raise(status, fail)
+        buf = C.create_string_buffer(int(needed.value))
+        status = lib().thb_region_describe(C.byref(self.desc), PlanOptions(int(reuse), int(fusion)), what, buf,
+                                           len(buf), C.byref(needed), counts, fail, len(fail))
+        _raise(status, fail)
+        return buf.value.decode(), list(counts)
+
+    def compile(self, device: int = 0, reuse=True, fusion=True) -> "CompiledRegion":
+        handle = C.c_void_p()
+        fail = _failure()
+        status = lib().thb_region_compile(C.byref(self.desc), PlanOptions(int(reuse), int(fusion)), device,
+                                          C.byref(handle), fail, len(fail))
+        _raise(status, fail)
+        return CompiledRegion(self, handle)
+
+
+def _host_args(values) -> tuple:
+    """Lays out host values (numpy arrays, python ints/floats) as AbiArg records."""
+    keep = []
+    args = (AbiArg * max(1, len(values)))()
+    for i, v in enumerate(values):
+        a = args[i]
+        if isinstance(v, np.ndarray):
+            dtype = I64 if v.dtype == np.int64 else F32 if v.dtype == np.float32 else 0
+            shape = (C.c_uint64 * max(1, v.ndim))(*v.shape)
+            keep.append(shape)
+            a.kind, a.dtype, a.rank = KIND_TENSOR, dtype, v.ndim
+            a.reserved = 0 if v.flags["C_CONTIGUOUS"] else 1
+            a.shape, a.data, a.count = shape, v.ctypes.data if v.size else None, v.size
+        else:
+            is_int = isinstance(v, (int, np.integer)) and not isinstance(v, bool)
+            scalar = C.c_int64(int(v)) if is_int else C.c_float(float(v))
+            keep.append(scalar)
+            a.kind, a.dtype, a.rank = KIND_SCALAR, I64 if is_int else F32, 0
+            a.shape, a.data, a.count = None, C.cast(C.byref(scalar), C.c_void_p), 1
+    return args, keep
+
+
+def _device_args(tensors) -> tuple:
+    """AbiArg records for device tensors (torch CUDA tensors) or host scalars."""
+    keep = []
+    args = (AbiArg * max(1, len(tensors)))()
+    for i, t in enumerate(tensors):
+        a = args[i]
+        if hasattr(t, "data_ptr"):
+            dtype = {"torch.int64": I64, "torch.float32": F32}.get(str(t.dtype), 0)
+            shape = (C.c_uint64 * max(1, t.dim()))(*t.shape)
+            keep.append(shape)
+            a.kind, a.dtype, a.rank = KIND_TENSOR, dtype, t.dim()
+            a.reserved = 0 if t.is_contiguous() else 1
+            a.shape, a.data, a.count = shape, t.data_ptr() or None, t.numel()
+        else:
+            is_int = isinstance(t, (int, np.integer))
+            scalar = C.c_int64(int(t)) if is_int else C.c_float(float(t))
+            keep.append(scalar)
+            a.kind, a.dtype, a.rank = KIND_SCALAR, I64 if is_int else F32, 0
+            a.shape, a.data, a.count = None, C.cast(C.byref(scalar), C.c_void_p), 1
+    return args, keep
+
+
+class Pending:
+    """A submitted execution (PendingGpuExecution)."""
+
+    def __init__(self, region: "CompiledRegion", handle: C.c_void_p, shape, dtype, evidence: dict):
+        self.region, self.handle, self.shape, self.dtype = region, handle, shape, dtype
+        self.submit_evidence = evidence
+        self._value = None
+
+    def state(self) -> int:
+        return lib().thb_pending_state(self.handle)
+
+    def observe(self, timeout_ms: int = 60000):
+        out = np.empty(self.shape, dtype=_NP[self.dtype])
+        ev = Evidence()
+        fail = _failure()
+        status = lib().thb_pending_observe(self.handle, out.ctypes.data if out.size else None, out.size,
+                                           timeout_ms, C.byref(ev), fail, len(fail))
+        self.evidence = ev.as_dict()
+        _raise(status, fail)
+        return out if self.shape != [] else out.reshape(()).item()
+
+    def release(self):
+        if self.handle:
+            lib().thb_pending_release(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
+
+
+class CompiledRegion:
+    """A planned, code-generated, device-resident region (thb_region)."""
+
+    def __init__(self, spec: RegionSpec, handle: C.c_void_p):
+        self.spec, self.handle = spec, handle
+
+    def execute(self, inputs, output_shape=None, out=None):
+        """executeNativeGpu: host values in, host value out (numpy / scalar).
+        `out` may supply a preallocated (for example pinned) host array."""
+        args, keep = _host_args(inputs)
+        shape = self.spec.infer_output_shape(inputs) if output_shape is None else list(output_shape)
+        if out is None:
+            out = np.empty([int(e) for e in shape], dtype=_NP[self.spec.output_dtype])
+        ev = Evidence()
+        fail = _failure()
+        status = lib().thb_region_execute(self.handle, args, len(inputs), out.ctypes.data if out.size else None,
+                                          out.size, C.byref(ev), fail, len(fail))
+        self.evidence = ev.as_dict()
+        _raise(status, fail)
+        return out if len(shape) else out.reshape(()).item()
+
+    def submit(self, inputs, output_shape=None) -> Pending:
+        args, keep = _host_args(inputs)
+        handle = C.c_void_p()
+        ev = Evidence()
+        fail = _failure()
+        status = lib().thb_region_submit(self.handle, args, len(inputs), C.byref(handle), C.byref(ev), fail, len(fail))
+        _raise(status, fail)
+        shape = self.spec.infer_output_shape(inputs) if output_shape is None else list(output_shape)
+        p = Pending(self, handle, [int(e) for e in shape], self.spec.output_dtype, ev.as_dict())
+        p._inputs = inputs  # host buffers must outlive the submission
+        return p
+
+    def launch(self, tensors, output, stream=0) -> None:
+        """Device-resident, stream-ordered launch (torch CUDA tensors)."""
+        args, keep = _device_args(tensors)
+        fail = _failure()
+        status = lib().thb_region_launch(self.handle, args, len(tensors), output.data_ptr(), output.numel(),
+                                         C.c_void_p(stream), fail, len(fail))
+        _raise(status, fail)
+
+    def check_errors(self, stream=0) -> None:
+        fail = _failure()
+        _raise(lib().thb_region_check_errors(self.handle, C.c_void_p(stream), fail, len(fail)), fail)
+
+    def source(self) -> str:
+        needed = C.c_uint64(0)
+        lib().thb_region_emit_source(self.handle, None, 0, C.byref(needed))
+        buf = C.create_string_buffer(int(needed.value))
+        lib().thb_region_emit_source(self.handle, buf, len(buf), C.byref(needed))
+        return buf.value.decode()
+
+    def plan(self) -> str:
+        needed = C.c_uint64(0)
+        lib().thb_region_dump_plan(self.handle, None, 0, C.byref(needed))
+        buf = C.create_string_buffer(int(needed.value))
+        lib().thb_region_dump_plan(self.handle, buf, len(buf), C.byref(needed))
+        return buf.value.decode()
+
+    def release(self):
+        if self.handle:
+            lib().thb_region_release(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass

@@ -1,0 +1,460 @@
+// extern "C" surface of libthiran_b200.so (declared in include/thiran_b200.h).
+#include <chrono>
+#include <cstring>
+#include <memory>
+#include <thread>
+
+#include "runtime.hpp"
+
+struct thb_region {
+    std::shared_ptr<thb::CompiledRegion> impl;
+};
+
+struct thb_pending {
+    std::unique_ptr<thb::Pending> impl;
+};
+
+namespace {
+
+using namespace thb;
+
+template <class F>
+int guarded(char* failure, std::uint64_t cap, F&& body) noexcept {
+    try {
+        return body();
+    } catch (const Failure& f) {
+        writeText(failure, cap, f.text());
+        return f.status();
+    } catch (const std::exception& e) {
+        writeText(failure, cap, std::string("GPU-INTERNAL: ") + e.what());
+        return THB_STATUS_UNKNOWN;
+    } catch (...) {
+        writeText(failure, cap, "GPU-INTERNAL: unknown native failure");
+        return THB_STATUS_UNKNOWN;
+    }
+}
+
+void cudaCheck(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) fail(Category::Runtime, "GPU-RUNTIME", std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// Validates the argument records against the region's Input nodes (the
+// preflight of src/backend/v0/NativeGpu.cpp:73-106) and binds them. In host
+// mode tensors are uploaded into the region's input buffers; identical host
+// storages are uploaded once (NativeGpu.cpp:961-971).
+std::vector<Value> bind(CompiledRegion& region, const thb_abi_arg* args, std::uint64_t argc, bool hostMode,
+                        cudaStream_t stream, thb_evidence& ev, std::uint64_t* distinctReads) {
+    const Region& r = region.region();
+    if (argc != r.inputs.size()) fail(Category::Unsupported, "GPU-INPUT-ARITY", "GPU input arity mismatch");
+    if (argc && !args) fail(Category::Validation, "GPU-INPUT-ARITY", "argument array is null");
+    std::vector<Value> values(argc);
+    for (std::uint64_t i = 0; i < argc; ++i) {
+        const Node& node = r.at(r.inputs[i]);
+        const thb_abi_arg& a = args[i];
+        Value& v = values[i];
+        if (a.kind == THB_KIND_TENSOR) {
+            if (!node.tensor()) fail(Category::Unsupported, "GPU-INPUT-TYPE", "tensor supplied for scalar GPU input");
+            if (a.dtype != static_cast<std::uint32_t>(node.dtype))
+                fail(Category::Unsupported, "GPU-INPUT-TYPE", "tensor dtype disagrees with the region input");
+            if (a.rank != node.rank || !a.shape)
+                fail(Category::Unsupported, "GPU-INPUT-SHAPE", "tensor rank disagrees with the region input");
+            std::uint64_t count = 1;
+            for (std::uint32_t d = 0; d < a.rank; ++d) {
+                if (node.extent[d] >= 0 && a.shape[d] != static_cast<std::uint64_t>(node.extent[d]))
+                    fail(Category::Unsupported, "GPU-INPUT-SHAPE", "tensor extent disagrees with the region input");
+                count = checkedMul(count, a.shape[d]);
+                v.shape[d] = a.shape[d];
+            }
+            if (count != a.count) fail(Category::Unsupported, "GPU-INPUT-SHAPE", "element count disagrees with shape");
+            if (a.reserved & 1u)
+                fail(Category::Unsupported, "GPU-UNSUPPORTED-LAYOUT",
+                     "native GPU requires materialized offset-zero contiguous row-major tensors");
+            if (count && !a.data) fail(Category::Unsupported, "GPU-INPUT-SHAPE", "tensor data pointer is null");
+            v.tensor = true;
+            v.onDevice = true;
+            v.dtype = node.dtype;
+            v.rank = a.rank;
+            v.data = const_cast<void*>(a.data);
+        } else if (a.kind == THB_KIND_SCALAR) {
+            if (node.tensor()) fail(Category::Unsupported, "GPU-INPUT-TYPE", "scalar supplied for tensor GPU input");
+            if (a.dtype != static_cast<std::uint32_t>(node.dtype) || a.count != 1 || !a.data)
+                fail(Category::Unsupported, "GPU-INPUT-TYPE", "scalar dtype disagrees with the region input");
+            v.dtype = node.dtype;
+            if (node.dtype == DType::I64) std::memcpy(&v.i64, a.data, 8);
+            else std::memcpy(&v.f32, a.data, 4);
+        } else {
+            fail(Category::Unsupported, "GPU-INPUT-TYPE", "argument kind is neither scalar nor tensor");
+        }
+    }
+    std::uint64_t reads = 0;
+    if (hostMode) {
+        std::map<const void*, void*> uploaded;
+        for (std::uint64_t i = 0; i < argc; ++i) {
+            Value& v = values[i];
+            if (!v.tensor) continue;
+            const void* host = v.data;
+            auto found = uploaded.find(host);
+            if (found != uploaded.end() && v.bytes()) {
+                v.data = found->second;
+                continue;
+            }
+            ++reads;
+            DeviceBuffer& buffer = region.inputBuffer(i);
+            if (buffer.reserve(v.bytes(), region.device())) {
+                ++ev.allocation_count;
+                ev.allocation_bytes_requested += v.bytes();
+            }
+            if (v.bytes()) {
+                cudaCheck(cudaMemcpyAsync(buffer.ptr, host, v.bytes(), cudaMemcpyHostToDevice, stream),
+                          "cudaMemcpyAsync(upload)");
+                ++ev.host_to_device_copies;
+                ev.host_to_device_bytes += v.bytes();
+                ++ev.input_storage_uploads;
+            }
+            uploaded[host] = buffer.ptr;
+            v.data = buffer.ptr;
+        }
+    }
+    if (distinctReads) *distinctReads = reads;
+    return values;
+}
+
+void checkOutputCount(const Value& out, std::uint64_t outputCount, bool needBuffer, const void* output) {
+    const std::uint64_t want = out.count();
+    if (outputCount != want)
+        fail(Category::Unsupported, "GPU-OUTPUT-SHAPE",
+             "output buffer holds " + std::to_string(outputCount) + " elements, region output has " + std::to_string(want));
+    if (needBuffer && want && !output) fail(Category::Unsupported, "GPU-OUTPUT-SHAPE", "output pointer is null");
+}
+
+// Copies a completed output into host memory (host scalars directly,
+// device values through `stream`).
+void downloadOutput(const Value& out, void* host, cudaStream_t stream, thb_evidence& ev) {
+    if (out.tensor || out.onDevice) {
+        if (out.bytes() && host) {
+            cudaCheck(cudaMemcpyAsync(host, out.data, out.bytes(), cudaMemcpyDeviceToHost, stream), "cudaMemcpyAsync(result)");
+            ++ev.device_to_host_copies;
+            ev.device_to_host_bytes += out.bytes();
+            ++ev.result_downloads;
+        }
+    } else if (host) {
+        if (out.dtype == DType::I64) std::memcpy(host, &out.i64, 8);
+        else std::memcpy(host, &out.f32, 4);
+    }
+}
+
+void waitEvent(cudaEvent_t event, std::uint64_t timeoutMs) {
+    const auto start = std::chrono::steady_clock::now();
+    unsigned sleepUs = 20;
+    for (;;) {
+        const cudaError_t e = cudaEventQuery(event);
+        if (e == cudaSuccess) return;
+        if (e != cudaErrorNotReady) cudaCheck(e, "cudaEventQuery");
+        if (timeoutMs && std::chrono::steady_clock::now() - start > std::chrono::milliseconds(timeoutMs))
+            fail(Category::Runtime, "GPU-TIMEOUT", "pending GPU execution did not complete in time");
+        std::this_thread::sleep_for(std::chrono::microseconds(sleepUs));
+        sleepUs = std::min(sleepUs * 2, 1000u);
+    }
+}
+
+} // namespace
+
+extern "C" {
+
+int thb_backend_built(void) { return 1; }
+
+uint32_t thb_abi_version(void) { return THB_ABI_VERSION; }
+
+int thb_probe(int device, thb_device_info* out) {
+    if (!out) return THB_STATUS_ABI;
+    std::memset(out, 0, sizeof *out);
+    out->backend_built = 1;
+    out->selected_device = -1;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        writeText(out->error_code, sizeof out->error_code, "GPU-DRIVER-NOT-FOUND");
+        writeText(out->name, sizeof out->name, cudaGetErrorString(e));
+        return THB_STATUS_BACKEND;
+    }
+    out->driver_loaded = 1;
+    int version = 0;
+    cudaDriverGetVersion(&version);
+    out->driver_version = version;
+    out->device_count = count;
+    if (device < 0 || device >= count) {
+        writeText(out->error_code, sizeof out->error_code, "GPU-INVALID-DEVICE");
+        return THB_STATUS_BACKEND;
+    }
+    cudaDeviceProp prop{};
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) {
+        cudaGetLastError();
+        writeText(out->error_code, sizeof out->error_code, "GPU-INVALID-DEVICE");
+        return THB_STATUS_BACKEND;
+    }
+    out->device_available = 1;
+    out->selected_device = device;
+    out->compute_major = prop.major;
+    out->compute_minor = prop.minor;
+    out->sm_count = prop.multiProcessorCount;
+    writeText(out->name, sizeof out->name, prop.name);
+    return THB_STATUS_OK;
+}
+
+int thb_region_compile(const thb_region_desc* desc, thb_plan_options options, int device, thb_region** out,
+                       char* failure, uint64_t cap) {
+    return guarded(failure, cap, [&] {
+        if (!desc || !out) fail(Category::Validation, "GPU-INVALID-REGION", "region descriptor or result is null");
+        *out = nullptr;
+        PlanOptions opts;
+        opts.enableReuse = options.enable_reuse != 0;
+        opts.enableFusion = options.enable_fusion != 0;
+        auto impl = std::make_shared<CompiledRegion>(*desc, opts, device);
+        *out = new thb_region{std::move(impl)};
+        return THB_STATUS_OK;
+    });
+}
+
+void thb_region_release(thb_region* region) { delete region; }
+
+int thb_region_execute(thb_region* region, const thb_abi_arg* args, uint64_t argc, void* output, uint64_t outputCount,
+                       thb_evidence* evidence, char* failure, uint64_t cap) {
+    thb_evidence ev{};
+    const int status = guarded(failure, cap, [&] {
+        if (!region) fail(Category::Validation, "GPU-INVALID-REGION", "region handle is null");
+        CompiledRegion& r = *region->impl;
+        std::lock_guard<std::mutex> lock(r.mutex);
+        r.planEvidence(ev);
+        cudaCheck(cudaSetDevice(r.device()), "cudaSetDevice");
+        cudaStream_t stream = r.stream();
+        std::uint64_t reads = 0;
+        auto inputs = bind(r, args, argc, true, stream, ev, &reads);
+        r.clearErrors(stream);
+        ++ev.submitted_operations;
+        Value out = r.run(inputs, stream, ev, nullptr,
+                          [&](const Value& o) { checkOutputCount(o, outputCount, true, output); });
+        downloadOutput(out, output, stream, ev);
+        std::vector<std::uint32_t> words(std::max<std::size_t>(1, r.errorWordCount()));
+        PinnedBuffer staged;
+        staged.reserve(words.size() * sizeof(std::uint32_t));
+        r.copyErrors(stream, static_cast<std::uint32_t*>(staged.ptr));
+        ++ev.event_records;
+        cudaCheck(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
+        ++ev.synchronizations;
+        ++ev.observations;
+        ev.released_reservations = reads + 1;
+        ev.retained_planner_allocations = 0;
+        std::memcpy(words.data(), staged.ptr, words.size() * sizeof(std::uint32_t));
+        const std::string id = r.firstFailure(words.data());
+        if (!id.empty()) fail(Category::Semantic, id, id);
+        return THB_STATUS_OK;
+    });
+    if (evidence) *evidence = ev;
+    return status;
+}
+
+int thb_region_submit(thb_region* region, const thb_abi_arg* args, uint64_t argc, thb_pending** out,
+                      thb_evidence* evidence, char* failure, uint64_t cap) {
+    thb_evidence ev{};
+    const int status = guarded(failure, cap, [&] {
+        if (!region || !out) fail(Category::Validation, "GPU-INVALID-REGION", "region handle or result is null");
+        *out = nullptr;
+        CompiledRegion& r = *region->impl;
+        std::lock_guard<std::mutex> lock(r.mutex);
+        r.planEvidence(ev);
+        cudaCheck(cudaSetDevice(r.device()), "cudaSetDevice");
+        cudaStream_t stream = r.stream();
+        auto pending = std::make_unique<Pending>();
+        pending->region = region->impl;
+        auto inputs = bind(r, args, argc, true, stream, ev, &pending->reads);
+        r.clearErrors(stream);
+        ++ev.submitted_operations;
+        Value result = r.run(inputs, stream, ev);
+        pending->result = result;
+        if (result.tensor || result.onDevice) {
+            pending->outputBytes = result.bytes();
+            pending->output.reserve(result.bytes());
+            downloadOutput(result, pending->output.ptr, stream, ev);
+        }
+        pending->errors.reserve(std::max<std::size_t>(1, r.errorWordCount()) * sizeof(std::uint32_t));
+        r.copyErrors(stream, static_cast<std::uint32_t*>(pending->errors.ptr));
+        cudaCheck(cudaEventCreateWithFlags(&pending->done, cudaEventDisableTiming), "cudaEventCreate");
+        cudaCheck(cudaEventRecord(pending->done, stream), "cudaEventRecord");
+        ++ev.event_records;
+        ++ev.stream_submissions;
+        ev.pending_operations = 1;
+        ev.active_read_reservations = pending->reads;
+        ev.active_write_reservations = 1;
+        pending->evidence = ev;
+        *out = new thb_pending{std::move(pending)};
+        return THB_STATUS_OK;
+    });
+    if (evidence) *evidence = ev;
+    return status;
+}
+
+int thb_pending_state(const thb_pending* pending) {
+    if (!pending || !pending->impl) return -1;
+    if (pending->impl->observed) return 1;
+    return cudaEventQuery(pending->impl->done) == cudaSuccess ? 1 : 0;
+}
+
+int thb_pending_observe(thb_pending* handle, void* output, uint64_t outputCount, uint64_t timeoutMs,
+                        thb_evidence* evidence, char* failure, uint64_t cap) {
+    if (!handle || !handle->impl) {
+        writeText(failure, cap, "GPU-INVALID-PENDING: pending handle is null");
+        return THB_STATUS_ABI;
+    }
+    Pending& p = *handle->impl;
+    const int status = guarded(failure, cap, [&] {
+        if (!p.observed) {
+            cudaCheck(cudaSetDevice(p.region->device()), "cudaSetDevice");
+            waitEvent(p.done, timeoutMs);
+            p.observed = true;
+            ++p.evidence.synchronizations;
+            ++p.evidence.observations;
+            p.evidence.pending_operations = 0;
+            p.evidence.active_read_reservations = 0;
+            p.evidence.active_write_reservations = 0;
+            p.evidence.released_reservations = p.reads + 1;
+            p.evidence.retained_planner_allocations = 0;
+            const std::string id = p.region->firstFailure(static_cast<const std::uint32_t*>(p.errors.ptr));
+            if (!id.empty()) {
+                p.status = THB_STATUS_SEMANTIC;
+                p.failureText = id;
+            }
+        }
+        if (p.status != THB_STATUS_OK) fail(Category::Semantic, p.failureText, p.failureText);
+        checkOutputCount(p.result, outputCount, true, output);
+        if (p.result.tensor || p.result.onDevice) {
+            if (p.outputBytes) std::memcpy(output, p.output.ptr, p.outputBytes);
+        } else if (output) {
+            if (p.result.dtype == DType::I64) std::memcpy(output, &p.result.i64, 8);
+            else std::memcpy(output, &p.result.f32, 4);
+        }
+        return THB_STATUS_OK;
+    });
+    if (evidence) *evidence = p.evidence;
+    return status;
+}
+
+void thb_pending_release(thb_pending* handle) {
+    if (!handle) return;
+    if (handle->impl && !handle->impl->observed) {
+        Pending& p = *handle->impl;
+        try {
+            cudaSetDevice(p.region->device());
+            cudaEventSynchronize(p.done);
+            const std::string id = p.region->firstFailure(static_cast<const std::uint32_t*>(p.errors.ptr));
+            if (!id.empty()) recordUnobserved(id);
+        } catch (...) {
+            recordUnobserved("GPU-DRAIN-FAILURE");
+        }
+    }
+    delete handle;
+}
+
+uint64_t thb_take_unobserved_errors(char* buffer, uint64_t capacity) {
+    const auto ids = takeUnobserved();
+    std::string text;
+    for (std::size_t i = 0; i < ids.size(); ++i) text += (i ? "\n" : "") + ids[i];
+    writeText(buffer, capacity, text);
+    return ids.size();
+}
+
+int thb_region_launch(thb_region* region, const thb_abi_arg* args, uint64_t argc, void* output, uint64_t outputCount,
+                      void* stream, char* failure, uint64_t cap) {
+    return guarded(failure, cap, [&] {
+        if (!region) fail(Category::Validation, "GPU-INVALID-REGION", "region handle is null");
+        CompiledRegion& r = *region->impl;
+        std::lock_guard<std::mutex> lock(r.mutex);
+        thb_evidence ev{};
+        auto inputs = bind(r, args, argc, false, static_cast<cudaStream_t>(stream), ev, nullptr);
+        const Node& outNode = r.region().at(r.region().output);
+        if (!outNode.tensor()) fail(Category::Unsupported, "GPU-OUTPUT-SHAPE", "device launch needs a tensor output");
+        r.run(inputs, static_cast<cudaStream_t>(stream), ev, output,
+              [&](const Value& o) { checkOutputCount(o, outputCount, true, output); });
+        return THB_STATUS_OK;
+    });
+}
+
+int thb_region_check_errors(thb_region* region, void* stream, char* failure, uint64_t cap) {
+    return guarded(failure, cap, [&] {
+        if (!region) fail(Category::Validation, "GPU-INVALID-REGION", "region handle is null");
+        CompiledRegion& r = *region->impl;
+        std::lock_guard<std::mutex> lock(r.mutex);
+        cudaCheck(cudaSetDevice(r.device()), "cudaSetDevice");
+        auto s = static_cast<cudaStream_t>(stream);
+        PinnedBuffer staged;
+        staged.reserve(std::max<std::size_t>(1, r.errorWordCount()) * sizeof(std::uint32_t));
+        r.copyErrors(s, static_cast<std::uint32_t*>(staged.ptr));
+        r.clearErrors(s);
+        cudaCheck(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+        const std::string id = r.firstFailure(static_cast<const std::uint32_t*>(staged.ptr));
+        if (!id.empty()) fail(Category::Semantic, id, id);
+        return THB_STATUS_OK;
+    });
+}
+
+static int writeOut(const std::string& text, char* buffer, uint64_t capacity, uint64_t* needed) {
+    if (needed) *needed = text.size() + 1;
+    writeText(buffer, capacity, text);
+    return (capacity >= text.size() + 1 || !buffer) ? THB_STATUS_OK : THB_STATUS_ABI;
+}
+
+int thb_region_emit_source(const thb_region* region, char* buffer, uint64_t capacity, uint64_t* needed) {
+    if (!region) return THB_STATUS_ABI;
+    return writeOut(region->impl->source(), buffer, capacity, needed);
+}
+
+int thb_region_dump_plan(const thb_region* region, char* buffer, uint64_t capacity, uint64_t* needed) {
+    if (!region) return THB_STATUS_ABI;
+    return writeOut(region->impl->region().dump() + region->impl->plan().dump(region->impl->region()), buffer,
+                    capacity, needed);
+}
+
+int thb_region_describe(const thb_region_desc* desc, thb_plan_options options, uint32_t what, char* buffer,
+                        uint64_t capacity, uint64_t* needed, uint64_t* counts, char* failure, uint64_t cap) {
+    return guarded(failure, cap, [&] {
+        if (!desc) fail(Category::Validation, "GPU-INVALID-REGION", "region descriptor is null");
+        const Region region = importRegion(*desc);
+        PlanOptions opts;
+        opts.enableReuse = options.enable_reuse != 0;
+        opts.enableFusion = options.enable_fusion != 0;
+        const Plan plan = buildPlan(region, opts);
+        std::vector<GroupKernel> kernels;
+        const std::string source = generateSource(region, plan, kernels);
+        if (counts) {
+            counts[0] = plan.groups.size();
+            counts[1] = 0;
+            counts[2] = 0;
+            for (const auto& g : plan.groups) {
+                counts[1] += g.fused;
+                counts[2] += g.kind != GroupKind::Index;
+            }
+        }
+        std::string text;
+        if (what == THB_DESCRIBE_PLAN) text = region.dump() + plan.dump(region);
+        else if (what == THB_DESCRIBE_SOURCE) text = source;
+        else if (what == THB_DESCRIBE_CUBIN) text = std::to_string(kernels.empty() ? 0 : compileCubin(source).size());
+        else fail(Category::Validation, "GPU-DESCRIBE", "unknown describe selector");
+        return writeOut(text, buffer, capacity, needed);
+    });
+}
+
+int thb_region_plan_counts(const thb_region* region, uint64_t* fusionGroups, uint64_t* fusedGroups, uint64_t* kernels) {
+    if (!region) return THB_STATUS_ABI;
+    const Plan& plan = region->impl->plan();
+    std::uint64_t fused = 0, launches = 0;
+    for (const auto& g : plan.groups) {
+        fused += g.fused;
+        launches += g.kind != GroupKind::Index;
+    }
+    if (fusionGroups) *fusionGroups = plan.groups.size();
+    if (fusedGroups) *fusedGroups = fused;
+    if (kernels) *kernels = launches;
+    return THB_STATUS_OK;
+}
+
+} // extern "C"

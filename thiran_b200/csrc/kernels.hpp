@@ -1,0 +1,41 @@
+// Ahead-of-time compiled sm_100a kernels (reductions, row-wise softmax) and
+// their launchers. Every launcher validates its sizes on the host and returns
+// the launch status; nothing here allocates.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+namespace thb::kernels {
+
+// y[r, :] = softmax(x[r, :]) for a row-major [rows, cols] f32 matrix:
+// m = max_j x, e_j = exp(x_j - m), y_j = e_j / sum_j e_j, with the row sum
+// accumulated in f32 over a fixed tree. Rows up to kMaxSmemRowCols columns are
+// staged whole into shared memory with the bulk-copy (TMA) engine.
+cudaError_t softmaxRowsF32(const float* x, float* y, std::uint64_t rows, std::uint64_t cols, int smCount,
+                           cudaStream_t stream, std::uint32_t* status);
+// y[r] = max_j x[r, j].
+cudaError_t maxRowsF32(const float* x, float* y, std::uint64_t rows, std::uint64_t cols, int smCount,
+                       cudaStream_t stream, std::uint32_t* status);
+// y[r] = sum_j x[r, j], accumulated in f64, rounded once to f32.
+cudaError_t sumRowsF32(const float* x, float* y, std::uint64_t rows, std::uint64_t cols, int smCount,
+                       cudaStream_t stream, std::uint32_t* status);
+// y[c] = sum_r x[r, c], accumulated in f64, rounded once to f32.
+cudaError_t sumColsF32(const float* x, float* y, std::uint64_t rows, std::uint64_t cols, int smCount,
+                       cudaStream_t stream);
+
+// Full-tensor sum in two deterministic passes: pass 1 writes one f64 partial
+// per block of a fixed grid into `partials`, pass 2 adds them in block order.
+// `out64` (optional) receives the f64 total, `out32` (optional) its f32
+// rounding. `partials` must hold sumAllPartialCount(n, smCount) doubles.
+std::uint32_t sumAllPartialCount(std::uint64_t n, int smCount);
+cudaError_t sumAllF32(const float* x, std::uint64_t n, double* partials, std::uint32_t partialCount, double* out64,
+                      float* out32, int smCount, cudaStream_t stream);
+
+// Largest row length the shared-memory staged softmax handles (longer rows
+// take the streaming two-pass kernel).
+constexpr std::uint64_t kMaxSmemRowCols = 8192;
+
+} // namespace thb::kernels

@@ -1,0 +1,473 @@
+// Persistent device runtime (see runtime.hpp).
+#include "runtime.hpp"
+
+#include <algorithm>
+#include <cstring>
+
+#include "kernels.hpp"
+
+namespace thb {
+
+namespace {
+
+void check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) fail(Category::Runtime, "GPU-RUNTIME", std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+std::mutex deviceMutex;
+std::map<int, DeviceInfo> deviceInfos;
+
+std::mutex unobservedMutex;
+std::vector<std::string> unobservedErrors;
+
+} // namespace
+
+DeviceBuffer::~DeviceBuffer() {
+    if (ptr) {
+        int previous = -1;
+        cudaGetDevice(&previous);
+        cudaSetDevice(device);
+        cudaFree(ptr);
+        if (previous >= 0) cudaSetDevice(previous);
+    }
+}
+
+bool DeviceBuffer::reserve(std::size_t want, int ordinal) {
+    if (ptr && bytes >= want) return false;
+    if (ptr) {
+        cudaFree(ptr);
+        ptr = nullptr;
+        bytes = 0;
+    }
+    device = ordinal;
+    const std::size_t rounded = std::max<std::size_t>(256, (want + 255) / 256 * 256);
+    check(cudaMalloc(&ptr, rounded), "cudaMalloc");
+    bytes = rounded;
+    return true;
+}
+
+PinnedBuffer::~PinnedBuffer() {
+    if (ptr) cudaFreeHost(ptr);
+}
+
+void PinnedBuffer::reserve(std::size_t want) {
+    if (ptr && bytes >= want) return;
+    if (ptr) cudaFreeHost(ptr);
+    ptr = nullptr;
+    bytes = 0;
+    const std::size_t rounded = std::max<std::size_t>(64, want);
+    check(cudaMallocHost(&ptr, rounded), "cudaMallocHost");
+    bytes = rounded;
+}
+
+const DeviceInfo& useDevice(int ordinal) {
+    std::lock_guard<std::mutex> lock(deviceMutex);
+    int count = 0;
+    const cudaError_t e = cudaGetDeviceCount(&count);
+    if (e == cudaErrorInsufficientDriver || e == cudaErrorNoDevice || e == cudaErrorInitializationError ||
+        e == cudaErrorSystemDriverMismatch || e == cudaErrorCompatNotSupportedOnDevice) {
+        cudaGetLastError();
+        fail(Category::BackendUnavailable, "GPU-DRIVER-NOT-FOUND", std::string("CUDA driver/device unavailable: ") +
+                                                                        cudaGetErrorString(e));
+    }
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        fail(Category::BackendUnavailable, "GPU-DRIVER-NOT-FOUND", cudaGetErrorString(e));
+    }
+    if (ordinal < 0 || ordinal >= count)
+        fail(Category::InvalidDevice, "GPU-INVALID-DEVICE", "device ordinal " + std::to_string(ordinal) +
+                                                                 " outside [0," + std::to_string(count) + ")");
+    check(cudaSetDevice(ordinal), "cudaSetDevice");
+    auto found = deviceInfos.find(ordinal);
+    if (found == deviceInfos.end()) {
+        cudaDeviceProp prop{};
+        check(cudaGetDeviceProperties(&prop, ordinal), "cudaGetDeviceProperties");
+        if (prop.major < 10)
+            fail(Category::Unsupported, "GPU-UNSUPPORTED-DEVICE",
+                 std::string("this engine is built for sm_100a (B200); device is ") + prop.name);
+        DeviceInfo info;
+        info.ordinal = ordinal;
+        info.smCount = prop.multiProcessorCount;
+        info.major = prop.major;
+        info.minor = prop.minor;
+        found = deviceInfos.emplace(ordinal, info).first;
+    }
+    return found->second;
+}
+
+void recordUnobserved(const std::string& id) {
+    std::lock_guard<std::mutex> lock(unobservedMutex);
+    unobservedErrors.push_back(id);
+}
+
+std::vector<std::string> takeUnobserved() {
+    std::lock_guard<std::mutex> lock(unobservedMutex);
+    std::vector<std::string> out;
+    out.swap(unobservedErrors);
+    return out;
+}
+
+Pending::~Pending() {
+    if (done) cudaEventDestroy(done);
+}
+
+// ---- compiled region --------------------------------------------------------
+
+CompiledRegion::CompiledRegion(const thb_region_desc& desc, PlanOptions options, int device)
+    : region_(importRegion(desc)), plan_(buildPlan(region_, options)), device_(device) {
+    // Planning and code generation need no device: a malformed region fails
+    // before any driver call (NativeGpuTests.cpp:175-198 contract).
+    source_ = generateSource(region_, plan_, kernels_);
+    info_ = &useDevice(device);
+    if (!kernels_.empty()) module_ = compileAndLoad(source_, device, kernels_, moduleJitted_, moduleLoaded_);
+    check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreateWithFlags");
+    errors_.reserve(std::max<std::size_t>(1, plan_.groups.size()) * sizeof(std::uint32_t) + 64, device_);
+    check(cudaMemsetAsync(errors_.ptr, 0, errors_.bytes, stream_), "cudaMemsetAsync");
+    check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+}
+
+CompiledRegion::~CompiledRegion() {
+    if (stream_) {
+        int previous = -1;
+        cudaGetDevice(&previous);
+        cudaSetDevice(device_);
+        cudaStreamSynchronize(stream_);
+        cudaStreamDestroy(stream_);
+        if (previous >= 0) cudaSetDevice(previous);
+    }
+}
+
+DeviceBuffer& CompiledRegion::inputBuffer(std::size_t position) {
+    auto& slot = inputs_[position];
+    if (!slot) slot = std::make_unique<DeviceBuffer>();
+    return *slot;
+}
+
+void CompiledRegion::clearErrors(cudaStream_t stream) {
+    check(cudaMemsetAsync(errors_.ptr, 0, errorWordCount() * sizeof(std::uint32_t), stream), "cudaMemsetAsync(errors)");
+}
+
+void CompiledRegion::copyErrors(cudaStream_t stream, std::uint32_t* host) {
+    check(cudaMemcpyAsync(host, errors_.ptr, errorWordCount() * sizeof(std::uint32_t), cudaMemcpyDeviceToHost, stream),
+          "cudaMemcpyAsync(errors)");
+}
+
+std::string CompiledRegion::firstFailure(const std::uint32_t* words) const {
+    for (std::size_t g = 0; g < plan_.groups.size(); ++g) {
+        if (!words[g]) continue;
+        // Group error codes: bit 0 = checked i64 overflow, bit 1 = recipe
+        // divide by zero (the reference's error words 1 and 2,
+        // src/backend/v0/NativeGpu.cpp:1123-1125).
+        if (words[g] & 1u) return "TH-SPEC-I64-OVERFLOW";
+        if (words[g] & 2u) return "TH021-DIVIDE-BY-ZERO";
+        return "GPU-KERNEL-STATUS";
+    }
+    return {};
+}
+
+void CompiledRegion::planEvidence(thb_evidence& ev) const {
+    ev.logical_tensor_values = plan_.values.size();
+    ev.physical_slots = plan_.slots.size();
+    ev.fusion_groups = plan_.groups.size();
+    ev.logical_intermediates = 0;
+    for (const auto& n : region_.nodes)
+        if (n.tensor() && n.op != Op::Input && n.op != Op::Alias && n.id != region_.output) ++ev.logical_intermediates;
+    ev.materialized_intermediates = 0;
+    for (const auto& v : plan_.values)
+        if (v.value == v.root && v.materialized && v.klass == ValueClass::Temporary) ++ev.materialized_intermediates;
+    ev.physical_temporary_slots = 0;
+    ev.reused_slot_assignments = 0;
+    for (const auto& s : plan_.slots) {
+        if (s.reusable && !s.external) ++ev.physical_temporary_slots;
+        std::uint64_t roots = 0;
+        for (auto id : s.values) {
+            const ValuePlan* v = plan_.value(id);
+            roots += v && v->value == v->root;
+        }
+        if (roots > 1) ev.reused_slot_assignments += roots - 1;
+    }
+    ev.fused_kernel_groups = 0;
+    for (const auto& g : plan_.groups) ev.fused_kernel_groups += g.fused;
+    ev.module_loads = moduleLoaded_ ? 1 : 0;
+    ev.driver_jit_loads = moduleJitted_ ? 1 : 0;
+}
+
+void* CompiledRegion::slotPointer(std::uint32_t value, std::size_t bytes, thb_evidence& ev) {
+    const ValuePlan* v = plan_.value(value);
+    if (!v || !v->slot)
+        fail(Category::Unsupported, "GPU-INVALID-PLAN", "materialized tensor v" + std::to_string(value) + " has no slot");
+    if (outputOverride_ && v->root == outputRoot_) return outputOverride_;
+    auto& buffer = slots_[*v->slot];
+    if (!buffer) buffer = std::make_unique<DeviceBuffer>();
+    if (buffer->reserve(bytes, device_)) {
+        ++ev.allocation_count;
+        ev.allocation_bytes_requested += bytes;
+    }
+    touched_.insert(*v->slot);
+    return buffer->ptr;
+}
+
+void CompiledRegion::launchElementwise(const FusionGroup& group, const std::vector<const Value*>& operands, Value& out,
+                                       cudaStream_t stream, thb_evidence& ev) {
+    const GroupKernel* kernel = nullptr;
+    for (const auto& k : kernels_)
+        if (k.group == group.id) kernel = &k;
+    if (!kernel) fail(Category::Unsupported, "GPU-INVALID-PLAN", "fusion group has no generated kernel");
+    const std::uint64_t n = out.count();
+    if (n == 0) return;
+    bool aligned = (reinterpret_cast<std::uintptr_t>(out.data) % 16) == 0;
+    for (const Value* v : operands) aligned = aligned && (reinterpret_cast<std::uintptr_t>(v->data) % 16) == 0;
+    const unsigned lanes = group.dtype == DType::F32 ? 4 : 2;
+    const std::uint64_t work = aligned ? std::max<std::uint64_t>(1, n / lanes) : n;
+    const std::uint64_t perBlock = static_cast<std::uint64_t>(kBlock) * (aligned ? kUnroll : 1);
+    const std::uint64_t cap = static_cast<std::uint64_t>(info_->smCount) * 8;
+    const unsigned blocks = static_cast<unsigned>(std::max<std::uint64_t>(1, std::min(cap, (work + perBlock - 1) / perBlock)));
+    std::vector<void*> args;
+    void* outPtr = out.data;
+    std::vector<const void*> inPtrs;
+    for (const Value* v : operands) inPtrs.push_back(v->data);
+    std::uint64_t count = n;
+    std::uint32_t* errorWord = static_cast<std::uint32_t*>(errors_.ptr) + (group.id - 1);
+    args.push_back(&outPtr);
+    for (auto& p : inPtrs) args.push_back(&p);
+    args.push_back(&count);
+    args.push_back(&errorWord);
+    const void* fn = aligned ? kernel->vectorKernel : kernel->scalarKernel;
+    check(cudaLaunchKernel(fn, dim3(blocks), dim3(kBlock), args.data(), 0, stream), "cudaLaunchKernel(fusion-group)");
+    ++ev.kernel_launches;
+    ++ev.stream_submissions;
+}
+
+void CompiledRegion::launchReduction(const FusionGroup& group, const Value& in, Value& out, cudaStream_t stream,
+                                     thb_evidence& ev) {
+    const Node& node = region_.at(group.nodes.front());
+    const float* x = static_cast<const float*>(in.data);
+    float* y = static_cast<float*>(out.data);
+    const std::uint64_t rows = in.rank == 2 ? in.shape[0] : 1;
+    const std::uint64_t cols = in.rank == 2 ? in.shape[1] : in.shape[0];
+    if (in.count() == 0) {
+        if (out.count()) check(cudaMemsetAsync(out.data, 0, out.bytes(), stream), "cudaMemsetAsync(empty-sum)");
+        return;
+    }
+    std::uint32_t* status = static_cast<std::uint32_t*>(errors_.ptr) + (group.id - 1);
+    cudaError_t e = cudaSuccess;
+    switch (node.op) {
+    case Op::Softmax: e = kernels::softmaxRowsF32(x, y, rows, cols, info_->smCount, stream, status); break;
+    case Op::RowMax: e = kernels::maxRowsF32(x, y, rows, cols, info_->smCount, stream, status); break;
+    case Op::Sum:
+        if (in.rank == 1) {
+            const std::uint32_t parts = kernels::sumAllPartialCount(in.count(), info_->smCount);
+            auto& scratch = scalars_[0x80000000u | group.id];
+            if (!scratch) scratch = std::make_unique<DeviceBuffer>();
+            if (scratch->reserve(parts * sizeof(double), device_)) {
+                ++ev.allocation_count;
+                ev.allocation_bytes_requested += parts * sizeof(double);
+            }
+            e = kernels::sumAllF32(x, in.count(), static_cast<double*>(scratch->ptr), parts, nullptr, y,
+                                   info_->smCount, stream);
+        } else if (node.axis == 1) {
+            e = kernels::sumRowsF32(x, y, rows, cols, info_->smCount, stream, status);
+        } else {
+            e = kernels::sumColsF32(x, y, rows, cols, info_->smCount, stream);
+        }
+        break;
+    default: fail(Category::Unsupported, "GPU-UNSUPPORTED-OP", "reduction group holds a non-reduction node");
+    }
+    check(e, "reduction launch");
+    ++ev.kernel_launches;
+    ++ev.stream_submissions;
+}
+
+Value CompiledRegion::run(const std::vector<Value>& inputs, cudaStream_t stream, thb_evidence& ev,
+                          void* outputOverride, const std::function<void(const Value&)>& onShapes) {
+    check(cudaSetDevice(device_), "cudaSetDevice");
+    touched_.clear();
+    outputOverride_ = outputOverride;
+    const Node& outputNode = region_.at(region_.output);
+    outputRoot_ = outputNode.tensor() ? region_.canonical(region_.output) : 0;
+    if (outputRoot_) {
+        const ValuePlan* rootPlan = plan_.value(outputRoot_);
+        if (rootPlan) outputRoot_ = rootPlan->root;
+    }
+    if (inputs.size() != region_.inputs.size())
+        fail(Category::Unsupported, "GPU-INPUT-ARITY", "GPU input arity mismatch");
+    std::map<std::uint32_t, Value> values;
+    for (std::size_t i = 0; i < inputs.size(); ++i) values[region_.inputs[i]] = inputs[i];
+
+    // Pass 1: runtime shapes and every host-side check, before any launch.
+    std::map<std::uint32_t, Value> shapes = values;
+    for (const auto& n : region_.nodes) {
+        if (n.op == Op::Input) continue;
+        Value v;
+        v.dtype = n.dtype;
+        v.rank = n.rank;
+        v.tensor = n.tensor();
+        auto dep = [&](std::size_t k) -> const Value& { return shapes.at(region_.canonical(n.dependencies.at(k))); };
+        switch (n.op) {
+        case Op::Integer: v.i64 = n.integer; break;
+        case Op::Float: v.f32 = n.floating; break;
+        case Op::TensorLiteral:
+            for (std::uint32_t a = 0; a < n.rank; ++a) v.shape[a] = static_cast<std::uint64_t>(n.extent[a]);
+            break;
+        case Op::Alias: v = dep(0); break;
+        case Op::Copy: case Op::Negate: case Op::Relu: case Op::Softmax:
+            v.shape[0] = dep(0).shape[0]; v.shape[1] = dep(0).shape[1]; break;
+        case Op::Add: case Op::Subtract: case Op::ElementMultiply: case Op::Extension: {
+            const Value& a = dep(0);
+            for (std::size_t k = 1; k < n.dependencies.size(); ++k) {
+                const Value& b = dep(k);
+                if (b.rank != a.rank || b.shape[0] != a.shape[0] || b.shape[1] != a.shape[1])
+                    fail(Category::Unsupported, "GPU-RUNTIME-SHAPE",
+                         "runtime fused elementwise inputs require equal dtype and shape");
+            }
+            v.shape[0] = a.shape[0]; v.shape[1] = a.shape[1];
+            break;
+        }
+        case Op::Sum: {
+            const Value& a = dep(0);
+            if (a.rank == 2) v.shape[0] = n.axis == 1 ? a.shape[0] : a.shape[1];
+            break;
+        }
+        case Op::RowMax: {
+            const Value& a = dep(0);
+            if (a.shape[1] == 0 && a.shape[0] != 0)
+                fail(Category::Semantic, "TH-SPEC-EMPTY-REDUCTION", "max over an empty row");
+            v.shape[0] = a.shape[0];
+            break;
+        }
+        case Op::Index: {
+            const Value& a = dep(0);
+            std::uint64_t linear = 0;
+            for (std::size_t axis = 0; axis < n.indices.size(); ++axis) {
+                const Value& c = shapes.at(region_.canonical(n.indices[axis]));
+                if (c.onDevice)
+                    fail(Category::Unsupported, "GPU-DYNAMIC-INDEX", "device-computed index coordinates are unsupported");
+                if (c.i64 < 0 || static_cast<std::uint64_t>(c.i64) >= a.shape[axis])
+                    fail(Category::Semantic, "TH-SPEC-BOUNDS", "GPU index is out of bounds");
+                linear = linear * a.shape[axis] + static_cast<std::uint64_t>(c.i64);
+            }
+            v.i64 = static_cast<std::int64_t>(linear);  // linear offset, used in pass 2
+            v.onDevice = true;
+            break;
+        }
+        default: fail(Category::Unsupported, "GPU-UNSUPPORTED-OP", std::string("no GPU lowering for ") + opName(n.op));
+        }
+        for (std::uint32_t a = 0; a < n.rank; ++a)
+            if (n.extent[a] >= 0 && static_cast<std::uint64_t>(n.extent[a]) != v.shape[a])
+                fail(Category::Unsupported, "GPU-RUNTIME-SHAPE", "runtime shape disagrees with the region's shape fact");
+        shapes[n.id] = v;
+    }
+    if (onShapes) onShapes(shapes.at(region_.output));
+
+    // Pass 2: materialise and launch in region order.
+    std::set<std::uint32_t> launched;
+    for (const auto& n : region_.nodes) {
+        if (n.op == Op::Input) continue;
+        Value v = shapes.at(n.id);
+        switch (n.op) {
+        case Op::Integer: case Op::Float: break;
+        case Op::Alias: v = values.at(region_.canonical(n.dependencies.at(0))); break;
+        case Op::TensorLiteral: {
+            v.data = slotPointer(n.id, v.bytes(), ev);
+            bool device = false;
+            for (auto d : n.dependencies) device = device || values.at(d).onDevice;
+            if (device) {
+                const std::size_t w = width(n.dtype);
+                for (std::size_t k = 0; k < n.dependencies.size(); ++k) {
+                    const Value& s = values.at(n.dependencies[k]);
+                    if (s.onDevice)
+                        check(cudaMemcpyAsync(static_cast<char*>(v.data) + k * w, s.data, w, cudaMemcpyDeviceToDevice, stream),
+                              "cudaMemcpyAsync(literal)");
+                    else
+                        check(cudaMemcpyAsync(static_cast<char*>(v.data) + k * w,
+                                              n.dtype == DType::I64 ? static_cast<const void*>(&s.i64)
+                                                                    : static_cast<const void*>(&s.f32),
+                                              w, cudaMemcpyHostToDevice, stream),
+                              "cudaMemcpyAsync(literal)");
+                    ++ev.device_to_device_copies;
+                    ev.device_to_device_bytes += w;
+                }
+            } else if (v.bytes()) {
+                std::vector<unsigned char> host(v.bytes());
+                for (std::size_t k = 0; k < n.dependencies.size(); ++k) {
+                    const Value& s = values.at(n.dependencies[k]);
+                    if (n.dtype == DType::I64) std::memcpy(host.data() + 8 * k, &s.i64, 8);
+                    else std::memcpy(host.data() + 4 * k, &s.f32, 4);
+                }
+                check(cudaMemcpyAsync(v.data, host.data(), host.size(), cudaMemcpyHostToDevice, stream),
+                      "cudaMemcpyAsync(literal)");
+                ++ev.host_to_device_copies;
+                ev.host_to_device_bytes += host.size();
+            }
+            break;
+        }
+        case Op::Copy: {
+            const Value& src = values.at(region_.canonical(n.dependencies.at(0)));
+            v.data = v.bytes() ? slotPointer(n.id, v.bytes(), ev) : nullptr;
+            if (v.bytes()) {
+                check(cudaMemcpyAsync(v.data, src.data, v.bytes(), cudaMemcpyDeviceToDevice, stream), "cudaMemcpyAsync(copy)");
+                ++ev.device_to_device_copies;
+                ev.device_to_device_bytes += v.bytes();
+                ++ev.stream_submissions;
+            }
+            break;
+        }
+        case Op::Index: {
+            const Value& src = values.at(region_.canonical(n.dependencies.at(0)));
+            auto& buffer = scalars_[n.id];
+            if (!buffer) buffer = std::make_unique<DeviceBuffer>();
+            if (buffer->reserve(8, device_)) ++ev.allocation_count;
+            const std::size_t w = width(src.dtype);
+            check(cudaMemcpyAsync(buffer->ptr, static_cast<const char*>(src.data) + static_cast<std::size_t>(v.i64) * w, w,
+                                  cudaMemcpyDeviceToDevice, stream),
+                  "cudaMemcpyAsync(index)");
+            ++ev.device_to_device_copies;
+            ev.device_to_device_bytes += w;
+            v.data = buffer->ptr;
+            v.onDevice = true;
+            break;
+        }
+        default: {
+            const FusionGroup* group = plan_.groupFor(n.id);
+            if (!group) fail(Category::Unsupported, "GPU-INVALID-PLAN", "kernel node outside every group");
+            if (group->nodes.front() != n.id || !launched.insert(group->id).second) break;
+            const Value& shape = shapes.at(group->output);
+            Value out = shape;
+            if (out.rank == 0) {  // scalar reduction result lives in a device scalar buffer
+                auto& buffer = scalars_[group->output];
+                if (!buffer) buffer = std::make_unique<DeviceBuffer>();
+                if (buffer->reserve(8, device_)) ++ev.allocation_count;
+                out.data = buffer->ptr;
+                out.onDevice = true;
+            } else {
+                out.data = out.bytes() ? slotPointer(group->output, out.bytes(), ev) : nullptr;
+            }
+            if (group->kind == GroupKind::Elementwise) {
+                std::vector<const Value*> operands;
+                for (auto id : group->inputs) operands.push_back(&values.at(id));
+                launchElementwise(*group, operands, out, stream, ev);
+            } else {
+                launchReduction(*group, values.at(region_.canonical(n.dependencies.at(0))), out, stream, ev);
+            }
+            values[group->output] = out;
+            continue;
+        }
+        }
+        values[n.id] = v;
+    }
+    ev.planner_owned_allocations = 0;
+    for (auto id : touched_) ev.planner_owned_allocations += !plan_.slots.at(id - 1).external;
+    ev.retained_planner_allocations = ev.planner_owned_allocations;
+    Value result = values.at(region_.output);
+    if (outputOverride && result.tensor && result.data != outputOverride && result.bytes()) {
+        check(cudaMemcpyAsync(outputOverride, result.data, result.bytes(), cudaMemcpyDeviceToDevice, stream),
+              "cudaMemcpyAsync(output)");
+        ++ev.device_to_device_copies;
+        ev.device_to_device_bytes += result.bytes();
+        result.data = outputOverride;
+    }
+    outputOverride_ = nullptr;
+    return result;
+}
+
+} // namespace thb

@@ -1,0 +1,88 @@
+"""Standard TensorRegions of the benchmark workloads.
+
+Each builder reproduces, node for node, the region the reference's
+extractStrictRegion (src/backend/v0/TensorRegion.cpp:230-447) produces for the
+corresponding V0 source, including the Alias node every `let` binding and
+parameter use introduces, so node ids and fusion groups can be compared with
+the reference planner's output directly.
+"""
+from __future__ import annotations
+
+from . import (F32, I64, RegionBuilder, Operation, SCALAR_ADD, SCALAR_MULTIPLY, SCALAR_SUBTRACT,
+               recipe_from_expression)
+
+# ((x*1.5 + 0.25)*x - x)*0.5 + x as one V0 extension scalar recipe: the form
+# in which the reference runs this chain natively (a ConstantF32 recipe; the
+# literal scalar-broadcast source is rejected by its native extractor).
+CHAIN_RECIPE = recipe_from_expression([
+    ("x", 0),                      # 0 x
+    ("c", 1.5),                    # 1
+    (SCALAR_MULTIPLY, 0, 1),       # 2 x*1.5
+    ("c", 0.25),                   # 3
+    (SCALAR_ADD, 2, 3),            # 4 +0.25
+    (SCALAR_MULTIPLY, 4, 0),       # 5 *x
+    (SCALAR_SUBTRACT, 5, 0),       # 6 -x
+    ("c", 0.5),                    # 7
+    (SCALAR_MULTIPLY, 6, 7),       # 8 *0.5
+    (SCALAR_ADD, 8, 0),            # 9 +x
+])
+
+
+def chain_operation() -> Operation:
+    return Operation("research_chain", CHAIN_RECIPE, root=9, arity=1)
+
+
+def f32_chain(n=None):
+    """fn f(x: Tensor<f32,1>) -> Tensor<f32,1> { return research_chain(x) }"""
+    b = RegionBuilder("f")
+    x = b.input(F32, [n])
+    xa = b.alias(x)
+    y = b.extension(chain_operation(), xa)
+    return b.build(y)
+
+
+def i64_region(rows=None, cols=None):
+    """fn f(a,b: Tensor<i64,2>) { let s = a + b; let m = s .* a; return m - b }"""
+    b = RegionBuilder("f")
+    a = b.input(I64, [rows, cols])
+    c = b.input(I64, [rows, cols])
+    s = b.add(b.alias(a), b.alias(c))
+    m = b.mul(b.alias(s), b.alias(a))
+    o = b.sub(b.alias(m), b.alias(c))
+    return b.build(o)
+
+
+def f32_chain4(n=None):
+    """The reference GPU integration chain: C=A+B; D=C.*B; E=D-A; return E+B."""
+    b = RegionBuilder("f")
+    A = b.input(F32, [n])
+    B = b.input(F32, [n])
+    C = b.add(b.alias(A), b.alias(B))
+    D = b.mul(b.alias(C), b.alias(B))
+    E = b.sub(b.alias(D), b.alias(A))
+    F = b.add(b.alias(E), b.alias(B))
+    return b.build(F)
+
+
+def i64_dynamic(n=None):
+    """fn f(x,y: Tensor<i64,1>) { let z=x+y; return z.*y }"""
+    b = RegionBuilder("f")
+    x = b.input(I64, [n])
+    y = b.input(I64, [n])
+    z = b.add(b.alias(x), b.alias(y))
+    r = b.mul(b.alias(z), b.alias(y))
+    return b.build(r)
+
+
+def softmax_rows(rows=None, cols=None):
+    """Row-wise softmax over the last axis (engine-side op)."""
+    b = RegionBuilder("softmax")
+    x = b.input(F32, [rows, cols])
+    return b.build(b.softmax(x))
+
+
+def full_sum(n=None):
+    """Full-tensor sum of a flattened tensor: sum(x, 0) -> f32."""
+    b = RegionBuilder("total")
+    x = b.input(F32, [n])
+    return b.build(b.sum(x, 0))
