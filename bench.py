@@ -131,7 +131,145 @@ class Softmax(Workload):
                 "parallelism": f"row-sharded x{world}, no collective", "l2": "2 GiB/step >> L2"}
 
 
-WORKLOADS = {w.name: w for w in (I64Region(), F32Chain(), Softmax())}
+class Mlp(Workload):
+    name = "mlp"
+    dtype = "bf16"
+    batch, d_in, hidden, d_out = 8192, 4096, 16384, 4096
+    ncu_name = "gemm_mlp"
+
+    def flops_per_step(self):
+        # 2 forward + 3 backward GEMMs of 2*B*4096*16384 each (the reference's
+        # AD also emits a dead dX GEMM, Autodiff.cpp:224, not computed here).
+        return 5 * 2 * self.batch * self.d_in * self.hidden
+
+    def config(self, world):
+        return {"workload": "2-layer MLP fwd+bwd+SGD: batch 8192, 4096->16384->4096, ReLU, MSE vs N(0,1) targets, "
+                            "Xavier-uniform weights, seed 4; bf16 GEMM operands, f32 accumulate",
+                "global_batch": self.batch, "dims": [self.d_in, self.hidden, self.d_out],
+                "parallelism": f"data-parallel x{world}, NCCL all-reduce of dW1+dW2" if world > 1 else "single GPU",
+                "l2": "weights 2x128 MiB bf16 + activations >> 126 MB L2"}
+
+
+WORKLOADS = {w.name: w for w in (I64Region(), F32Chain(), Softmax(), Mlp())}
+
+
+def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_over_ranks):
+    b = workload.batch // world
+    d_in, hidden, d_out = workload.d_in, workload.hidden, workload.d_out
+    g = torch.Generator(device="cuda").manual_seed(4)
+    bound1 = (6.0 / (d_in + hidden)) ** 0.5
+    bound2 = (6.0 / (hidden + d_out)) ** 0.5
+    w1 = (torch.rand((d_in, hidden), device="cuda", generator=g) * 2 - 1) * bound1
+    w2 = (torch.rand((hidden, d_out), device="cuda", generator=g) * 2 - 1) * bound2
+    gx = torch.Generator(device="cuda").manual_seed(4 + 1000 * rank)
+    x = torch.randn((b, d_in), device="cuda", generator=gx)
+    t = torch.randn((b, d_out), device="cuda", generator=gx)
+    stream = torch.cuda.Stream()
+    s = stream.cuda_stream
+    session = thb.MlpSession(b, d_in, hidden, d_out, global_batch=workload.batch, device=local)
+    dw1 = session.bind(thb.MLP_DW1, torch.empty((d_in, hidden), device="cuda"))
+    dw2 = session.bind(thb.MLP_DW2, torch.empty((hidden, d_out), device="cuda"))
+    loss = session.bind(thb.MLP_LOSS_SUM, torch.zeros(2, dtype=torch.float64, device="cuda"))
+    session.set_weights(w1, w2, s)
+    lr = 1e-3
+
+    def step():
+        session.forward_backward(x, t, s)
+        if world > 1:
+            with torch.cuda.stream(stream):
+                dist.all_reduce(dw1)
+                dist.all_reduce(dw2)
+        session.apply_sgd(lr, s)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    thb.check_device_status(local, s)
+    session.enable_timing(True)
+    sampler = ClockSampler(local)
+    sampler.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    gemm_ms, gemm_launches = session.read_timing()
+    session.enable_timing(False)
+    thb.check_device_status(local, s)
+    total_ms = max_over_ranks(start.elapsed_time(end))
+    flops_rank = workload.flops_per_step() / world
+    value = workload.flops_per_step() * args.steps / (total_ms / 1e3) / 1e12
+    achieved = (flops_rank / 5) * gemm_launches / (gemm_ms / 1e3) / 1e12
+
+    # End to end: X, T from pinned host memory every step, loss read back.
+    hx = x.cpu().pin_memory()
+    ht = t.cpu().pin_memory()
+    host_loss = torch.zeros(2, dtype=torch.float64).pin_memory()
+    e2e_steps = args.e2e_steps or max(3, min(args.steps, 10))
+    barrier()
+    t0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        for _ in range(e2e_steps):
+            x.copy_(hx, non_blocking=True)
+            t.copy_(ht, non_blocking=True)
+            step()
+            host_loss.copy_(loss, non_blocking=True)
+            stream.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    e2e_value = workload.flops_per_step() * e2e_steps / e2e_s / 1e12
+
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "tests"))
+        import oracle_lib
+        rng = np.random.default_rng(4)
+        cb, ci, ch, co = 256, 512, 1024, 512
+        xs = rng.standard_normal((cb, ci)).astype(np.float32)
+        ts = rng.standard_normal((cb, co)).astype(np.float32)
+        w1s = rng.uniform(-0.05, 0.05, (ci, ch)).astype(np.float32)
+        w2s = rng.uniform(-0.05, 0.05, (ch, co)).astype(np.float32)
+        reps = 3
+        c0 = time.perf_counter()
+        for _ in range(reps):
+            oracle_lib.mlp_step(xs, ts, w1s, w2s, lr)
+        cpu_s = time.perf_counter() - c0
+        cpu_baseline = {"value": 5 * 2 * cb * ci * ch * reps / cpu_s / 1e12, "unit": "TFLOP/s", "cores": 1,
+                        "kind": "port",
+                        "sample": f"{reps} MLP steps at batch {cb}, {ci}->{ch}->{co} (the oracle's f64-accumulated "
+                                  f"restatement; the reference trains only in its interpreter), {cpu_s:.2f} s"}
+    if rank == 0:
+        peak = 1383.9
+        peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+        peak_kind = "fallback 1.4 PFLOP/s sustained"
+        if os.path.exists(peaks_path):
+            with open(peaks_path) as f:
+                peak = float(json.load(f)["bf16_tflops_sustained"])
+            peak_kind = "measured (MEASURED_PEAKS.json bf16_tflops_sustained)"
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (torch.Generator on device, seeded)", "config": workload.config(world),
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "kernel": "tcgen05 GEMM (128x256 tiles, TMEM accumulators)",
+                         "algorithmic_flops_per_launch": flops_rank / 5,
+                         "avg_launch_ms": gemm_ms / max(1, gemm_launches), "peak_source": peak_kind},
+            "cpu_baseline": cpu_baseline,
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": (x.numel() + t.numel()) * 4,
+                    "d2h_bytes_per_step": 16, "steps": e2e_steps, "api": "thb_mlp_* (inputs from pinned host)"},
+            "gpu_launches": args.steps * 10,
+            "clocks": clocks,
+            "loss": float(loss[0].item()) / (workload.batch * d_out) if world == 1 else None,
+        }
+        print(json.dumps(line), flush=True)
+    session.release()
+    return 0
 
 
 # ---- clocks ------------------------------------------------------------------------
@@ -329,8 +467,14 @@ def main():
     p.add_argument("--workload", default="i64_region", choices=sorted(WORKLOADS))
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--shrink", type=int, default=1,
+                   help="divide the leading extent (small cases for profiler captures; not a bench line)")
     args = p.parse_args()
     workload = WORKLOADS[args.workload]
+    if args.shrink > 1:
+        for attr in ("rows", "n", "batch"):
+            if hasattr(workload, attr):
+                setattr(workload, attr, getattr(workload, attr) // args.shrink)
     if args.impl == "reference":
         return reference_arm(args, workload)
 
@@ -356,6 +500,12 @@ def main():
         t = torch.tensor([x], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    if workload.name == "mlp":
+        rc = run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_over_ranks)
+        if world > 1:
+            dist.destroy_process_group()
+        return rc
 
     spec, inputs, out = workload.build(torch, rank, world)
     region = spec.compile(local)

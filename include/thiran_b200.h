@@ -318,6 +318,90 @@ int thb_region_plan_counts(const thb_region* region, uint64_t* fusion_groups, ui
  *                       the cubin size in bytes as decimal text.
  * counts (optional, 3 entries): fusion groups, fused groups, kernel groups. */
 enum { THB_DESCRIBE_PLAN = 0, THB_DESCRIBE_SOURCE = 1, THB_DESCRIBE_CUBIN = 2 };
+
+/* ---- tensor-core GEMM ----------------------------------------------------
+ * Engine addition: the reference's only matmul is its Evaluator's sequential
+ * f32 triple loop (src/semantic/v0/Evaluator.cpp:125-154), rejected by the
+ * native extractor ("MatMul lowering deferred", TensorRegion.cpp:424).
+ * C[M,N] = A[M,K] B[K,N], bf16 operands, f32 accumulation in tensor memory
+ * (tcgen05). A is K-major (stored [M][K]) or MN-major (stored [K][M]); B is
+ * K-major (stored [N][K]) or MN-major (stored [K][N]); leading dimensions in
+ * elements, multiples of 8; operands 16-byte aligned. */
+enum { THB_MAJOR_K = 0, THB_MAJOR_MN = 1 };
+enum {
+    THB_EPI_F32 = 0,       /* C f32  = acc */
+    THB_EPI_BF16 = 1,      /* C bf16 = acc */
+    THB_EPI_RELU_BF16 = 2, /* C bf16 = max(acc, 0) */
+    THB_EPI_MASK_BF16 = 3  /* C bf16 = aux[i,j] > 0 ? acc : 0 (aux bf16 [M][N]) */
+};
+typedef struct thb_gemm_desc {
+    uint64_t m, n, k;
+    const void* a;
+    uint32_t a_major;
+    uint64_t lda;
+    const void* b;
+    uint32_t b_major;
+    uint64_t ldb;
+    void* c;
+    uint64_t ldc;
+    uint32_t epilogue;
+    const void* aux;
+    uint64_t ld_aux;
+    void* c_f32_copy; /* optional f32 copy of a bf16 epilogue's values (ld = ldc) */
+} thb_gemm_desc;
+
+/* Stream-ordered launch on `device` (pointers are device memory there). A
+ * bounded wait that expires inside the kernel latches GPU-KERNEL-TIMEOUT in
+ * the device status word, read by thb_device_check_status. */
+int thb_gemm_bf16(int device, const thb_gemm_desc* desc, void* stream, char* failure, uint64_t failure_cap);
+
+/* Synchronises `stream`, reads and clears the device status word that
+ * kernels outside a region (GEMM, MLP steps) latch. */
+int thb_device_check_status(int device, void* stream, char* failure, uint64_t failure_cap);
+
+/* ---- MLP training step -----------------------------------------------------
+ * Replaces training::trainingStep (src/training/v0/Training.cpp:382-432) for
+ * the two-layer MLP H = relu(X W1), Y = H W2, L = mean((Y - T)^2), whose
+ * backward follows the reverse-AD rules of src/autodiff/v0/Autodiff.cpp
+ * (matmul :216-227) and whose update is plain SGD (Training.cpp:368-371).
+ * W1 is [in][hidden], W2 [hidden][out], f32 masters with bf16 GEMM copies.
+ * `global_batch` is the batch summed over data-parallel ranks; dY is scaled
+ * by 2 / (global_batch * out) so that summing rank gradients gives the
+ * gradient of the global mean loss. All pointers are device memory. */
+typedef struct thb_mlp thb_mlp;
+enum {
+    THB_MLP_W1 = 0, THB_MLP_W2 = 1, THB_MLP_DW1 = 2, THB_MLP_DW2 = 3,
+    THB_MLP_Y = 4, THB_MLP_H = 5, THB_MLP_LOSS_SUM = 6
+};
+int thb_mlp_create(int device, uint64_t batch, uint64_t global_batch, uint64_t in, uint64_t hidden, uint64_t out,
+                   thb_mlp** session, char* failure, uint64_t failure_cap);
+void thb_mlp_release(thb_mlp* session);
+/* Copies f32 W1, W2 (device) into the session and refreshes the bf16 copies. */
+int thb_mlp_set_weights(thb_mlp* session, const float* w1, const float* w2, void* stream, char* failure,
+                        uint64_t failure_cap);
+/* Forward, loss and backward for x [batch][in], t [batch][out] (f32, 16-byte
+ * aligned): fills Y, H, dW1, dW2 and the rank's loss sum. */
+int thb_mlp_forward_backward(thb_mlp* session, const float* x, const float* t, void* stream, char* failure,
+                             uint64_t failure_cap);
+/* W -= lr dW for both layers (after any gradient all-reduce). */
+int thb_mlp_apply_sgd(thb_mlp* session, float lr, void* stream, char* failure, uint64_t failure_cap);
+/* One full single-device step: forward_backward then apply_sgd. */
+int thb_mlp_step(thb_mlp* session, const float* x, const float* t, float lr, void* stream, char* failure,
+                 uint64_t failure_cap);
+/* Device pointer and element count of a session buffer (THB_MLP_*); Y and
+ * dW are f32, H bf16, the loss sum one f64. */
+int thb_mlp_buffer(thb_mlp* session, uint32_t which, void** device_pointer, uint64_t* elements);
+/* Replaces a session buffer by caller-owned device memory of the same size
+ * and type (for example a tensor a collective library reduces in place);
+ * the caller keeps it alive while the session uses it. The previous
+ * contents are not copied. */
+int thb_mlp_bind(thb_mlp* session, uint32_t which, void* device_pointer);
+/* CUDA-event timing of the session's GEMM launches, recorded on the stream
+ * they are launched on (up to 512 launches between reads). */
+int thb_mlp_enable_timing(thb_mlp* session, int enabled);
+/* Waits for the recorded events and returns the summed GEMM device time (ms)
+ * and launch count since the previous read, then resets them. */
+int thb_mlp_read_timing(thb_mlp* session, double* gemm_ms, uint64_t* gemm_launches);
 int thb_region_describe(const thb_region_desc* region, thb_plan_options options, uint32_t what,
                         char* buffer, uint64_t capacity, uint64_t* needed, uint64_t* counts,
                         char* failure, uint64_t failure_cap);

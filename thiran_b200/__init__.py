@@ -111,6 +111,17 @@ class DeviceInfo(C.Structure):
                 ("reserved", C.c_int32), ("name", C.c_char * 256), ("error_code", C.c_char * 64)]
 
 
+MAJOR_K, MAJOR_MN = 0, 1
+EPI_F32, EPI_BF16, EPI_RELU_BF16, EPI_MASK_BF16 = 0, 1, 2, 3
+
+
+class GemmDesc(C.Structure):
+    _fields_ = [("m", C.c_uint64), ("n", C.c_uint64), ("k", C.c_uint64), ("a", C.c_void_p), ("a_major", C.c_uint32),
+                ("lda", C.c_uint64), ("b", C.c_void_p), ("b_major", C.c_uint32), ("ldb", C.c_uint64),
+                ("c", C.c_void_p), ("ldc", C.c_uint64), ("epilogue", C.c_uint32), ("aux", C.c_void_p),
+                ("ld_aux", C.c_uint64), ("c_f32_copy", C.c_void_p)]
+
+
 # ---- library --------------------------------------------------------------------------
 
 _lib = None
@@ -141,7 +152,104 @@ SIGNATURES = {
                                          C.POINTER(C.c_uint64)]),
     "thb_region_describe": (C.c_int, [C.POINTER(RegionDesc), PlanOptions, C.c_uint32, C.c_char_p, C.c_uint64,
                                       C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.c_char_p, C.c_uint64]),
+    "thb_gemm_bf16": (C.c_int, [C.c_int, C.POINTER(GemmDesc), C.c_void_p, C.c_char_p, C.c_uint64]),
+    "thb_device_check_status": (C.c_int, [C.c_int, C.c_void_p, C.c_char_p, C.c_uint64]),
+    "thb_mlp_create": (C.c_int, [C.c_int, C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64,
+                                 C.POINTER(C.c_void_p), C.c_char_p, C.c_uint64]),
+    "thb_mlp_release": (None, [C.c_void_p]),
+    "thb_mlp_set_weights": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p, C.c_uint64]),
+    "thb_mlp_forward_backward": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p, C.c_uint64]),
+    "thb_mlp_apply_sgd": (C.c_int, [C.c_void_p, C.c_float, C.c_void_p, C.c_char_p, C.c_uint64]),
+    "thb_mlp_step": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_char_p, C.c_uint64]),
+    "thb_mlp_buffer": (C.c_int, [C.c_void_p, C.c_uint32, C.POINTER(C.c_void_p), C.POINTER(C.c_uint64)]),
+    "thb_mlp_bind": (C.c_int, [C.c_void_p, C.c_uint32, C.c_void_p]),
+    "thb_mlp_enable_timing": (C.c_int, [C.c_void_p, C.c_int]),
+    "thb_mlp_read_timing": (C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
 }
+
+MLP_W1, MLP_W2, MLP_DW1, MLP_DW2, MLP_Y, MLP_H, MLP_LOSS_SUM = range(7)
+
+
+class MlpSession:
+    """Two-layer MLP training session (thb_mlp): H = relu(X W1), Y = H W2,
+    L = mean((Y - T)^2), SGD. Tensors are torch CUDA tensors."""
+
+    def __init__(self, batch, d_in, hidden, d_out, global_batch=None, device=0):
+        self.batch, self.d_in, self.hidden, self.d_out = batch, d_in, hidden, d_out
+        self.global_batch = global_batch or batch
+        self.device = device
+        handle = C.c_void_p()
+        fail = _failure()
+        _raise(lib().thb_mlp_create(device, batch, self.global_batch, d_in, hidden, d_out, C.byref(handle), fail,
+                                    len(fail)), fail)
+        self.handle = handle
+
+    def _call(self, name, *args):
+        fail = _failure()
+        _raise(getattr(lib(), name)(self.handle, *args, fail, len(fail)), fail)
+
+    def set_weights(self, w1, w2, stream=0):
+        self._call("thb_mlp_set_weights", w1.data_ptr(), w2.data_ptr(), C.c_void_p(stream))
+
+    def forward_backward(self, x, t, stream=0):
+        self._call("thb_mlp_forward_backward", x.data_ptr(), t.data_ptr(), C.c_void_p(stream))
+
+    def apply_sgd(self, lr, stream=0):
+        self._call("thb_mlp_apply_sgd", C.c_float(lr), C.c_void_p(stream))
+
+    def step(self, x, t, lr, stream=0):
+        self._call("thb_mlp_step", x.data_ptr(), t.data_ptr(), C.c_float(lr), C.c_void_p(stream))
+
+    def enable_timing(self, enabled=True):
+        if lib().thb_mlp_enable_timing(self.handle, int(enabled)) != STATUS_OK:
+            raise GpuError(STATUS_BACKEND, "GPU-RUNTIME: cannot create timing events")
+
+    def read_timing(self):
+        """(summed GEMM device ms, GEMM launches) since the previous read."""
+        ms, n = C.c_double(), C.c_uint64()
+        if lib().thb_mlp_read_timing(self.handle, C.byref(ms), C.byref(n)) != STATUS_OK:
+            raise GpuError(STATUS_BACKEND, "GPU-RUNTIME: cannot read timing events")
+        return ms.value, int(n.value)
+
+    def bind(self, which, tensor):
+        """Makes the session use `tensor`'s device memory for buffer `which`."""
+        if lib().thb_mlp_bind(self.handle, which, tensor.data_ptr()) != STATUS_OK:
+            raise GpuError(STATUS_ABI, "GPU-MLP-ARGUMENT: cannot bind buffer")
+        return tensor
+
+    def buffer(self, which):
+        """(device pointer, element count) of a session buffer."""
+        ptr, count = C.c_void_p(), C.c_uint64()
+        if lib().thb_mlp_buffer(self.handle, which, C.byref(ptr), C.byref(count)) != STATUS_OK:
+            raise GpuError(STATUS_ABI, "GPU-MLP-ARGUMENT: unknown buffer")
+        return ptr.value, int(count.value)
+
+    def release(self):
+        if self.handle:
+            lib().thb_mlp_release(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
+
+
+def gemm(a, b, c, m, n, k, a_major=MAJOR_K, b_major=MAJOR_K, epilogue=EPI_F32, aux=None, c_f32=None,
+         device=0, stream=0, lda=None, ldb=None, ldc=None):
+    """C = A B on the tensor cores; a, b, c, aux are CUDA tensors (torch)."""
+    desc = GemmDesc(m, n, k, a.data_ptr(), a_major, lda or (m if a_major == MAJOR_MN else k), b.data_ptr(), b_major,
+                    ldb or (n if b_major == MAJOR_MN else k), c.data_ptr(), ldc or n, epilogue,
+                    aux.data_ptr() if aux is not None else None, n if aux is not None else 0,
+                    c_f32.data_ptr() if c_f32 is not None else None)
+    fail = _failure()
+    _raise(lib().thb_gemm_bf16(device, C.byref(desc), C.c_void_p(stream), fail, len(fail)), fail)
+
+
+def check_device_status(device=0, stream=0):
+    fail = _failure()
+    _raise(lib().thb_device_check_status(device, C.c_void_p(stream), fail, len(fail)), fail)
 
 
 def lib() -> C.CDLL:

@@ -4,6 +4,8 @@
 #include <memory>
 #include <thread>
 
+#include "gemm.hpp"
+#include "mlp.hpp"
 #include "runtime.hpp"
 
 struct thb_region {
@@ -12,6 +14,23 @@ struct thb_region {
 
 struct thb_pending {
     std::unique_ptr<thb::Pending> impl;
+};
+
+struct thb_mlp {
+    int device = 0;
+    int smCount = 148;
+    thb::mlp::Buffers b;
+    thb::mlp::GemmTimer timer;
+    std::vector<std::unique_ptr<thb::DeviceBuffer>> owned;
+    ~thb_mlp() {
+        for (auto& e : timer.events)
+            if (e) cudaEventDestroy(e);
+    }
+    void* alloc(std::size_t bytes) {
+        owned.push_back(std::make_unique<thb::DeviceBuffer>());
+        owned.back()->reserve(bytes, device);
+        return owned.back()->ptr;
+    }
 };
 
 namespace {
@@ -395,6 +414,189 @@ int thb_region_check_errors(thb_region* region, void* stream, char* failure, uin
         if (!id.empty()) fail(Category::Semantic, id, id);
         return THB_STATUS_OK;
     });
+}
+
+int thb_gemm_bf16(int device, const thb_gemm_desc* desc, void* stream, char* failure, uint64_t cap) {
+    return guarded(failure, cap, [&] {
+        if (!desc) fail(Category::Validation, "GPU-GEMM-ARGUMENT", "GEMM descriptor is null");
+        const DeviceInfo& info = useDevice(device);
+        gemm::Problem q;
+        q.m = desc->m;
+        q.n = desc->n;
+        q.k = desc->k;
+        q.a = desc->a;
+        q.aMajorMN = desc->a_major == THB_MAJOR_MN;
+        q.lda = desc->lda;
+        q.b = desc->b;
+        q.bMajorMN = desc->b_major == THB_MAJOR_MN;
+        q.ldb = desc->ldb;
+        q.c = desc->c;
+        q.ldc = desc->ldc;
+        q.epilogue = static_cast<int>(desc->epilogue);
+        q.aux = desc->aux;
+        q.ldAux = desc->ld_aux;
+        q.c2 = desc->c_f32_copy;
+        if (desc->a_major > THB_MAJOR_MN || desc->b_major > THB_MAJOR_MN)
+            fail(Category::Validation, "GPU-GEMM-ARGUMENT", "operand major must be THB_MAJOR_K or THB_MAJOR_MN");
+        if (const char* bad = gemm::validate(q)) fail(Category::Validation, "GPU-GEMM-ARGUMENT", bad);
+        cudaCheck(gemm::run(q, info.smCount, deviceStatus(device), static_cast<cudaStream_t>(stream)), "tcgen05 GEMM launch");
+        return THB_STATUS_OK;
+    });
+}
+
+int thb_device_check_status(int device, void* stream, char* failure, uint64_t cap) {
+    return guarded(failure, cap, [&] {
+        std::uint32_t* word = deviceStatus(device);
+        auto s = static_cast<cudaStream_t>(stream);
+        std::uint32_t host = 0;
+        cudaCheck(cudaMemcpyAsync(&host, word, sizeof host, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync(status)");
+        cudaCheck(cudaMemsetAsync(word, 0, sizeof host, s), "cudaMemsetAsync(status)");
+        cudaCheck(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+        if (host) fail(Category::Runtime, statusText(host), "a kernel reported status " + std::to_string(host));
+        return THB_STATUS_OK;
+    });
+}
+
+int thb_mlp_create(int device, uint64_t batch, uint64_t globalBatch, uint64_t in, uint64_t hidden, uint64_t out,
+                   thb_mlp** session, char* failure, uint64_t cap) {
+    return guarded(failure, cap, [&] {
+        if (!session) fail(Category::Validation, "GPU-MLP-ARGUMENT", "session result pointer is null");
+        *session = nullptr;
+        if (!batch || !in || !hidden || !out || globalBatch < batch)
+            fail(Category::Validation, "GPU-MLP-ARGUMENT", "MLP extents must be positive and global_batch >= batch");
+        if (batch % 8 || in % 8 || hidden % 8 || out % 8)
+            fail(Category::Validation, "GPU-MLP-ARGUMENT", "MLP extents must be multiples of 8 (16-byte rows)");
+        const DeviceInfo& info = useDevice(device);
+        auto s = std::make_unique<thb_mlp>();
+        s->device = device;
+        s->smCount = info.smCount;
+        auto& b = s->b;
+        b.batch = batch;
+        b.globalBatch = globalBatch;
+        b.in = in;
+        b.hidden = hidden;
+        b.out = out;
+        b.w1 = static_cast<float*>(s->alloc(in * hidden * 4));
+        b.w2 = static_cast<float*>(s->alloc(hidden * out * 4));
+        b.w1b = s->alloc(in * hidden * 2);
+        b.w2b = s->alloc(hidden * out * 2);
+        b.xb = s->alloc(batch * in * 2);
+        b.h = s->alloc(batch * hidden * 2);
+        b.y = static_cast<float*>(s->alloc(batch * out * 4));
+        b.dy = s->alloc(batch * out * 2);
+        b.dh = s->alloc(batch * hidden * 2);
+        b.dw1 = static_cast<float*>(s->alloc(in * hidden * 4));
+        b.dw2 = static_cast<float*>(s->alloc(hidden * out * 4));
+        b.lossPartials = static_cast<double*>(s->alloc(mlp::lossPartialCount(info.smCount) * 8));
+        b.lossSum = static_cast<double*>(s->alloc(8));
+        *session = s.release();
+        return THB_STATUS_OK;
+    });
+}
+
+void thb_mlp_release(thb_mlp* session) { delete session; }
+
+int thb_mlp_set_weights(thb_mlp* s, const float* w1, const float* w2, void* stream, char* failure, uint64_t cap) {
+    return guarded(failure, cap, [&] {
+        if (!s || !w1 || !w2) fail(Category::Validation, "GPU-MLP-ARGUMENT", "null session or weights");
+        useDevice(s->device);
+        auto st = static_cast<cudaStream_t>(stream);
+        const auto& b = s->b;
+        cudaCheck(cudaMemcpyAsync(b.w1, w1, b.in * b.hidden * 4, cudaMemcpyDeviceToDevice, st), "cudaMemcpyAsync(W1)");
+        cudaCheck(cudaMemcpyAsync(b.w2, w2, b.hidden * b.out * 4, cudaMemcpyDeviceToDevice, st), "cudaMemcpyAsync(W2)");
+        cudaCheck(mlp::castToBf16(b.w1, b.w1b, b.in * b.hidden, s->smCount, st), "cast W1");
+        cudaCheck(mlp::castToBf16(b.w2, b.w2b, b.hidden * b.out, s->smCount, st), "cast W2");
+        return THB_STATUS_OK;
+    });
+}
+
+int thb_mlp_forward_backward(thb_mlp* s, const float* x, const float* t, void* stream, char* failure, uint64_t cap) {
+    return guarded(failure, cap, [&] {
+        if (!s || !x || !t) fail(Category::Validation, "GPU-MLP-ARGUMENT", "null session or data");
+        if ((reinterpret_cast<std::uintptr_t>(x) | reinterpret_cast<std::uintptr_t>(t)) % 16)
+            fail(Category::Validation, "GPU-MLP-ARGUMENT", "x and t must be 16-byte aligned");
+        useDevice(s->device);
+        cudaCheck(mlp::forwardBackward(s->b, x, t, s->smCount, deviceStatus(s->device), static_cast<cudaStream_t>(stream),
+                                       &s->timer),
+                  "MLP forward/backward");
+        return THB_STATUS_OK;
+    });
+}
+
+int thb_mlp_apply_sgd(thb_mlp* s, float lr, void* stream, char* failure, uint64_t cap) {
+    return guarded(failure, cap, [&] {
+        if (!s) fail(Category::Validation, "GPU-MLP-ARGUMENT", "null session");
+        useDevice(s->device);
+        cudaCheck(mlp::applySgd(s->b, lr, s->smCount, static_cast<cudaStream_t>(stream)), "MLP SGD");
+        return THB_STATUS_OK;
+    });
+}
+
+int thb_mlp_step(thb_mlp* s, const float* x, const float* t, float lr, void* stream, char* failure, uint64_t cap) {
+    const int status = thb_mlp_forward_backward(s, x, t, stream, failure, cap);
+    if (status != THB_STATUS_OK) return status;
+    return thb_mlp_apply_sgd(s, lr, stream, failure, cap);
+}
+
+int thb_mlp_buffer(thb_mlp* s, uint32_t which, void** pointer, uint64_t* elements) {
+    if (!s || !pointer) return THB_STATUS_ABI;
+    const auto& b = s->b;
+    switch (which) {
+    case THB_MLP_W1: *pointer = b.w1; if (elements) *elements = b.in * b.hidden; break;
+    case THB_MLP_W2: *pointer = b.w2; if (elements) *elements = b.hidden * b.out; break;
+    case THB_MLP_DW1: *pointer = b.dw1; if (elements) *elements = b.in * b.hidden; break;
+    case THB_MLP_DW2: *pointer = b.dw2; if (elements) *elements = b.hidden * b.out; break;
+    case THB_MLP_Y: *pointer = b.y; if (elements) *elements = b.batch * b.out; break;
+    case THB_MLP_H: *pointer = b.h; if (elements) *elements = b.batch * b.hidden; break;
+    case THB_MLP_LOSS_SUM: *pointer = b.lossSum; if (elements) *elements = 1; break;
+    default: return THB_STATUS_ABI;
+    }
+    return THB_STATUS_OK;
+}
+
+int thb_mlp_enable_timing(thb_mlp* s, int enabled) {
+    if (!s) return THB_STATUS_ABI;
+    if (enabled && !s->timer.events[0]) {
+        if (cudaSetDevice(s->device) != cudaSuccess) return THB_STATUS_BACKEND;
+        for (auto& e : s->timer.events)
+            if (cudaEventCreate(&e) != cudaSuccess) return THB_STATUS_BACKEND;
+    }
+    s->timer.enabled = enabled != 0;
+    s->timer.used = 0;
+    s->timer.launches = 0;
+    return THB_STATUS_OK;
+}
+
+int thb_mlp_read_timing(thb_mlp* s, double* gemmMs, uint64_t* gemmLaunches) {
+    if (!s || !gemmMs || !gemmLaunches) return THB_STATUS_ABI;
+    double total = 0.0;
+    for (unsigned k = 0; k + 1 < s->timer.used; k += 2) {
+        if (cudaEventSynchronize(s->timer.events[k + 1]) != cudaSuccess) return THB_STATUS_BACKEND;
+        float ms = 0.0f;
+        if (cudaEventElapsedTime(&ms, s->timer.events[k], s->timer.events[k + 1]) != cudaSuccess) return THB_STATUS_BACKEND;
+        total += ms;
+    }
+    *gemmMs = total;
+    *gemmLaunches = s->timer.launches;
+    s->timer.used = 0;
+    s->timer.launches = 0;
+    return THB_STATUS_OK;
+}
+
+int thb_mlp_bind(thb_mlp* s, uint32_t which, void* pointer) {
+    if (!s || !pointer || reinterpret_cast<std::uintptr_t>(pointer) % 16) return THB_STATUS_ABI;
+    auto& b = s->b;
+    switch (which) {
+    case THB_MLP_W1: b.w1 = static_cast<float*>(pointer); break;
+    case THB_MLP_W2: b.w2 = static_cast<float*>(pointer); break;
+    case THB_MLP_DW1: b.dw1 = static_cast<float*>(pointer); break;
+    case THB_MLP_DW2: b.dw2 = static_cast<float*>(pointer); break;
+    case THB_MLP_Y: b.y = static_cast<float*>(pointer); break;
+    case THB_MLP_H: b.h = pointer; break;
+    case THB_MLP_LOSS_SUM: b.lossSum = static_cast<double*>(pointer); break;
+    default: return THB_STATUS_ABI;
+    }
+    return THB_STATUS_OK;
 }
 
 static int writeOut(const std::string& text, char* buffer, uint64_t capacity, uint64_t* needed) {

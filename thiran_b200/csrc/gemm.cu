@@ -1,0 +1,441 @@
+// bf16 x bf16 -> f32 GEMM on the 5th-generation tensor cores (tcgen05) for sm_100a.
+//
+// C[M,N] = A[M,K] * B[K,N] with f32 accumulation in tensor memory. Operands
+// are read by TMA (no multicast) into 128B-swizzled shared memory; each
+// operand may be K-major (A stored [M][K], B stored [N][K]) or MN-major
+// (A stored [K][M], B stored [K][N]), so the transposed products of a
+// reverse-AD backward pass (dW = X^T dH) need no transpose copies.
+//
+// One persistent CTA per SM, 192 threads:
+//   warp 0      TMA producer (one lane): 4-stage ring of {A 128x64, B 256x64}
+//   warp 1      TMEM owner (alloc/dealloc 512 columns) and MMA issuer (one
+//               lane): 4 x tcgen05.mma (M=128, N=256, K=16) per stage
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, fused op, stores
+// Two TMEM accumulators (2 x 256 columns) let the epilogue of tile i overlap
+// the MMAs of tile i+1. Every mbarrier wait is bounded: on expiry the CTA
+// raises bit 4 of the status word, drains its copies and MMAs, frees TMEM and
+// returns.
+//
+// The reference's only matmul is its Evaluator's sequential f32 triple loop
+// (src/semantic/v0/Evaluator.cpp:125-154); reverse-mode rules dA = dZ B^T,
+// dB = A^T dZ come from src/autodiff/v0/Autodiff.cpp:216-227.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <mutex>
+
+#include "gemm.hpp"
+
+namespace thb::gemm {
+namespace {
+
+constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
+constexpr int kThreads = 192;
+constexpr uint32_t kABytes = kBM * kBK * 2;  // 16 KB
+constexpr uint32_t kBBytes = kBN * kBK * 2;  // 32 KB
+constexpr uint32_t kStageBytes = kABytes + kBBytes;
+constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024;  // + alignment slack
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kWaitStatus = 16u;
+constexpr uint64_t kSpinLimit = 1ull << 24;
+
+__device__ __forceinline__ uint32_t smem(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void mbarInit(uint64_t* b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbarExpect(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbarArrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem(b)) : "memory");
+}
+// True when the phase with parity `parity` has completed; false on timeout.
+__device__ __forceinline__ bool mbarWait(uint64_t* b, uint32_t parity) {
+    const uint32_t addr = smem(b);
+    for (uint64_t spin = 0; spin < kSpinLimit; ++spin) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(addr), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+__device__ __forceinline__ void tmaLoad2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem(bar))
+        : "memory");
+}
+
+// UMMA shared-memory descriptor, 128B swizzle, sm_100 version bits.
+__device__ __forceinline__ uint64_t ummaDesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+    d |= static_cast<uint64_t>(1) << 46;  // descriptor version (sm_100)
+    d |= static_cast<uint64_t>(2) << 61;  // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor: bf16 x bf16 -> f32, dense, M=128, N=256.
+template <bool A_MN, bool B_MN>
+__device__ __forceinline__ constexpr uint32_t instrDesc() {
+    return (1u << 4)                          // D format f32
+           | (1u << 7)                        // A bf16
+           | (1u << 10)                       // B bf16
+           | (static_cast<uint32_t>(A_MN) << 15) | (static_cast<uint32_t>(B_MN) << 16) |
+           (static_cast<uint32_t>(kBN >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mmaCommit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void fenceAfter() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fenceBefore() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmemLoad32(uint32_t addr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(addr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+struct Params {
+    uint32_t m, n, k;
+    uint32_t mTiles, nTiles, kBlocks;
+    void* c;
+    uint64_t ldc;
+    const __nv_bfloat16* aux;
+    uint64_t ldAux;
+    void* c2;  // optional f32 copy of the epilogue result
+    uint32_t* status;
+};
+
+__device__ __forceinline__ void tileCoords(uint32_t tile, const Params& p, uint32_t& mb, uint32_t& nb) {
+    constexpr uint32_t kGroup = 8;  // m-blocks per raster group (L2 reuse of B tiles)
+    const uint32_t perGroup = kGroup * p.nTiles;
+    const uint32_t group = tile / perGroup;
+    const uint32_t first = group * kGroup;
+    const uint32_t size = min(p.mTiles - first, kGroup);
+    const uint32_t local = tile % perGroup;
+    mb = first + local % size;
+    nb = local / size;
+}
+
+template <int EPI>
+__device__ __forceinline__ float epilogueValue(float acc, float aux) {
+    if constexpr (EPI == kEpiReluBf16) return acc > 0.0f ? acc : 0.0f;
+    if constexpr (EPI == kEpiMaskBf16) return aux > 0.0f ? acc : 0.0f;
+    return acc;
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemmKernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, const Params p) {
+    extern __shared__ uint8_t dynamicSmem[];
+    __shared__ __align__(8) uint64_t full[kStages], empty[kStages], tmemFull[2], tmemEmpty[2], mmaDone;
+    __shared__ uint32_t tmemSlot;
+    __shared__ volatile int abortFlag;
+
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dynamicSmem) + 1023) & ~uintptr_t(1023));
+    const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t tiles = p.mTiles * p.nTiles;
+
+    if (threadIdx.x == 0) {
+        abortFlag = 0;
+        for (int s = 0; s < kStages; ++s) {
+            mbarInit(&full[s], 1);
+            mbarInit(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbarInit(&tmemFull[a], 1);
+            mbarInit(&tmemEmpty[a], 128);
+        }
+        mbarInit(&mmaDone, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem(&tmemSlot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    fenceBefore();
+    __syncthreads();
+    fenceAfter();
+    const uint32_t tmemBase = tmemSlot;
+
+    if (warp == 0 && lane == 0) {
+        // ---- TMA producer ----
+        uint32_t stage = 0, phase = 0;
+        uint32_t issuedParity[kStages];
+        uint32_t issued = 0;  // bitmask of stages with a load issued
+        for (uint32_t tile = blockIdx.x; tile < tiles && !abortFlag; tile += gridDim.x) {
+            uint32_t mb, nb;
+            tileCoords(tile, p, mb, nb);
+            for (uint32_t kb = 0; kb < p.kBlocks; ++kb) {
+                if (!mbarWait(&empty[stage], phase ^ 1u)) { abortFlag = 1; break; }
+                uint8_t* a = base + stage * kStageBytes;
+                uint8_t* b = a + kABytes;
+                mbarExpect(&full[stage], kStageBytes);
+                const int32_t k0 = static_cast<int32_t>(kb * kBK);
+                if constexpr (A_MN) {
+                    tmaLoad2d(a, &mapA, static_cast<int32_t>(mb * kBM), k0, &full[stage]);
+                    tmaLoad2d(a + kABytes / 2, &mapA, static_cast<int32_t>(mb * kBM + 64), k0, &full[stage]);
+                } else {
+                    tmaLoad2d(a, &mapA, k0, static_cast<int32_t>(mb * kBM), &full[stage]);
+                }
+                if constexpr (B_MN) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        tmaLoad2d(b + j * (kBBytes / 4), &mapB, static_cast<int32_t>(nb * kBN + 64 * j), k0, &full[stage]);
+                } else {
+                    tmaLoad2d(b, &mapB, k0, static_cast<int32_t>(nb * kBN), &full[stage]);
+                }
+                issuedParity[stage] = phase;
+                issued |= 1u << stage;
+                if (++stage == kStages) { stage = 0; phase ^= 1u; }
+            }
+        }
+        if (abortFlag) {
+            // Let loads already issued land before the CTA can exit.
+            for (int s = 0; s < kStages; ++s)
+                if (issued & (1u << s)) (void)mbarWait(&full[s], issuedParity[s]);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---- MMA issuer ----
+        constexpr uint32_t idesc = instrDesc<A_MN, B_MN>();
+        uint32_t stage = 0, phase = 0, acc = 0, accPhase = 0;
+        for (uint32_t tile = blockIdx.x; tile < tiles && !abortFlag; tile += gridDim.x) {
+            if (!mbarWait(&tmemEmpty[acc], accPhase ^ 1u)) { abortFlag = 1; break; }
+            fenceAfter();
+            const uint32_t d = tmemBase + acc * kBN;
+            bool ok = true;
+            for (uint32_t kb = 0; kb < p.kBlocks; ++kb) {
+                if (!mbarWait(&full[stage], phase)) { abortFlag = 1; ok = false; break; }
+                fenceAfter();
+                const uint32_t a = smem(base + stage * kStageBytes);
+                const uint32_t b = a + kABytes;
+#pragma unroll
+                for (uint32_t ks = 0; ks < kBK / 16; ++ks) {
+                    const uint64_t da = A_MN ? ummaDesc(a + ks * 2048u, kABytes / 2, 1024u) : ummaDesc(a + ks * 32u, 16u, 1024u);
+                    const uint64_t db = B_MN ? ummaDesc(b + ks * 2048u, kBBytes / 4, 1024u) : ummaDesc(b + ks * 32u, 16u, 1024u);
+                    mma(d, da, db, idesc, (kb | ks) != 0 ? 1u : 0u);
+                }
+                mmaCommit(&empty[stage]);
+                if (++stage == kStages) { stage = 0; phase ^= 1u; }
+            }
+            if (!ok) break;
+            mmaCommit(&tmemFull[acc]);
+            if (++acc == 2) { acc = 0; accPhase ^= 1u; }
+        }
+        // All MMAs issued by this thread complete before TMEM is released.
+        mmaCommit(&mmaDone);
+        if (!mbarWait(&mmaDone, 0)) abortFlag = 1;
+    } else if (warp >= 2) {
+        // ---- epilogue ----
+        const uint32_t quadrant = warp % 4;  // TMEM lanes 32*quadrant .. +31
+        const uint32_t row = quadrant * 32 + lane;
+        uint32_t acc = 0, accPhase = 0;
+        for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+            uint32_t mb, nb;
+            tileCoords(tile, p, mb, nb);
+            if (!mbarWait(&tmemFull[acc], accPhase)) abortFlag = 1;
+            if (abortFlag) break;
+            fenceAfter();
+            const uint64_t grow = static_cast<uint64_t>(mb) * kBM + row;
+#pragma unroll 1
+            for (uint32_t chunk = 0; chunk < kBN / 32; ++chunk) {
+                uint32_t r[32];
+                tmemLoad32(tmemBase + ((quadrant * 32u) << 16) + acc * kBN + chunk * 32u, r);
+                const uint64_t col0 = static_cast<uint64_t>(nb) * kBN + chunk * 32u;
+                if (grow >= p.m || col0 >= p.n) continue;
+                const bool full32 = col0 + 32 <= p.n;
+                float aux[32];
+                if constexpr (EPI == kEpiMaskBf16) {
+                    const __nv_bfloat16* src = p.aux + grow * p.ldAux + col0;
+                    if (full32 && (reinterpret_cast<uintptr_t>(src) % 16 == 0)) {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const uint4 v = *reinterpret_cast<const uint4*>(src + q * 8);
+                            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const float2 f = __bfloat1622float2(h[e]);
+                                aux[q * 8 + 2 * e] = f.x;
+                                aux[q * 8 + 2 * e + 1] = f.y;
+                            }
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) aux[j] = col0 + j < p.n ? __bfloat162float(src[j]) : 0.0f;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) aux[j] = 0.0f;
+                }
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = epilogueValue<EPI>(__uint_as_float(r[j]), aux[j]);
+                if constexpr (EPI == kEpiF32) {
+                    float* dst = static_cast<float*>(p.c) + grow * p.ldc + col0;
+                    if (full32 && reinterpret_cast<uintptr_t>(dst) % 16 == 0) {
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            *reinterpret_cast<float4*>(dst + 4 * q) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                    } else {
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < p.n) dst[j] = v[j];
+                    }
+                } else {
+                    __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.c) + grow * p.ldc + col0;
+                    if (full32 && reinterpret_cast<uintptr_t>(dst) % 16 == 0) {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            uint4 packed;
+                            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&packed);
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
+                            *reinterpret_cast<uint4*>(dst + q * 8) = packed;
+                        }
+                    } else {
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < p.n) dst[j] = __float2bfloat16_rn(v[j]);
+                    }
+                    if (p.c2) {
+                        float* dst2 = static_cast<float*>(p.c2) + grow * p.ldc + col0;
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < p.n) dst2[j] = v[j];
+                    }
+                }
+            }
+            fenceBefore();
+            mbarArrive(&tmemEmpty[acc]);
+            if (++acc == 2) { acc = 0; accPhase ^= 1u; }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && abortFlag) atomicOr(p.status, kWaitStatus);
+    if (warp == 1) {
+        fenceAfter();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmemBase), "r"(kTmemCols) : "memory");
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encodeFn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [outer][inner] matrix with leading
+// dimension `ld` elements; box = 64 inner elements (one 128 B swizzle row)
+// by `boxOuter` rows.
+bool makeMap(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t boxOuter) {
+    auto fn = encodeFn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {ld * 2};
+    cuuint32_t box[2] = {64, boxOuter};
+    cuuint32_t elem[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, elem,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+cudaError_t launchTyped(const CUtensorMap& a, const CUtensorMap& b, const Params& p, int smCount, cudaStream_t stream) {
+    auto kernel = gemmKernel<A_MN, B_MN, EPI>;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    const uint32_t tiles = p.mTiles * p.nTiles;
+    const uint32_t grid = tiles < static_cast<uint32_t>(smCount) ? tiles : static_cast<uint32_t>(smCount);
+    kernel<<<grid, kThreads, kSmemBytes, stream>>>(a, b, p);
+    return cudaGetLastError();
+}
+
+template <bool A_MN, bool B_MN>
+cudaError_t launchEpi(int epi, const CUtensorMap& a, const CUtensorMap& b, const Params& p, int sm, cudaStream_t s) {
+    switch (epi) {
+    case kEpiF32: return launchTyped<A_MN, B_MN, kEpiF32>(a, b, p, sm, s);
+    case kEpiBf16: return launchTyped<A_MN, B_MN, kEpiBf16>(a, b, p, sm, s);
+    case kEpiReluBf16: return launchTyped<A_MN, B_MN, kEpiReluBf16>(a, b, p, sm, s);
+    case kEpiMaskBf16: return launchTyped<A_MN, B_MN, kEpiMaskBf16>(a, b, p, sm, s);
+    }
+    return cudaErrorInvalidValue;
+}
+
+} // namespace
+
+const char* validate(const Problem& q) {
+    if (q.m == 0 || q.n == 0 || q.k == 0) return "GEMM extents must be positive";
+    if (q.m > (1u << 30) || q.n > (1u << 30) || q.k > (1u << 30)) return "GEMM extent too large";
+    if (!q.a || !q.b || !q.c) return "GEMM operand pointer is null";
+    if (q.lda % 8 || q.ldb % 8) return "operand leading dimensions must be multiples of 8 elements (16 bytes)";
+    if ((reinterpret_cast<uintptr_t>(q.a) | reinterpret_cast<uintptr_t>(q.b)) % 16) return "operands must be 16-byte aligned";
+    if (q.lda < (q.aMajorMN ? q.m : q.k) || q.ldb < (q.bMajorMN ? q.n : q.k)) return "leading dimension too small";
+    if (q.ldc < q.n) return "ldc smaller than N";
+    if (q.epilogue == kEpiMaskBf16 && (!q.aux || q.ldAux < q.n)) return "mask epilogue needs an auxiliary bf16 matrix";
+    if (q.epilogue < kEpiF32 || q.epilogue > kEpiMaskBf16) return "unknown epilogue";
+    return nullptr;
+}
+
+cudaError_t run(const Problem& q, int smCount, uint32_t* status, cudaStream_t stream) {
+    CUtensorMap a, b;
+    const bool okA = q.aMajorMN ? makeMap(&a, q.a, q.m, q.k, q.lda, 64) : makeMap(&a, q.a, q.k, q.m, q.lda, kBM);
+    const bool okB = q.bMajorMN ? makeMap(&b, q.b, q.n, q.k, q.ldb, 64) : makeMap(&b, q.b, q.k, q.n, q.ldb, kBN);
+    if (!okA || !okB) return cudaErrorInvalidValue;
+    Params p{};
+    p.m = static_cast<uint32_t>(q.m);
+    p.n = static_cast<uint32_t>(q.n);
+    p.k = static_cast<uint32_t>(q.k);
+    p.mTiles = static_cast<uint32_t>((q.m + kBM - 1) / kBM);
+    p.nTiles = static_cast<uint32_t>((q.n + kBN - 1) / kBN);
+    p.kBlocks = static_cast<uint32_t>((q.k + kBK - 1) / kBK);
+    p.c = q.c;
+    p.ldc = q.ldc;
+    p.aux = static_cast<const __nv_bfloat16*>(q.aux);
+    p.ldAux = q.ldAux;
+    p.c2 = q.c2;
+    p.status = status;
+    if (q.aMajorMN) {
+        if (q.bMajorMN) return launchEpi<true, true>(q.epilogue, a, b, p, smCount, stream);
+        return launchEpi<true, false>(q.epilogue, a, b, p, smCount, stream);
+    }
+    if (q.bMajorMN) return launchEpi<false, true>(q.epilogue, a, b, p, smCount, stream);
+    return launchEpi<false, false>(q.epilogue, a, b, p, smCount, stream);
+}
+
+} // namespace thb::gemm

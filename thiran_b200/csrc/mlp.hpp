@@ -1,0 +1,56 @@
+// Two-layer MLP training step (see mlp.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace thb::mlp {
+
+// Device buffers of one training session (all owned by the session).
+struct Buffers {
+    std::uint64_t batch = 0, globalBatch = 0, in = 0, hidden = 0, out = 0;
+    float* w1 = nullptr;       // f32 [in][hidden]
+    float* w2 = nullptr;       // f32 [hidden][out]
+    void* w1b = nullptr;       // bf16 copies
+    void* w2b = nullptr;
+    void* xb = nullptr;        // bf16 [batch][in]
+    void* h = nullptr;         // bf16 [batch][hidden]
+    float* y = nullptr;        // f32 [batch][out]
+    void* dy = nullptr;        // bf16 [batch][out]
+    void* dh = nullptr;        // bf16 [batch][hidden]
+    float* dw1 = nullptr;      // f32 [in][hidden]
+    float* dw2 = nullptr;      // f32 [hidden][out]
+    double* lossPartials = nullptr;
+    double* lossSum = nullptr; // sum over this rank's batch of (Y - T)^2
+};
+
+// Optional CUDA-event timing of the GEMM launches of a step (recorded on the
+// launching stream).
+struct GemmTimer {
+    bool enabled = false;
+    std::uint64_t launches = 0;
+    cudaEvent_t events[2 * 512] = {};
+    unsigned used = 0;  // events recorded since the last read
+    void begin(cudaStream_t s) {
+        if (enabled && used + 2 <= sizeof(events) / sizeof(events[0])) cudaEventRecord(events[used], s);
+    }
+    void end(cudaStream_t s) {
+        if (enabled && used + 2 <= sizeof(events) / sizeof(events[0])) {
+            cudaEventRecord(events[used + 1], s);
+            used += 2;
+            ++launches;
+        }
+    }
+};
+
+unsigned lossPartialCount(int smCount);
+cudaError_t castToBf16(const float* x, void* y, std::uint64_t n, int smCount, cudaStream_t s);
+cudaError_t sgdUpdate(float* w, const float* g, void* wb, std::uint64_t n, float lr, int smCount, cudaStream_t s);
+// Forward, loss and backward: fills h, y, dy, dh, dw1, dw2 and lossSum.
+cudaError_t forwardBackward(const Buffers&, const float* x, const float* t, int smCount, std::uint32_t* status,
+                            cudaStream_t s, GemmTimer* timer = nullptr);
+// W -= lr * dW for both layers, refreshing the bf16 copies.
+cudaError_t applySgd(const Buffers&, float lr, int smCount, cudaStream_t s);
+
+} // namespace thb::mlp

@@ -26,7 +26,7 @@ constexpr unsigned kRowThreads = 256;
 constexpr unsigned kRowWarps = kRowThreads / 32;
 constexpr unsigned kStages = 4;
 constexpr unsigned kWaitStatus = 16u;            // status bit raised on a wait timeout
-constexpr std::uint64_t kSpinLimit = 1ull << 26; // bounded mbarrier polling
+constexpr std::uint64_t kSpinLimit = 1ull << 22; // bounded mbarrier polling (~seconds at most)
 
 enum class RowOp { Softmax, Max, Sum };
 

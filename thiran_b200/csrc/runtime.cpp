@@ -95,6 +95,27 @@ const DeviceInfo& useDevice(int ordinal) {
     return found->second;
 }
 
+std::uint32_t* deviceStatus(int ordinal) {
+    static std::mutex statusMutex;
+    static std::map<int, std::unique_ptr<DeviceBuffer>> words;
+    useDevice(ordinal);
+    std::lock_guard<std::mutex> lock(statusMutex);
+    auto& word = words[ordinal];
+    if (!word) {
+        word = std::make_unique<DeviceBuffer>();
+        word->reserve(sizeof(std::uint32_t), ordinal);
+        check(cudaMemset(word->ptr, 0, word->bytes), "cudaMemset(status)");
+    }
+    return static_cast<std::uint32_t*>(word->ptr);
+}
+
+std::string statusText(std::uint32_t word) {
+    if (word & 16u) return "GPU-KERNEL-TIMEOUT";
+    if (word & 1u) return "TH-SPEC-I64-OVERFLOW";
+    if (word & 2u) return "TH021-DIVIDE-BY-ZERO";
+    return "GPU-KERNEL-STATUS";
+}
+
 void recordUnobserved(const std::string& id) {
     std::lock_guard<std::mutex> lock(unobservedMutex);
     unobservedErrors.push_back(id);
@@ -158,9 +179,7 @@ std::string CompiledRegion::firstFailure(const std::uint32_t* words) const {
         // Group error codes: bit 0 = checked i64 overflow, bit 1 = recipe
         // divide by zero (the reference's error words 1 and 2,
         // src/backend/v0/NativeGpu.cpp:1123-1125).
-        if (words[g] & 1u) return "TH-SPEC-I64-OVERFLOW";
-        if (words[g] & 2u) return "TH021-DIVIDE-BY-ZERO";
-        return "GPU-KERNEL-STATUS";
+        return statusText(words[g]);
     }
     return {};
 }
@@ -366,7 +385,14 @@ Value CompiledRegion::run(const std::vector<Value>& inputs, cudaStream_t stream,
         Value v = shapes.at(n.id);
         switch (n.op) {
         case Op::Integer: case Op::Float: break;
-        case Op::Alias: v = values.at(region_.canonical(n.dependencies.at(0))); break;
+        case Op::Alias: {
+            // An alias of a fused intermediate names a value that is never
+            // materialized (src/backend/v0/NativeGpu.cpp:984-988 skips it the same way).
+            auto found = values.find(region_.canonical(n.dependencies.at(0)));
+            if (found == values.end()) continue;
+            v = found->second;
+            break;
+        }
         case Op::TensorLiteral: {
             v.data = slotPointer(n.id, v.bytes(), ev);
             bool device = false;
@@ -430,7 +456,9 @@ Value CompiledRegion::run(const std::vector<Value>& inputs, cudaStream_t stream,
         default: {
             const FusionGroup* group = plan_.groupFor(n.id);
             if (!group) fail(Category::Unsupported, "GPU-INVALID-PLAN", "kernel node outside every group");
-            if (group->nodes.front() != n.id || !launched.insert(group->id).second) break;
+            // Only the group's first node launches; the others (fused
+            // intermediates and the terminal) are produced by that launch.
+            if (group->nodes.front() != n.id || !launched.insert(group->id).second) continue;
             const Value& shape = shapes.at(group->output);
             Value out = shape;
             if (out.rank == 0) {  // scalar reduction result lives in a device scalar buffer

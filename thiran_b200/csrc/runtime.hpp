@@ -58,6 +58,12 @@ struct DeviceInfo {
 // GPU-DRIVER-NOT-FOUND / GPU-INVALID-DEVICE.
 const DeviceInfo& useDevice(int ordinal);
 
+// Per-device 32-bit status word latched by kernels launched outside a
+// region (bit 4 = a bounded wait expired). Allocated zeroed on first use.
+std::uint32_t* deviceStatus(int ordinal);
+// Text of a nonzero status word.
+std::string statusText(std::uint32_t word);
+
 // A runtime value during one execution.
 struct Value {
     bool tensor = false;
