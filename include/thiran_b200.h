@@ -406,6 +406,26 @@ int thb_region_describe(const thb_region_desc* region, thb_plan_options options,
                         char* buffer, uint64_t capacity, uint64_t* needed, uint64_t* counts,
                         char* failure, uint64_t failure_cap);
 
+/* ---- full-tensor sum without allocation --------------------------------
+ * No counterpart in the reference. For callers that cannot allocate device
+ * memory: hosts that own all device memory through their own allocator and
+ * do not let a component call cudaMalloc / cudaFree (which can synchronise
+ * the device and fragment the host's pool). The caller passes x (n f32
+ * values on `device`) and at least one output (device pointers: *out_f32 the
+ * f32 rounding, *out_f64 the f64 total). The block partials live in a fixed
+ * scratch array inside the library — 4096 f64 values (32 KiB) that every GPU
+ * loading the library holds until exit; a reduction needing more partials
+ * than that is rejected with GPU-NOALLOC-SIZE (on a B200 the sum uses at most
+ * 4 x 148 = 592). Nothing is allocated: the first call on a device resolves
+ * the scratch's device address once (make that first call before any stream
+ * capture). Every call shares the one scratch array, and each call writes
+ * every partial it later reads, so nothing needs clearing; calls that overlap
+ * on the GPU (different streams, or different host threads on one device)
+ * race on the scratch and must be serialised by the caller. Results are
+ * identical to the region Sum path (same kernels, same grid). */
+int thb_sum_all_f32_noalloc(int device, const float* x, uint64_t n, float* out_f32, double* out_f64,
+                            void* stream, char* failure, uint64_t failure_cap);
+
 #ifdef __cplusplus
 }
 #endif

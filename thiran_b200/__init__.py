@@ -165,6 +165,8 @@ SIGNATURES = {
     "thb_mlp_bind": (C.c_int, [C.c_void_p, C.c_uint32, C.c_void_p]),
     "thb_mlp_enable_timing": (C.c_int, [C.c_void_p, C.c_int]),
     "thb_mlp_read_timing": (C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
+    "thb_sum_all_f32_noalloc": (C.c_int, [C.c_int, C.c_void_p, C.c_uint64, C.c_void_p, C.c_void_p, C.c_void_p,
+                                          C.c_char_p, C.c_uint64]),
 }
 
 MLP_W1, MLP_W2, MLP_DW1, MLP_DW2, MLP_Y, MLP_H, MLP_LOSS_SUM = range(7)
