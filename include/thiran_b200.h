@@ -65,7 +65,23 @@ enum {
     THB_OP_SUM = 32,     /* sum(A, axis): Evaluator.cpp:214-251; axis in node.axis */
     THB_OP_ROW_MAX = 33, /* max over the last axis */
     THB_OP_SOFTMAX = 34, /* softmax over the last axis (RegionPythonEmitter.cpp:293-294) */
-    THB_OP_RELU = 35     /* max(x, 0) (PythonExecutorEmitter.cpp:94) */
+    THB_OP_RELU = 35,    /* max(x, 0) (PythonExecutorEmitter.cpp:94) */
+    /* Reverse-AD operations the reference emits into backward functions and
+     * evaluates only in its Evaluator (src/autodiff/v0/Autodiff.cpp:195-294):
+     *   EXTENSION_GRADIENT: deps = primal operands..., primal result, output
+     *     cotangent; axis = operand index k; evaluates the descriptor's
+     *     gradient recipe k elementwise (Autodiff.cpp:231-270);
+     *   TRANSPOSE (Evaluator.cpp:200-213); MATMUL (Evaluator.cpp:125-154),
+     *     f32 operands computed as bf16 x bf16 -> f32 on the tensor cores;
+     *   BROADCAST_TO_SHAPE: deps = value, reference; axis (Evaluator.cpp:278-309);
+     *   REDUCE_TO_SHAPE: deps = value, reference (Evaluator.cpp:258-277);
+     *   ZERO_LIKE: deps = reference. */
+    THB_OP_EXTENSION_GRADIENT = 36,
+    THB_OP_TRANSPOSE = 37,
+    THB_OP_MATMUL = 38,
+    THB_OP_BROADCAST_TO_SHAPE = 39,
+    THB_OP_REDUCE_TO_SHAPE = 40,
+    THB_OP_ZERO_LIKE = 41
 };
 
 /* Scalar recipe opcodes (include/extension/v0/Extension.hpp:16-17). */

@@ -226,7 +226,15 @@ double orc_mlp_step(const float* x, const float* t, float* w1, float* w2, uint64
 
 static int elementwise_op(uint32_t op) {
     return op == THB_OP_NEGATE || op == THB_OP_ADD || op == THB_OP_SUBTRACT || op == THB_OP_ELEMENT_MULTIPLY ||
-           op == THB_OP_EXTENSION || op == THB_OP_RELU;
+           op == THB_OP_EXTENSION || op == THB_OP_RELU || op == THB_OP_EXTENSION_GRADIENT;
+}
+
+/* The recipe an Extension / ExtensionGradient node evaluates: the forward
+ * recipe, or gradient recipe `axis` over (primals..., result, cotangent)
+ * (src/autodiff/v0/Autodiff.cpp:231-270). */
+static const thb_scalar_recipe* node_recipe(const thb_region_node* n) {
+    if (n->op == THB_OP_EXTENSION) return &n->extension->forward;
+    return &n->extension->derivative->gradients[n->axis];
 }
 
 int orc_region_eval(const thb_region_desc* r, const thb_abi_arg* args, uint64_t argc, void* output,
@@ -305,6 +313,81 @@ int orc_region_eval(const thb_region_desc* r, const thb_abi_arg* args, uint64_t 
             }
             break;
         }
+        case THB_OP_TRANSPOSE: {
+            /* Evaluator.cpp:200-213 */
+            const size_t w = n->dtype == THB_DTYPE_I64 ? 8 : 4;
+            v->shape[0] = d0->shape[1];
+            v->shape[1] = d0->shape[0];
+            v->count = d0->count;
+            v->data = malloc(w * (v->count ? v->count : 1));
+            v->owned = 1;
+            for (uint64_t i = 0; i < d0->shape[0]; ++i)
+                for (uint64_t j = 0; j < d0->shape[1]; ++j)
+                    memcpy((char*)v->data + (j * d0->shape[0] + i) * w, (const char*)d0->data + (i * d0->shape[1] + j) * w, w);
+            break;
+        }
+        case THB_OP_MATMUL: {
+            /* Evaluator.cpp:125-154: sequential-k f32, each op rounded */
+            const value_t* d1 = &vals[position_of(r, n->dependencies[1])];
+            v->shape[0] = d0->shape[0];
+            v->shape[1] = d1->shape[1];
+            v->count = v->shape[0] * v->shape[1];
+            v->data = malloc(4 * (v->count ? v->count : 1));
+            v->owned = 1;
+            orc_matmul_f32((const float*)d0->data, (const float*)d1->data, (float*)v->data, d0->shape[0], d0->shape[1],
+                           d1->shape[1]);
+            break;
+        }
+        case THB_OP_BROADCAST_TO_SHAPE: {
+            /* Evaluator.cpp:278-309: target = reference shape, source = target without `axis` */
+            const value_t* ref = &vals[position_of(r, n->dependencies[1])];
+            v->shape[0] = ref->shape[0];
+            v->shape[1] = ref->shape[1];
+            v->count = ref->count;
+            v->data = malloc(4 * (v->count ? v->count : 1));
+            v->owned = 1;
+            for (uint64_t k = 0; k < v->count; ++k) {
+                float x;
+                if (!d0->tensor) x = d0->f;
+                else if (ref->rank == 2) x = ((const float*)d0->data)[n->axis == 0 ? k % ref->shape[1] : k / ref->shape[1]];
+                else x = ((const float*)d0->data)[0];
+                ((float*)v->data)[k] = x;
+            }
+            break;
+        }
+        case THB_OP_REDUCE_TO_SHAPE: {
+            /* Evaluator.cpp:258-277: sequential f32 accumulation in source order */
+            const value_t* ref = &vals[position_of(r, n->dependencies[1])];
+            if (!ref->tensor) {
+                float acc = 0.0f;
+                for (uint64_t k = 0; k < d0->count; ++k) acc = acc + ((const float*)d0->data)[k];
+                v->f = acc;
+                v->tensor = 0;
+                break;
+            }
+            v->shape[0] = ref->shape[0];
+            v->shape[1] = ref->shape[1];
+            v->count = ref->count;
+            v->data = calloc(v->count ? v->count : 1, 4);
+            v->owned = 1;
+            const uint32_t delta = d0->rank - ref->rank;
+            for (uint64_t k = 0; k < d0->count; ++k) {
+                uint64_t sc[2] = {0, 0}, tc[2] = {0, 0};
+                if (d0->rank == 2) { sc[0] = k / d0->shape[1]; sc[1] = k % d0->shape[1]; }
+                else sc[0] = k;
+                for (uint32_t d = 0; d < ref->rank; ++d) tc[d] = ref->shape[d] == 1 ? 0 : sc[d + delta];
+                const uint64_t t = ref->rank == 2 ? tc[0] * ref->shape[1] + tc[1] : tc[0];
+                ((float*)v->data)[t] = ((float*)v->data)[t] + ((const float*)d0->data)[k];
+            }
+            break;
+        }
+        case THB_OP_ZERO_LIKE:
+            v->shape[0] = d0->shape[0];
+            v->shape[1] = d0->shape[1];
+            v->count = d0->count;
+            v->data = calloc(v->count ? v->count : 1, 4);
+            v->owned = 1;
+            break;
         case THB_OP_SOFTMAX: case THB_OP_ROW_MAX: case THB_OP_SUM: {
             const uint64_t rows = d0->rank == 2 ? d0->shape[0] : 1;
             const uint64_t cols = d0->rank == 2 ? d0->shape[1] : d0->shape[0];
@@ -349,11 +432,11 @@ int orc_region_eval(const thb_region_desc* r, const thb_abi_arg* args, uint64_t 
                 } else {
                     const float a = ((const float*)d0->data)[k];
                     float out = 0.0f;
-                    if (n->op == THB_OP_EXTENSION) {
-                        float in[8];
-                        for (uint32_t j = 0; j < n->dependency_count && j < 8; ++j)
+                    if (n->op == THB_OP_EXTENSION || n->op == THB_OP_EXTENSION_GRADIENT) {
+                        float in[10];
+                        for (uint32_t j = 0; j < n->dependency_count && j < 10; ++j)
                             in[j] = ((const float*)vals[position_of(r, n->dependencies[j])].data)[k];
-                        const int rs = orc_recipe_eval(&n->extension->forward, in, &out);
+                        const int rs = orc_recipe_eval(node_recipe(n), in, &out);
                         if (rs == 2) {
                             set_failure(failure, cap, "TH021-DIVIDE-BY-ZERO");
                             status = 2;

@@ -18,6 +18,7 @@
 //
 // Tensor files: "THB1", u32 dtype (1 i64, 2 f32), u32 rank, u64 shape[rank],
 // little-endian elements; rank 0 is a scalar.
+#include "autodiff/v0/Autodiff.hpp"
 #include "backend/v0/NativeCpu.hpp"
 #include "backend/v0/PhysicalPlan.hpp"
 #include "extension/v0/Extension.hpp"
@@ -27,6 +28,7 @@
 #include "semantic/v0/Verifier.hpp"
 
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <iostream>
@@ -54,16 +56,47 @@ constexpr e::ScalarNodeV0 chainNodes[] = {
     {e::ScalarOpcode::Multiply, 6, 7, 0, 0.0f},    // 8 *0.5
     {e::ScalarOpcode::Add, 8, 0, 0, 0.0f},         // 9 +x
 };
+// d/dx of the chain, over (x, y, dz): dz * ((((x*1.5 + 0.25) + x*1.5) - 1) * 0.5 + 1)
+constexpr e::ScalarNodeV0 chainGradientNodes[] = {
+    {e::ScalarOpcode::Input, 0, 0, 0, 0.0f},        // 0 x
+    {e::ScalarOpcode::ConstantF32, 0, 0, 0, 1.5f},  // 1
+    {e::ScalarOpcode::Multiply, 0, 1, 0, 0.0f},     // 2 x*1.5
+    {e::ScalarOpcode::ConstantF32, 0, 0, 0, 0.25f}, // 3
+    {e::ScalarOpcode::Add, 2, 3, 0, 0.0f},          // 4 x*1.5+0.25
+    {e::ScalarOpcode::Add, 4, 2, 0, 0.0f},          // 5 + x*1.5
+    {e::ScalarOpcode::ConstantF32, 0, 0, 0, 1.0f},  // 6
+    {e::ScalarOpcode::Subtract, 5, 6, 0, 0.0f},     // 7 - 1
+    {e::ScalarOpcode::ConstantF32, 0, 0, 0, 0.5f},  // 8
+    {e::ScalarOpcode::Multiply, 7, 8, 0, 0.0f},     // 9 * 0.5
+    {e::ScalarOpcode::Add, 9, 6, 0, 0.0f},          // 10 + 1
+    {e::ScalarOpcode::Input, 0, 0, 2, 0.0f},        // 11 dz
+    {e::ScalarOpcode::Multiply, 11, 10, 0, 0.0f},   // 12 dz * (...)
+};
+constexpr e::ScalarRecipeV0 chainGradients[] = {{chainGradientNodes, 13, 12, 3}};
+constexpr e::DerivativeV0 chainDerivative{1, 1, false, chainGradients, 1};
 constexpr e::ScalarNodeV0 squareLinearNodes[] = {
     {e::ScalarOpcode::Input, 0, 0, 0, 0.0f},
     {e::ScalarOpcode::Multiply, 0, 0, 0, 0.0f},
     {e::ScalarOpcode::Add, 1, 0, 0, 0.0f},
 };
+// The example extension's gradient (examples/research_extension): dz * (2x + 1).
+constexpr e::ScalarNodeV0 squareLinearGradientNodes[] = {
+    {e::ScalarOpcode::Input, 0, 0, 2, 0.0f},
+    {e::ScalarOpcode::ConstantF32, 0, 0, 0, 2.0f},
+    {e::ScalarOpcode::Input, 0, 0, 0, 0.0f},
+    {e::ScalarOpcode::Multiply, 1, 2, 0, 0.0f},
+    {e::ScalarOpcode::ConstantF32, 0, 0, 0, 1.0f},
+    {e::ScalarOpcode::Add, 3, 4, 0, 0.0f},
+    {e::ScalarOpcode::Multiply, 0, 5, 0, 0.0f},
+};
+constexpr e::ScalarRecipeV0 squareLinearGradients[] = {{squareLinearGradientNodes, 7, 6, 3}};
+constexpr e::DerivativeV0 squareLinearDerivative{1, 1, false, squareLinearGradients, 1};
 constexpr e::OperationDescriptorV0 operations[] = {
     {"research_chain", "1.0.0", 1, 1, 2, 0, true, e::EffectV0::Pure,
-     e::BackendV0::Reference | e::BackendV0::Cpu | e::BackendV0::Gpu, true, {chainNodes, 10, 9, 1}, nullptr},
+     e::BackendV0::Reference | e::BackendV0::Cpu | e::BackendV0::Gpu, true, {chainNodes, 10, 9, 1}, &chainDerivative},
     {"research_square_linear", "1.0.0", 1, 1, 2, 0, true, e::EffectV0::Pure,
-     e::BackendV0::Reference | e::BackendV0::Cpu | e::BackendV0::Gpu, true, {squareLinearNodes, 3, 2, 1}, nullptr},
+     e::BackendV0::Reference | e::BackendV0::Cpu | e::BackendV0::Gpu, true, {squareLinearNodes, 3, 2, 1},
+     &squareLinearDerivative},
 };
 constexpr e::ExtensionDescriptorV0 descriptor{e::extensionAbiVersion, "org.thiran.b200.oracle", "1.0.0", operations, 2,
                                              nullptr};
@@ -226,6 +259,44 @@ int main(int argc, char** argv) {
             const auto region = extract(module, function);
             std::ofstream out(argv[4]);
             out << b::emitCpp20(region, false, wrapper(region));
+            return 0;
+        }
+        if (mode == "vjp") {
+            // ref_driver vjp <program> <fn> <out-prefix> <cotangent.bin> <inputs...>
+            // Reverse mode over every parameter (autodiff::differentiate,
+            // src/autodiff/v0/Autodiff.cpp:72-294) executed by
+            // executeVjpWithPrimal (:379-393); writes <prefix>primal.bin and
+            // <prefix>grad<k>.bin.
+            if (argc < 6) throw std::runtime_error("vjp needs an output prefix and a cotangent");
+            const auto facts = analysis::analyze(module);
+            if (!facts.ok()) throw std::runtime_error("ownership analysis failed");
+            const s::Function* fn = nullptr;
+            for (const auto& candidate : module.functions)
+                if (candidate.name == function) fn = &candidate;
+            if (!fn) throw std::runtime_error("no function " + function);
+            thiran::v0::autodiff::ReverseModeRequest request;
+            request.function = fn->id;
+            for (std::size_t k = 0; k < fn->parameters.size(); ++k) request.wrtParameters.push_back(k);
+            const auto diff = thiran::v0::autodiff::differentiate(module, facts, request);
+            if (!diff.ok())
+                throw std::runtime_error("differentiate: " +
+                                         (diff.diagnostics.empty() ? std::string("failed") : diff.diagnostics.front().code));
+            if (std::getenv("THB_DUMP_BACKWARD")) std::cerr << diff.dump() << s::dump(*diff.module);
+            std::vector<s::RuntimeValue> inputs;
+            for (int k = 6; k < argc; ++k) inputs.push_back(readValue(argv[k]));
+            const auto result = thiran::v0::autodiff::executeVjpWithPrimal(diff, inputs, readValue(argv[5]));
+            if (!result.ok()) {
+                std::cout << "{\"status\":\"error\",\"error_id\":\"" << result.errorId << "\"}\n";
+                return 0;
+            }
+            const std::string prefix = argv[4];
+            writeValue(prefix + "primal.bin", *result.primal);
+            if (const auto* tuple = std::get_if<s::RuntimeTuple>(&result.gradients->data)) {
+                for (std::size_t k = 0; k < tuple->size(); ++k) writeValue(prefix + "grad" + std::to_string(k) + ".bin", (*tuple)[k]);
+            } else {
+                writeValue(prefix + "grad0.bin", *result.gradients);
+            }
+            std::cout << "{\"status\":\"ok\"}\n";
             return 0;
         }
         if (mode == "plan") {

@@ -65,6 +65,27 @@ def evaluate(program: str, function: str, inputs):
         return "ok", read_thb(out)
 
 
+def vjp(program: str, function: str, cotangent, inputs, gradients: int):
+    """Runs the reference's reverse mode (autodiff::differentiate +
+    executeVjpWithPrimal); returns (primal, [gradient per parameter])."""
+    with tempfile.TemporaryDirectory() as tmp:
+        src = os.path.join(tmp, "p.th")
+        with open(src, "w") as f:
+            f.write(program)
+        paths = []
+        for k, v in enumerate(inputs):
+            p = os.path.join(tmp, f"in{k}.bin")
+            write_thb(p, v)
+            paths.append(p)
+        ct = os.path.join(tmp, "ct.bin")
+        write_thb(ct, cotangent)
+        prefix = os.path.join(tmp, "out_")
+        res = subprocess.run([DRIVER, "vjp", src, function, prefix, ct] + paths, capture_output=True, text=True,
+                             check=True)
+        assert json.loads(res.stdout.strip().splitlines()[-1])["status"] == "ok", res.stdout
+        return read_thb(prefix + "primal.bin"), [read_thb(prefix + f"grad{k}.bin") for k in range(gradients)]
+
+
 def plan(program: str, function: str, fusion=True):
     with tempfile.TemporaryDirectory() as tmp:
         src = os.path.join(tmp, "p.th")
@@ -129,6 +150,13 @@ fn cols(A: Tensor<f32,2>) -> Tensor<f32,1> { return sum(A, 0) }
 fn total(A: Tensor<f32,2>) -> f32 { return sum(sum(A, 1), 0) }
 """
 MATMUL = "fn mm(A: Tensor<f32,2>, B: Tensor<f32,2>) -> Tensor<f32,2> { return A * B }"
+LINEAR_LOSS = """fn loss(x: Tensor<f32,2>, w1: Tensor<f32,2>, w2: Tensor<f32,2>, t: Tensor<f32,2>) -> f32 {
+let h = x * w1
+let y = h * w2
+let e = y - t
+let s = e .* e
+return sum(sum(s, 1), 0)
+}"""
 
 
 def main():
@@ -211,6 +239,24 @@ def main():
     mb = rng.standard_normal((32, 24)).astype(np.float32)
     status, value = evaluate(MATMUL, "mm", [ma, mb])
     arrays["mm_a"], arrays["mm_b"], arrays["mm_out"] = ma, mb, value
+
+    # Reverse mode (src/autodiff/v0/Autodiff.cpp): extension gradient recipes
+    # and the matmul / sum / broadcast rules of a linear two-layer loss.
+    rng = np.random.default_rng(6)
+    dz = rng.uniform(-2, 2, 7).astype(np.float32)
+    _, (g,) = vjp(SQUARE_LINEAR, "f", dz, [xs], 1)
+    arrays["ad_square_linear_dz"], arrays["ad_square_linear_grad"] = dz, g
+    cx = rng.uniform(-1, 1, 4096).astype(np.float32)
+    cdz = rng.uniform(-1, 1, 4096).astype(np.float32)
+    _, (g,) = vjp(CHAIN, "f", cdz, [cx], 1)
+    arrays["ad_chain_x"], arrays["ad_chain_dz"], arrays["ad_chain_grad"] = cx, cdz, g
+    lx = rng.standard_normal((16, 32)).astype(np.float32)
+    lw1 = (rng.standard_normal((32, 64)) * 0.2).astype(np.float32)
+    lw2 = (rng.standard_normal((64, 32)) * 0.2).astype(np.float32)
+    lt = rng.standard_normal((16, 32)).astype(np.float32)
+    loss, (gx, gw1, gw2, gt) = vjp(LINEAR_LOSS, "loss", np.float32(1.0), [lx, lw1, lw2, lt], 4)
+    arrays.update(ad_lin_x=lx, ad_lin_w1=lw1, ad_lin_w2=lw2, ad_lin_t=lt, ad_lin_loss=np.float32(loss),
+                  ad_lin_dx=gx, ad_lin_dw1=gw1, ad_lin_dw2=gw2, ad_lin_dt=gt)
 
     np.savez_compressed(os.path.join(HERE, "reference_outputs.npz"), **arrays)
     with open(os.path.join(HERE, "reference_fixtures.json"), "w") as f:

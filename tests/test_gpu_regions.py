@@ -232,6 +232,44 @@ def test_i64_region_8192_exact(device):
     np.testing.assert_array_equal(out, orc.region_eval(spec, [a, b]))
 
 
+def pinned(torch, array):
+    t = torch.from_numpy(array).pin_memory()
+    return t, t.numpy()
+
+
+def test_pipelined_host_execution(device):
+    """Large row-local regions over pinned host buffers run chunk by chunk on
+    three streams; results and checked failures are unchanged."""
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(21)
+    spec = regions.i64_region()
+    region = spec.compile(device)
+    _, a = pinned(torch, rng.integers(-1000, 1001, (2048, 8192), dtype=np.int64))
+    _, b = pinned(torch, rng.integers(-1000, 1001, (2048, 8192), dtype=np.int64))
+    _, out = pinned(torch, np.empty((2048, 8192), np.int64))
+    region.execute([a, b], out=out)
+    assert region.evidence["host_to_device_copies"] > 2  # chunked
+    np.testing.assert_array_equal(out, orc.region_eval(spec, [a, b]))
+    a[-1, -1], b[-1, -1] = 2**62, 2**62  # overflow in the last chunk only
+    with pytest.raises(thb.GpuError) as err:
+        region.execute([a, b], out=out)
+    assert err.value.code == "TH-SPEC-I64-OVERFLOW"
+    # Pageable buffers take the unchunked path with the same result.
+    a[-1, -1], b[-1, -1] = 1, 1
+    np.testing.assert_array_equal(region.execute([a.copy(), b.copy()]), orc.region_eval(spec, [a, b]))
+
+
+def test_pipelined_softmax_rows(device):
+    torch = pytest.importorskip("torch")
+    _, x = pinned(torch, np.random.default_rng(22).standard_normal((8192, 4096)).astype(np.float32))
+    _, out = pinned(torch, np.empty((8192, 4096), np.float32))
+    region = regions.softmax_rows().compile(device)
+    region.execute([x], out=out)
+    assert region.evidence["host_to_device_copies"] > 1
+    ref = orc.softmax_rows(x)
+    assert float(np.max(np.abs(out - ref) / ref)) <= 1e-5
+
+
 def test_device_launch_path(device):
     torch = pytest.importorskip("torch")
     spec = regions.i64_region()

@@ -144,3 +144,23 @@ def test_planted_mistake_is_caught(golden):
     out = orc.region_eval(regions.f32_chain(), [golden["chain_x"]])
     out[123] = np.nextafter(out[123], np.float32(2))
     assert out.view(np.uint32).tolist() != golden["chain_native_cpu"].view(np.uint32).tolist()
+
+
+def test_ad_extension_gradients_match_reference(golden):
+    """Gradient recipes of extension descriptors, evaluated elementwise, equal
+    the reference's reverse mode (Autodiff.cpp:231-270) bit for bit."""
+    spec = regions.extension_gradient(regions.square_linear_operation())
+    out = orc.region_eval(spec, [golden["kat_square_linear_in"], golden["ad_square_linear_dz"]])
+    assert out.view(np.uint32).tolist() == golden["ad_square_linear_grad"].view(np.uint32).tolist()
+    spec = regions.extension_gradient(regions.chain_operation())
+    out = orc.region_eval(spec, [golden["ad_chain_x"], golden["ad_chain_dz"]])
+    assert out.view(np.uint32).tolist() == golden["ad_chain_grad"].view(np.uint32).tolist()
+
+
+@pytest.mark.parametrize("name", ["dx", "dw1", "dw2", "dt"])
+def test_ad_linear_loss_backward_matches_reference(golden, name):
+    """The reference's generated backward (BroadcastToShape, ReduceToShape,
+    Transpose, MatMul, Negate) restated as a region reproduces its vjp."""
+    args = [golden["ad_lin_x"], golden["ad_lin_w1"], golden["ad_lin_w2"], golden["ad_lin_t"], 1.0]
+    out = orc.region_eval(regions.linear_loss_backward(name), args)
+    assert out.view(np.uint32).tolist() == golden[f"ad_lin_{name}"].view(np.uint32).tolist()

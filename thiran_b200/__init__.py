@@ -32,6 +32,8 @@ KIND_SCALAR, KIND_TENSOR = 1, 2
 (OP_INPUT, OP_INTEGER, OP_FLOAT, OP_TENSOR_LITERAL, OP_ALIAS, OP_COPY, OP_NEGATE, OP_ADD, OP_SUBTRACT,
  OP_ELEMENT_MULTIPLY, OP_EXTENSION, OP_INDEX, OP_UNSUPPORTED) = range(13)
 OP_SUM, OP_ROW_MAX, OP_SOFTMAX, OP_RELU = 32, 33, 34, 35
+(OP_EXTENSION_GRADIENT, OP_TRANSPOSE, OP_MATMUL, OP_BROADCAST_TO_SHAPE, OP_REDUCE_TO_SHAPE,
+ OP_ZERO_LIKE) = range(36, 42)
 (SCALAR_INPUT, SCALAR_CONSTANT_F32, SCALAR_ADD, SCALAR_SUBTRACT, SCALAR_MULTIPLY, SCALAR_DIVIDE,
  SCALAR_NEGATE) = range(1, 8)
 EFFECT_PURE, EFFECT_MAY_TRAP = 0, 1
@@ -320,6 +322,11 @@ class Operation:
     backends: int = BACKEND_REFERENCE | BACKEND_CPU | BACKEND_GPU
     minimum_rank: int = 1
     maximum_rank: int = 2
+    # Reverse derivative (DerivativeV0): one gradient recipe (nodes, root) per
+    # operand over (primals..., result, cotangent); None = not differentiable.
+    gradients: Sequence = None
+    saved_inputs: int = 0
+    saves_output: bool = False
     _keep: list = field(default_factory=list, repr=False)
 
     def descriptor(self) -> OperationDesc:
@@ -327,9 +334,24 @@ class Operation:
         name = self.name.encode()
         version = self.semantic_version.encode()
         self._keep[:] = [nodes, name, version]
+        derivative = None
+        if self.gradients is not None:
+            recipes = (ScalarRecipe * self.arity)()
+            mask = 0
+            for k, g in enumerate(self.gradients):
+                if g is None:
+                    continue
+                g_nodes, g_root = g
+                arr = (ScalarNode * len(g_nodes))(*[ScalarNode(*t) for t in g_nodes])
+                self._keep.append(arr)
+                recipes[k] = ScalarRecipe(arr, len(g_nodes), g_root, self.arity + 2)
+                mask |= 1 << k
+            d = Derivative(mask, self.saved_inputs or mask, 1 if self.saves_output else 0, recipes, self.arity)
+            self._keep += [recipes, d]
+            derivative = C.pointer(d)
         return OperationDesc(name, version, self.arity, self.minimum_rank, self.maximum_rank, 0, 1, self.effect,
                              self.backends, 1 if self.fusible else 0,
-                             ScalarRecipe(nodes, len(self.recipe), self.root, self.arity), None)
+                             ScalarRecipe(nodes, len(self.recipe), self.root, self.arity), derivative)
 
 
 def recipe_from_expression(ops: Sequence[tuple]) -> list[tuple]:
@@ -425,6 +447,29 @@ class RegionBuilder:
         kept = [e for i, e in enumerate(shape) if i != axis]
         return self._add(OP_SUM, dtype, kept, deps=[a], axis=axis)
 
+    # reverse-AD operations (Autodiff.cpp emits them into backward functions)
+    def extension_gradient(self, operation: Operation, operand: int, *args):
+        """Gradient of `operation` w.r.t. operand `operand`; args = primal
+        operands..., primal result, output cotangent."""
+        return self._add(OP_EXTENSION_GRADIENT, *self._like(args[0]), deps=list(args), axis=operand,
+                         extension=operation)
+
+    def transpose(self, a):
+        dtype, shape = self._like(a)
+        return self._add(OP_TRANSPOSE, dtype, [shape[1], shape[0]], deps=[a])
+
+    def matmul(self, a, b):
+        return self._add(OP_MATMUL, F32, [self._like(a)[1][0], self._like(b)[1][1]], deps=[a, b])
+
+    def broadcast_to_shape(self, value, reference, axis):
+        return self._add(OP_BROADCAST_TO_SHAPE, *self._like(reference), deps=[value, reference], axis=axis)
+
+    def reduce_to_shape(self, value, reference):
+        return self._add(OP_REDUCE_TO_SHAPE, *self._like(reference), deps=[value, reference])
+
+    def zero_like(self, reference):
+        return self._add(OP_ZERO_LIKE, *self._like(reference), deps=[reference])
+
     def build(self, output: int) -> "RegionSpec":
         self.output = output
         return RegionSpec(self)
@@ -485,6 +530,12 @@ class RegionSpec:
                 s = [e for i, e in enumerate(deps[0]) if i != n["axis"]]
             elif op == OP_ROW_MAX:
                 s = [deps[0][0]]
+            elif op == OP_TRANSPOSE:
+                s = [deps[0][1], deps[0][0]]
+            elif op == OP_MATMUL:
+                s = [deps[0][0], deps[1][1]]
+            elif op in (OP_BROADCAST_TO_SHAPE, OP_REDUCE_TO_SHAPE):
+                s = list(deps[1])
             else:
                 s = list(deps[0]) if deps else list(n["shape"])
             shapes[n["id"]] = s

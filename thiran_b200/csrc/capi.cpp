@@ -162,6 +162,89 @@ void downloadOutput(const Value& out, void* host, cudaStream_t stream, thb_evide
     }
 }
 
+bool pinnedHost(const void* p) {
+    cudaPointerAttributes attr{};
+    if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return attr.type == cudaMemoryTypeHost;
+}
+
+// Chunked, three-stream execution of a row-local region over pinned host
+// buffers (see CompiledRegion::Lane). Returns false, having done nothing,
+// when the region or the buffers do not qualify.
+bool executePipelined(CompiledRegion& r, const std::vector<Value>& host, void* output, std::uint64_t outputCount,
+                      cudaStream_t stream, thb_evidence& ev, std::uint32_t* stagedErrors) {
+    constexpr std::size_t kMinBytes = 64ull << 20;
+    constexpr std::size_t kChunkBytes = 48ull << 20;
+    if (!r.rowLocal() || host.empty() || !output) return false;
+    const Node& outNode = r.region().at(r.region().output);
+    const std::uint64_t rows = host[0].shape[0];
+    if (!host[0].tensor || rows == 0) return false;
+    std::size_t total = 0, rowBytes = 0;
+    for (const Value& v : host) {
+        if (!v.tensor || v.shape[0] != rows || !pinnedHost(v.data)) return false;
+        total += v.bytes();
+        rowBytes += v.bytes() / rows;
+    }
+    if (outputCount % rows) return false;
+    const std::size_t outRowBytes = static_cast<std::size_t>(outputCount / rows) * width(outNode.dtype);
+    total += outRowBytes * rows;
+    rowBytes += outRowBytes;
+    if (total < kMinBytes || !pinnedHost(output)) return false;
+
+    const std::uint64_t chunkRows = std::max<std::uint64_t>(1, kChunkBytes / rowBytes);
+    cudaEvent_t cleared = r.lane(0).done;
+    r.clearErrors(stream);
+    cudaCheck(cudaEventRecord(cleared, stream), "cudaEventRecord(clear)");
+    for (std::size_t k = 0; k < CompiledRegion::kLanes; ++k)
+        cudaCheck(cudaStreamWaitEvent(r.lane(k).stream, cleared, 0), "cudaStreamWaitEvent");
+    std::size_t used = 0;
+    for (std::uint64_t start = 0, chunk = 0; start < rows; start += chunkRows, ++chunk) {
+        const std::uint64_t n = std::min(chunkRows, rows - start);
+        auto& lane = r.lane(chunk);
+        used = std::max<std::size_t>(used, chunk + 1);
+        std::vector<Value> part = host;
+        for (std::size_t i = 0; i < host.size(); ++i) {
+            const std::size_t rb = host[i].bytes() / rows;
+            if (lane.inputs[i]->reserve(rb * chunkRows, r.device())) {
+                ++ev.allocation_count;
+                ev.allocation_bytes_requested += rb * chunkRows;
+            }
+            cudaCheck(cudaMemcpyAsync(lane.inputs[i]->ptr, static_cast<const char*>(host[i].data) + start * rb, rb * n,
+                                      cudaMemcpyHostToDevice, lane.stream),
+                      "cudaMemcpyAsync(upload chunk)");
+            ++ev.host_to_device_copies;
+            ev.host_to_device_bytes += rb * n;
+            part[i].data = lane.inputs[i]->ptr;
+            part[i].shape[0] = n;
+        }
+        if (lane.output.reserve(outRowBytes * chunkRows, r.device())) {
+            ++ev.allocation_count;
+            ev.allocation_bytes_requested += outRowBytes * chunkRows;
+        }
+        r.run(part, lane.stream, ev, lane.output.ptr, [&](const Value& o) {
+            if (o.count() != n * (outputCount / rows))
+                fail(Category::Unsupported, "GPU-OUTPUT-SHAPE", "output buffer size disagrees with the region output");
+        });
+        cudaCheck(cudaMemcpyAsync(static_cast<char*>(output) + start * outRowBytes, lane.output.ptr, outRowBytes * n,
+                                  cudaMemcpyDeviceToHost, lane.stream),
+                  "cudaMemcpyAsync(download chunk)");
+        ++ev.device_to_host_copies;
+        ev.device_to_host_bytes += outRowBytes * n;
+    }
+    ev.input_storage_uploads += host.size();
+    ++ev.result_downloads;
+    for (std::size_t k = 0; k < std::min(used, CompiledRegion::kLanes); ++k) {
+        auto& lane = r.lane(k);
+        cudaCheck(cudaEventRecord(lane.done, lane.stream), "cudaEventRecord(lane)");
+        cudaCheck(cudaStreamWaitEvent(stream, lane.done, 0), "cudaStreamWaitEvent(lane)");
+    }
+    r.copyErrors(stream, stagedErrors);
+    return true;
+}
+
 void waitEvent(cudaEvent_t event, std::uint64_t timeoutMs) {
     const auto start = std::chrono::steady_clock::now();
     unsigned sleepUs = 20;
@@ -248,16 +331,23 @@ int thb_region_execute(thb_region* region, const thb_abi_arg* args, uint64_t arg
         cudaCheck(cudaSetDevice(r.device()), "cudaSetDevice");
         cudaStream_t stream = r.stream();
         std::uint64_t reads = 0;
-        auto inputs = bind(r, args, argc, true, stream, ev, &reads);
-        r.clearErrors(stream);
-        ++ev.submitted_operations;
-        Value out = r.run(inputs, stream, ev, nullptr,
-                          [&](const Value& o) { checkOutputCount(o, outputCount, true, output); });
-        downloadOutput(out, output, stream, ev);
         std::vector<std::uint32_t> words(std::max<std::size_t>(1, r.errorWordCount()));
         PinnedBuffer staged;
         staged.reserve(words.size() * sizeof(std::uint32_t));
-        r.copyErrors(stream, static_cast<std::uint32_t*>(staged.ptr));
+        ++ev.submitted_operations;
+        const auto hostValues = bind(r, args, argc, false, stream, ev, &reads);
+        bool pipelined = false;
+        if (r.rowLocal())
+            pipelined = executePipelined(r, hostValues, output, outputCount, stream, ev,
+                                         static_cast<std::uint32_t*>(staged.ptr));
+        if (!pipelined) {
+            auto inputs = bind(r, args, argc, true, stream, ev, &reads);
+            r.clearErrors(stream);
+            Value out = r.run(inputs, stream, ev, nullptr,
+                              [&](const Value& o) { checkOutputCount(o, outputCount, true, output); });
+            downloadOutput(out, output, stream, ev);
+            r.copyErrors(stream, static_cast<std::uint32_t*>(staged.ptr));
+        }
         ++ev.event_records;
         cudaCheck(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
         ++ev.synchronizations;

@@ -125,8 +125,11 @@ void emitBody(std::ostringstream& out, const Region& region, const FusionGroup& 
     for (auto id : group.nodes) {
         const Node& n = region.at(id);
         const std::string v = "v" + std::to_string(id);
-        if (n.op == Op::Extension) {
-            const Recipe& recipe = n.extension->forward;
+        if (n.op == Op::Extension || n.op == Op::ExtensionGradient) {
+            // A gradient recipe reads (primals..., result, cotangent), which
+            // are exactly the node's dependencies in order.
+            const Recipe& recipe =
+                n.op == Op::Extension ? n.extension->forward : n.extension->derivative->gradients.at(n.axis);
             const std::string prefix = "e" + std::to_string(id) + "_";
             for (std::size_t r = 0; r < recipe.nodes.size(); ++r) {
                 const ScalarNode& s = recipe.nodes[r];

@@ -34,6 +34,18 @@ std::uint32_t sumAllPartialCount(std::uint64_t n, int smCount);
 cudaError_t sumAllF32(const float* x, std::uint64_t n, double* partials, std::uint32_t partialCount, double* out64,
                       float* out32, int smCount, cudaStream_t stream);
 
+// y[c, r] = x[r, c] for a row-major [rows, cols] matrix of 4- or 8-byte
+// elements (32x32 shared-memory tiles, coalesced on both sides).
+cudaError_t transpose(const void* x, void* y, std::uint64_t rows, std::uint64_t cols, std::size_t elementBytes,
+                      int smCount, cudaStream_t stream);
+// y[r, c] = axis == 0 ? src[c] : src[r] over a row-major [rows, cols] target
+// (BroadcastToShape: the source is the target with `axis` removed).
+cudaError_t broadcastF32(const float* src, float* y, std::uint64_t rows, std::uint64_t cols, int axis, int smCount,
+                         cudaStream_t stream);
+// y[i] = *deviceScalar (when not null) else value, for i < n.
+cudaError_t fillF32(const float* deviceScalar, float value, float* y, std::uint64_t n, int smCount,
+                    cudaStream_t stream);
+
 // Largest row length the shared-memory staged softmax handles (longer rows
 // take the streaming two-pass kernel).
 constexpr std::uint64_t kMaxSmemRowCols = 8192;

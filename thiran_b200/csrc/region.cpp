@@ -26,16 +26,27 @@ const char* opName(Op op) {
     case Op::RowMax: return "RowMax";
     case Op::Softmax: return "Softmax";
     case Op::Relu: return "Relu";
+    case Op::ExtensionGradient: return "ExtensionGradient";
+    case Op::Transpose: return "Transpose";
+    case Op::MatMul: return "MatMul";
+    case Op::BroadcastToShape: return "BroadcastToShape";
+    case Op::ReduceToShape: return "ReduceToShape";
+    case Op::ZeroLike: return "ZeroLike";
     }
     return "Unsupported";
 }
 
 bool isElementwise(Op op) {
     return op == Op::Negate || op == Op::Add || op == Op::Subtract || op == Op::ElementMultiply ||
-           op == Op::Extension || op == Op::Relu;
+           op == Op::Extension || op == Op::Relu || op == Op::ExtensionGradient;
 }
 
 bool isReduction(Op op) { return op == Op::Sum || op == Op::RowMax || op == Op::Softmax; }
+
+bool isKernelOp(Op op) {
+    return op == Op::Transpose || op == Op::MatMul || op == Op::BroadcastToShape || op == Op::ReduceToShape ||
+           op == Op::ZeroLike;
+}
 
 // ---- operation descriptors ---------------------------------------------------
 
@@ -260,7 +271,9 @@ Region importRegion(const thb_region_desc& desc) {
         case THB_OP_INPUT: case THB_OP_INTEGER: case THB_OP_FLOAT: case THB_OP_TENSOR_LITERAL:
         case THB_OP_ALIAS: case THB_OP_COPY: case THB_OP_NEGATE: case THB_OP_ADD: case THB_OP_SUBTRACT:
         case THB_OP_ELEMENT_MULTIPLY: case THB_OP_EXTENSION: case THB_OP_INDEX: case THB_OP_SUM:
-        case THB_OP_ROW_MAX: case THB_OP_SOFTMAX: case THB_OP_RELU:
+        case THB_OP_ROW_MAX: case THB_OP_SOFTMAX: case THB_OP_RELU: case THB_OP_EXTENSION_GRADIENT:
+        case THB_OP_TRANSPOSE: case THB_OP_MATMUL: case THB_OP_BROADCAST_TO_SHAPE: case THB_OP_REDUCE_TO_SHAPE:
+        case THB_OP_ZERO_LIKE:
             break;
         default: n.op = Op::Unsupported;
         }
@@ -379,6 +392,66 @@ std::vector<std::string> verifyRegion(const Region& region) {
             if (!ok) errors.push_back("TRV12 malformed Softmax");
             break;
         }
+        case Op::ExtensionGradient: {
+            // deps: arity primals, the primal result, the output cotangent;
+            // axis selects the differentiable operand (Autodiff.cpp:231-270).
+            bool ok = n.extension && n.extension->derivative && validateOperation(*n.extension).empty() &&
+                      n.dtype == DType::F32 && numericTensor(n) && n.axis >= 0 &&
+                      static_cast<std::uint32_t>(n.axis) < n.extension->arity &&
+                      n.dependencies.size() == n.extension->arity + 2u;
+            if (ok) {
+                const auto& d = *n.extension->derivative;
+                ok = ((d.differentiableInputs >> n.axis) & 1ULL) &&
+                     static_cast<std::size_t>(n.axis) < d.gradients.size() && !d.gradients[n.axis].nodes.empty();
+                for (auto id : n.dependencies) {
+                    const Node* in = region.find(id);
+                    ok = ok && in && in->sameType(n) && !in->knownShapeMismatch(n);
+                }
+            }
+            if (!ok) errors.push_back("TRV11 malformed extension gradient");
+            break;
+        }
+        case Op::Transpose: {
+            const Node* in = dep(0);
+            bool ok = n.dependencies.size() == 1 && in && in->rank == 2 && n.rank == 2 && in->dtype == n.dtype;
+            ok = ok && (n.extent[0] < 0 || in->extent[1] < 0 || n.extent[0] == in->extent[1]) &&
+                 (n.extent[1] < 0 || in->extent[0] < 0 || n.extent[1] == in->extent[0]);
+            if (!ok) errors.push_back("TRV12 malformed Transpose");
+            break;
+        }
+        case Op::MatMul: {
+            const Node* a = dep(0); const Node* b = dep(1);
+            bool ok = n.dependencies.size() == 2 && a && b && a->rank == 2 && b->rank == 2 && n.rank == 2 &&
+                      a->dtype == DType::F32 && b->dtype == DType::F32 && n.dtype == DType::F32;
+            ok = ok && (a->extent[1] < 0 || b->extent[0] < 0 || a->extent[1] == b->extent[0]) &&
+                 (n.extent[0] < 0 || a->extent[0] < 0 || n.extent[0] == a->extent[0]) &&
+                 (n.extent[1] < 0 || b->extent[1] < 0 || n.extent[1] == b->extent[1]);
+            if (!ok) errors.push_back("TRV12 malformed MatMul");
+            break;
+        }
+        case Op::BroadcastToShape: {
+            const Node* v = dep(0); const Node* ref = dep(1);
+            bool ok = n.dependencies.size() == 2 && v && ref && v->dtype == DType::F32 && ref->dtype == DType::F32 &&
+                      n.dtype == DType::F32 && numericTensor(*ref) && n.sameType(*ref) && !n.knownShapeMismatch(*ref) &&
+                      n.axis >= 0 && static_cast<std::uint32_t>(n.axis) < ref->rank && v->rank + 1 == ref->rank;
+            if (!ok) errors.push_back("TRV12 malformed BroadcastToShape");
+            break;
+        }
+        case Op::ReduceToShape: {
+            const Node* v = dep(0); const Node* ref = dep(1);
+            bool ok = n.dependencies.size() == 2 && v && ref && v->dtype == DType::F32 && ref->dtype == DType::F32 &&
+                      n.dtype == DType::F32 && numericTensor(*v) && n.rank == ref->rank && ref->rank <= v->rank &&
+                      !n.knownShapeMismatch(*ref);
+            if (!ok) errors.push_back("TRV12 malformed ReduceToShape");
+            break;
+        }
+        case Op::ZeroLike: {
+            const Node* ref = dep(0);
+            bool ok = n.dependencies.size() == 1 && ref && n.dtype == DType::F32 && n.rank == ref->rank &&
+                      !n.knownShapeMismatch(*ref);
+            if (!ok) errors.push_back("TRV12 malformed ZeroLike");
+            break;
+        }
         case Op::Unsupported: errors.push_back("TRV10 unsupported operation admitted"); break;
         case Op::Input: break;
         case Op::TensorLiteral: {
@@ -452,7 +525,9 @@ bool fusibleNode(const Node& n) {
     return n.extension && n.extension->fusible && n.extension->effect == THB_EFFECT_PURE;
 }
 
-bool kernelNode(const Node& n) { return isElementwise(n.op) || isReduction(n.op) || n.op == Op::Index; }
+bool kernelNode(const Node& n) {
+    return isElementwise(n.op) || isReduction(n.op) || isKernelOp(n.op) || n.op == Op::Index;
+}
 
 // Consumers of each canonical value, looking through Alias nodes
 // (fusionConsumers, src/backend/v0/PhysicalPlan.cpp:78-87).
@@ -504,7 +579,8 @@ std::vector<FusionGroup> makeGroups(const Region& region, const PlanOptions& opt
             FusionGroup g;
             g.id = static_cast<std::uint32_t>(groups.size() + 1);
             g.kind = isElementwise(current.op) ? GroupKind::Elementwise
-                   : isReduction(current.op) ? GroupKind::Reduction : GroupKind::Index;
+                   : isReduction(current.op) ? GroupKind::Reduction
+                   : isKernelOp(current.op) ? GroupKind::Kernel : GroupKind::Index;
             g.nodes = {current.id};
             g.output = current.id;
             g.dtype = current.op == Op::Index ? region.at(region.canonical(current.dependencies.at(0))).dtype : current.dtype;

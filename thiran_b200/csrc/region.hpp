@@ -38,6 +38,12 @@ enum class Op : std::uint32_t {
     RowMax = THB_OP_ROW_MAX,
     Softmax = THB_OP_SOFTMAX,
     Relu = THB_OP_RELU,
+    ExtensionGradient = THB_OP_EXTENSION_GRADIENT,
+    Transpose = THB_OP_TRANSPOSE,
+    MatMul = THB_OP_MATMUL,
+    BroadcastToShape = THB_OP_BROADCAST_TO_SHAPE,
+    ReduceToShape = THB_OP_REDUCE_TO_SHAPE,
+    ZeroLike = THB_OP_ZERO_LIKE,
 };
 
 const char* opName(Op op);
@@ -118,7 +124,9 @@ Region importRegion(const thb_region_desc&);
 // TRVnn errors, empty when the region is well formed.
 std::vector<std::string> verifyRegion(const Region&);
 
-enum class GroupKind { Elementwise, Reduction, Index };
+// Elementwise groups get a generated kernel; Reduction and Kernel groups run
+// one precompiled kernel (reductions, transpose, matmul, broadcast).
+enum class GroupKind { Elementwise, Reduction, Index, Kernel };
 
 struct FusionGroup {
     std::uint32_t id = 0;
@@ -174,5 +182,7 @@ Plan buildPlan(const Region&, PlanOptions);
 
 bool isElementwise(Op op);
 bool isReduction(Op op);
+// Transpose, MatMul, BroadcastToShape, ReduceToShape, ZeroLike.
+bool isKernelOp(Op op);
 
 } // namespace thb

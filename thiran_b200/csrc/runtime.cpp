@@ -4,7 +4,9 @@
 #include <algorithm>
 #include <cstring>
 
+#include "gemm.hpp"
 #include "kernels.hpp"
+#include "mlp.hpp"
 
 namespace thb {
 
@@ -145,17 +147,47 @@ CompiledRegion::CompiledRegion(const thb_region_desc& desc, PlanOptions options,
     errors_.reserve(std::max<std::size_t>(1, plan_.groups.size()) * sizeof(std::uint32_t) + 64, device_);
     check(cudaMemsetAsync(errors_.ptr, 0, errors_.bytes, stream_), "cudaMemsetAsync");
     check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+
+    // Row-local: one kernel group; every other node is an Input tensor or an
+    // Alias; the group's operation keeps rows independent.
+    rowLocal_ = plan_.groups.size() == 1 && region_.at(region_.output).tensor();
+    for (const auto& n : region_.nodes) {
+        if (n.op == Op::Input) rowLocal_ = rowLocal_ && n.tensor();
+        else if (n.op == Op::Alias) continue;
+        else if (isElementwise(n.op) || n.op == Op::Softmax || n.op == Op::RowMax) continue;
+        else if (n.op == Op::Sum) rowLocal_ = rowLocal_ && n.axis == 1;
+        else rowLocal_ = false;
+    }
 }
 
 CompiledRegion::~CompiledRegion() {
+    int previous = -1;
+    cudaGetDevice(&previous);
+    cudaSetDevice(device_);
+    for (auto& l : lanes_) {
+        if (l.stream) {
+            cudaStreamSynchronize(l.stream);
+            cudaStreamDestroy(l.stream);
+        }
+        if (l.done) cudaEventDestroy(l.done);
+    }
     if (stream_) {
-        int previous = -1;
-        cudaGetDevice(&previous);
-        cudaSetDevice(device_);
         cudaStreamSynchronize(stream_);
         cudaStreamDestroy(stream_);
-        if (previous >= 0) cudaSetDevice(previous);
     }
+    if (previous >= 0) cudaSetDevice(previous);
+}
+
+CompiledRegion::Lane& CompiledRegion::lane(std::size_t k) {
+    if (!lanesReady_) {
+        lanesReady_ = true;
+        for (auto& l : lanes_) {
+            check(cudaStreamCreateWithFlags(&l.stream, cudaStreamNonBlocking), "cudaStreamCreateWithFlags(lane)");
+            check(cudaEventCreateWithFlags(&l.done, cudaEventDisableTiming), "cudaEventCreate(lane)");
+            for (std::size_t i = 0; i < region_.inputs.size(); ++i) l.inputs.push_back(std::make_unique<DeviceBuffer>());
+        }
+    }
+    return lanes_[k % kLanes];
 }
 
 DeviceBuffer& CompiledRegion::inputBuffer(std::size_t position) {
@@ -297,6 +329,97 @@ void CompiledRegion::launchReduction(const FusionGroup& group, const Value& in, 
     ++ev.stream_submissions;
 }
 
+void* CompiledRegion::scratch(std::uint32_t key, std::size_t bytes, thb_evidence& ev) {
+    auto& buffer = scalars_[key];
+    if (!buffer) buffer = std::make_unique<DeviceBuffer>();
+    if (buffer->reserve(bytes, device_)) {
+        ++ev.allocation_count;
+        ev.allocation_bytes_requested += bytes;
+    }
+    return buffer->ptr;
+}
+
+void CompiledRegion::launchKernel(const FusionGroup& group, const std::vector<const Value*>& in, Value& out,
+                                  cudaStream_t stream, thb_evidence& ev) {
+    const Node& node = region_.at(group.nodes.front());
+    std::uint32_t* status = static_cast<std::uint32_t*>(errors_.ptr) + (group.id - 1);
+    const int sms = info_->smCount;
+    auto launched = [&](cudaError_t e, const char* what) {
+        check(e, what);
+        ++ev.kernel_launches;
+        ++ev.stream_submissions;
+    };
+    if (out.count() == 0) return;
+    switch (node.op) {
+    case Op::ZeroLike:
+        check(cudaMemsetAsync(out.data, 0, out.bytes(), stream), "cudaMemsetAsync(zero-like)");
+        ++ev.stream_submissions;
+        return;
+    case Op::Transpose:
+        launched(kernels::transpose(in[0]->data, out.data, in[0]->shape[0], in[0]->shape[1], width(in[0]->dtype), sms,
+                                    stream),
+                 "transpose launch");
+        return;
+    case Op::BroadcastToShape:
+        if (in[0]->rank == 0) {  // scalar source: host value or device scalar
+            launched(kernels::fillF32(in[0]->onDevice ? static_cast<const float*>(in[0]->data) : nullptr, in[0]->f32,
+                                      static_cast<float*>(out.data), out.count(), sms, stream),
+                     "broadcast fill");
+            return;
+        }
+        launched(kernels::broadcastF32(static_cast<const float*>(in[0]->data), static_cast<float*>(out.data),
+                                       out.rank == 2 ? out.shape[0] : 1, out.rank == 2 ? out.shape[1] : out.shape[0],
+                                       out.rank == 2 ? node.axis : 0, sms, stream),
+                 "broadcast launch");
+        return;
+    case Op::ReduceToShape: {
+        const Value& src = *in[0];
+        const float* x = static_cast<const float*>(src.data);
+        float* y = static_cast<float*>(out.data);
+        const std::uint64_t rows = src.rank == 2 ? src.shape[0] : 1;
+        const std::uint64_t cols = src.rank == 2 ? src.shape[1] : src.shape[0];
+        if (out.count() == src.count()) {  // nothing to reduce
+            check(cudaMemcpyAsync(out.data, src.data, src.bytes(), cudaMemcpyDeviceToDevice, stream), "reduce copy");
+            ++ev.device_to_device_copies;
+            ev.device_to_device_bytes += src.bytes();
+            return;
+        }
+        if (out.count() == 1) {
+            const std::uint32_t parts = kernels::sumAllPartialCount(src.count(), sms);
+            double* partials = static_cast<double*>(scratch(0x20000000u | group.id, parts * sizeof(double), ev));
+            launched(kernels::sumAllF32(x, src.count(), partials, parts, nullptr, y, sms, stream), "reduce sum");
+            return;
+        }
+        const bool keepRows = out.rank == 2 ? (out.shape[1] == 1) : false;
+        if (keepRows) launched(kernels::sumRowsF32(x, y, rows, cols, sms, stream, status), "reduce rows");
+        else launched(kernels::sumColsF32(x, y, rows, cols, sms, stream), "reduce columns");
+        return;
+    }
+    case Op::MatMul: {
+        const Value& a = *in[0];
+        const Value& b = *in[1];
+        const std::uint64_t m = a.shape[0], k = a.shape[1], n = b.shape[1];
+        void* a16 = scratch(0x30000000u | group.id, m * k * 2, ev);
+        void* b16 = scratch(0x38000000u | group.id, k * n * 2, ev);
+        launched(mlp::castToBf16(static_cast<const float*>(a.data), a16, m * k, sms, stream), "matmul cast A");
+        launched(mlp::castToBf16(static_cast<const float*>(b.data), b16, k * n, sms, stream), "matmul cast B");
+        if (k == 0) {
+            check(cudaMemsetAsync(out.data, 0, out.bytes(), stream), "cudaMemsetAsync(matmul k=0)");
+            return;
+        }
+        gemm::Problem q;
+        q.m = m; q.n = n; q.k = k;
+        q.a = a16; q.lda = k;
+        q.b = b16; q.bMajorMN = true; q.ldb = n;
+        q.c = out.data; q.ldc = n; q.epilogue = gemm::kEpiF32;
+        if (const char* bad = gemm::validate(q)) fail(Category::Unsupported, "GPU-UNSUPPORTED-SHAPE", bad);
+        launched(gemm::run(q, sms, status, stream), "matmul launch");
+        return;
+    }
+    default: fail(Category::Unsupported, "GPU-UNSUPPORTED-OP", "kernel group holds an unexpected node");
+    }
+}
+
 Value CompiledRegion::run(const std::vector<Value>& inputs, cudaStream_t stream, thb_evidence& ev,
                           void* outputOverride, const std::function<void(const Value&)>& onShapes) {
     check(cudaSetDevice(device_), "cudaSetDevice");
@@ -331,7 +454,44 @@ Value CompiledRegion::run(const std::vector<Value>& inputs, cudaStream_t stream,
         case Op::Alias: v = dep(0); break;
         case Op::Copy: case Op::Negate: case Op::Relu: case Op::Softmax:
             v.shape[0] = dep(0).shape[0]; v.shape[1] = dep(0).shape[1]; break;
-        case Op::Add: case Op::Subtract: case Op::ElementMultiply: case Op::Extension: {
+        case Op::Transpose:
+            v.shape[0] = dep(0).shape[1]; v.shape[1] = dep(0).shape[0]; break;
+        case Op::MatMul: {
+            const Value& a = dep(0);
+            const Value& b = dep(1);
+            if (a.shape[1] != b.shape[0])
+                fail(Category::Semantic, "TH-SPEC-SHAPE", "matmul inner extents differ");
+            if (a.shape[1] % 8 || b.shape[1] % 8)
+                fail(Category::Unsupported, "GPU-UNSUPPORTED-SHAPE",
+                     "tensor-core matmul needs K and N multiples of 8 (16-byte rows)");
+            v.shape[0] = a.shape[0]; v.shape[1] = b.shape[1];
+            break;
+        }
+        case Op::BroadcastToShape: {
+            const Value& src = dep(0);
+            const Value& ref = dep(1);
+            // The source is the target with `axis` removed (Evaluator.cpp:278-309).
+            const std::uint64_t kept = ref.rank == 2 ? ref.shape[n.axis == 0 ? 1 : 0] : 1;
+            if (src.rank + 1 != ref.rank || (ref.rank == 2 && src.shape[0] != kept))
+                fail(Category::Semantic, "TH-SPEC-BROADCAST", "broadcast source does not match the target");
+            v.shape[0] = ref.shape[0]; v.shape[1] = ref.shape[1];
+            break;
+        }
+        case Op::ReduceToShape: {
+            const Value& src = dep(0);
+            const Value& ref = dep(1);
+            // Target axes of extent 1 (or missing leading axes) are summed
+            // (Evaluator.cpp:258-277).
+            const std::uint32_t delta = src.rank - ref.rank;
+            for (std::uint32_t d = 0; d < ref.rank; ++d)
+                if (ref.shape[d] != 1 && ref.shape[d] != src.shape[d + delta])
+                    fail(Category::Semantic, "TH-SPEC-BROADCAST", "reduce target does not match the source");
+            v.shape[0] = ref.shape[0]; v.shape[1] = ref.shape[1];
+            break;
+        }
+        case Op::ZeroLike:
+            v.shape[0] = dep(0).shape[0]; v.shape[1] = dep(0).shape[1]; break;
+        case Op::Add: case Op::Subtract: case Op::ElementMultiply: case Op::Extension: case Op::ExtensionGradient: {
             const Value& a = dep(0);
             for (std::size_t k = 1; k < n.dependencies.size(); ++k) {
                 const Value& b = dep(k);
@@ -474,6 +634,10 @@ Value CompiledRegion::run(const std::vector<Value>& inputs, cudaStream_t stream,
                 std::vector<const Value*> operands;
                 for (auto id : group->inputs) operands.push_back(&values.at(id));
                 launchElementwise(*group, operands, out, stream, ev);
+            } else if (group->kind == GroupKind::Kernel) {
+                std::vector<const Value*> operands;
+                for (auto d : n.dependencies) operands.push_back(&values.at(region_.canonical(d)));
+                launchKernel(*group, operands, out, stream, ev);
             } else {
                 launchReduction(*group, values.at(region_.canonical(n.dependencies.at(0))), out, stream, ev);
             }

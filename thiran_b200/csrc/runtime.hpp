@@ -111,11 +111,28 @@ public:
     DeviceBuffer& inputBuffer(std::size_t position);
     std::mutex mutex;
 
+    // Chunked host execution: a row-local region (one kernel group whose
+    // output rows depend only on the same input rows) runs chunk by chunk on
+    // three streams, so the host->device copy of chunk k+1, the kernel on
+    // chunk k and the device->host copy of chunk k-1 overlap.
+    struct Lane {
+        cudaStream_t stream = nullptr;
+        cudaEvent_t done = nullptr;
+        std::vector<std::unique_ptr<DeviceBuffer>> inputs;
+        DeviceBuffer output;
+    };
+    static constexpr std::size_t kLanes = 3;
+    bool rowLocal() const { return rowLocal_; }
+    Lane& lane(std::size_t k);
+
 private:
     void launchElementwise(const FusionGroup&, const std::vector<const Value*>& operands, Value& out,
                            cudaStream_t stream, thb_evidence& evidence);
     void launchReduction(const FusionGroup&, const Value& operand, Value& out, cudaStream_t stream,
                          thb_evidence& evidence);
+    void launchKernel(const FusionGroup&, const std::vector<const Value*>& operands, Value& out,
+                      cudaStream_t stream, thb_evidence& evidence);
+    void* scratch(std::uint32_t key, std::size_t bytes, thb_evidence& evidence);
     void* slotPointer(std::uint32_t value, std::size_t bytes, thb_evidence& evidence);
 
     Region region_;
@@ -132,6 +149,9 @@ private:
     std::map<std::uint32_t, std::unique_ptr<DeviceBuffer>> scalars_;
     std::map<std::size_t, std::unique_ptr<DeviceBuffer>> inputs_;
     std::set<std::uint32_t> touched_;      // slots used by the current run
+    bool rowLocal_ = false;
+    bool lanesReady_ = false;
+    Lane lanes_[kLanes];
     void* outputOverride_ = nullptr;
     std::uint32_t outputRoot_ = 0;
 };

@@ -28,8 +28,77 @@ CHAIN_RECIPE = recipe_from_expression([
 ])
 
 
+# d/dx of the chain over (x, y, dz): dz * ((((x*1.5 + 0.25) + x*1.5) - 1) * 0.5 + 1)
+CHAIN_GRADIENT = recipe_from_expression([
+    ("x", 0),                      # 0 x
+    ("c", 1.5),                    # 1
+    (SCALAR_MULTIPLY, 0, 1),       # 2 x*1.5
+    ("c", 0.25),                   # 3
+    (SCALAR_ADD, 2, 3),            # 4 x*1.5+0.25
+    (SCALAR_ADD, 4, 2),            # 5 + x*1.5
+    ("c", 1.0),                    # 6
+    (SCALAR_SUBTRACT, 5, 6),       # 7 - 1
+    ("c", 0.5),                    # 8
+    (SCALAR_MULTIPLY, 7, 8),       # 9 * 0.5
+    (SCALAR_ADD, 9, 6),            # 10 + 1
+    ("x", 2),                      # 11 dz
+    (SCALAR_MULTIPLY, 11, 10),     # 12 dz * (...)
+])
+
+# examples/research_extension: x*x + x, gradient dz * (2x + 1).
+SQUARE_LINEAR_RECIPE = recipe_from_expression([("x", 0), (SCALAR_MULTIPLY, 0, 0), (SCALAR_ADD, 1, 0)])
+SQUARE_LINEAR_GRADIENT = recipe_from_expression([
+    ("x", 2), ("c", 2.0), ("x", 0), (SCALAR_MULTIPLY, 1, 2), ("c", 1.0), (SCALAR_ADD, 3, 4), (SCALAR_MULTIPLY, 0, 5),
+])
+
+
 def chain_operation() -> Operation:
-    return Operation("research_chain", CHAIN_RECIPE, root=9, arity=1)
+    return Operation("research_chain", CHAIN_RECIPE, root=9, arity=1, gradients=[(CHAIN_GRADIENT, 12)])
+
+
+def square_linear_operation() -> Operation:
+    return Operation("research_square_linear", SQUARE_LINEAR_RECIPE, root=2, arity=1,
+                     gradients=[(SQUARE_LINEAR_GRADIENT, 6)])
+
+
+def extension_gradient(operation: Operation, n=None):
+    """Backward of y = op(x): dx = gradient recipe over (x, y, dz)."""
+    b = RegionBuilder("grad")
+    x = b.input(F32, [n])
+    dz = b.input(F32, [n])
+    y = b.extension(operation, b.alias(x))
+    return b.build(b.extension_gradient(operation, 0, b.alias(x), y, b.alias(dz)))
+
+
+def linear_loss_backward(output="dw1"):
+    """The reverse-mode backward the reference generates for
+        fn loss(x, w1, w2, t) -> f32 { h = x*w1; y = h*w2; e = y - t; s = e.*e;
+                                        return sum(sum(s,1),0) }
+    (src/autodiff/v0/Autodiff.cpp:195-231), with the forward values it saves
+    recomputed in the same region. `output` selects dx, dw1, dw2 or dt."""
+    b = RegionBuilder("loss_backward")
+    x = b.input(F32, [None, None])
+    w1 = b.input(F32, [None, None])
+    w2 = b.input(F32, [None, None])
+    t = b.input(F32, [None, None])
+    ct = b.input(F32, [])
+    h = b.matmul(x, w1)
+    y = b.matmul(h, w2)
+    e = b.sub(y, t)
+    s = b.mul(e, e)
+    rows = b.sum(s, 1)
+    d16 = b.broadcast_to_shape(ct, rows, 0)
+    d17 = b.broadcast_to_shape(d16, s, 1)
+    d19 = b.reduce_to_shape(b.mul(d17, e), e)
+    d21 = b.reduce_to_shape(b.mul(d17, e), e)
+    d22 = b.add(d21, d19)
+    dy = b.reduce_to_shape(d22, y)
+    dt = b.neg(b.reduce_to_shape(d22, t))
+    dh = b.matmul(dy, b.transpose(w2))
+    dw2 = b.matmul(b.transpose(h), dy)
+    dx = b.matmul(dh, b.transpose(w1))
+    dw1 = b.matmul(b.transpose(x), dh)
+    return b.build({"dx": dx, "dw1": dw1, "dw2": dw2, "dt": dt}[output])
 
 
 def f32_chain(n=None):
