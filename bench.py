@@ -118,6 +118,7 @@ class Softmax(Workload):
     dtype = "f32"
     rows, cols = 65536, 4096
     ncu_name = "softmax_65536x4096"
+    kernel = "rowStaged softmax (rows staged by cp.async.bulk, mbarrier pipeline)"
 
     def build(self, torch, rank, world):
         from thiran_b200 import regions
@@ -129,6 +130,33 @@ class Softmax(Workload):
         return {"workload": "row softmax on [65536,4096] f32 ~ N(0,1) seed 3",
                 "global_shape": [self.rows, self.cols], "shard": f"rows/{world} per rank",
                 "parallelism": f"row-sharded x{world}, no collective", "l2": "2 GiB/step >> L2"}
+
+
+class FullSum(Workload):
+    """Full-tensor sum of the [65536, 4096] N(0,1) tensor: every rank sums its
+    row shard on the device (two-pass f64 reduction), the per-rank partials
+    are combined with an NCCL all-reduce."""
+    name = "sum"
+    bytes_per_element = 4
+    dtype = "f32"
+    rows, cols = 65536, 4096
+    ncu_name = "full_sum_65536x4096"
+    combine = True
+    kernel = "two-pass deterministic f64 full sum (sumAllPass1 + sumAllPass2)"
+    launches_per_step = 2
+
+    def build(self, torch, rank, world):
+        from thiran_b200 import regions
+        g = torch.Generator(device="cuda").manual_seed(3 + 1000 * rank)
+        x = torch.randn((self.rows // world) * self.cols, device="cuda", generator=g)
+        return regions.full_sum(), [x], torch.empty(1, device="cuda")
+
+    def config(self, world):
+        return {"workload": "full-tensor sum of [65536,4096] f32 ~ N(0,1) seed 3 (f64 accumulation)",
+                "global_shape": [self.rows, self.cols], "shard": f"rows/{world} per rank",
+                "parallelism": f"row-sharded x{world}, NCCL all-reduce of one f64 partial per rank"
+                               if world > 1 else "single GPU",
+                "l2": "1 GiB/step >> L2"}
 
 
 class Mlp(Workload):
@@ -150,7 +178,7 @@ class Mlp(Workload):
                 "l2": "weights 2x128 MiB bf16 + activations >> 126 MB L2"}
 
 
-WORKLOADS = {w.name: w for w in (I64Region(), F32Chain(), Softmax(), Mlp())}
+WORKLOADS = {w.name: w for w in (I64Region(), F32Chain(), Softmax(), FullSum(), Mlp())}
 
 
 def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_over_ranks):
@@ -172,10 +200,25 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
     loss = session.bind(thb.MLP_LOSS_SUM, torch.zeros(2, dtype=torch.float64, device="cuda"))
     session.set_weights(w1, w2, s)
     lr = 1e-3
+    multicast = None
+    if world > 1 and args.dp_collective == "nvls":
+        from thiran_b200.distributed import MulticastGradients
+        with torch.cuda.stream(stream):
+            multicast = MulticastGradients(session, dist)
+        if not multicast.available:
+            multicast = None
+    collective = ("fused GEMM epilogue multimem.red into NVLS multicast buffers" if multicast
+                  else "NCCL all-reduce of dW1+dW2" if world > 1 else None)
 
     def step():
+        if multicast:
+            with torch.cuda.stream(stream):
+                multicast.before_step()
         session.forward_backward(x, t, s)
-        if world > 1:
+        if multicast:
+            with torch.cuda.stream(stream):
+                multicast.after_backward()
+        elif world > 1:
             with torch.cuda.stream(stream):
                 dist.all_reduce(dw1)
                 dist.all_reduce(dw2)
@@ -254,7 +297,8 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (torch.Generator on device, seeded)", "config": workload.config(world),
+            "data": "synthetic (torch.Generator on device, seeded)",
+            "config": dict(workload.config(world), **({"gradient_reduction": collective} if collective else {})),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": None,
                          "kernel": "tcgen05 GEMM (128x256 tiles, TMEM accumulators)",
@@ -467,6 +511,9 @@ def main():
     p.add_argument("--workload", default="i64_region", choices=sorted(WORKLOADS))
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--dp-collective", default="nvls", choices=["nvls", "nccl"],
+                   help="MLP data-parallel gradient reduction: fused into the dW GEMMs through NVLink "
+                        "multicast (falls back to NCCL when unsupported) or NCCL all-reduce")
     p.add_argument("--shrink", type=int, default=1,
                    help="divide the leading extent (small cases for profiler captures; not a bench line)")
     args = p.parse_args()
@@ -511,13 +558,26 @@ def main():
     region = spec.compile(local)
     stream = torch.cuda.Stream()
     s = stream.cuda_stream
-    elements = out.numel()
+    elements = max(t.numel() for t in inputs)
     bytes_per_step_rank = elements * workload.bytes_per_element
+    combine = getattr(workload, "combine", False)
+    total = torch.zeros(1, dtype=torch.float64, device="cuda")
+    from thiran_b200.distributed import combine_partial_sums
+
+    def step(start=None, end=None):
+        if start is not None:
+            start.record(stream)
+        region.launch(inputs, out, s)
+        if end is not None:
+            end.record(stream)
+        if combine:  # one f64 partial per rank, all-reduced over NCCL
+            total.copy_(out)
+            combine_partial_sums(total, dist if world > 1 else None)
 
     # Warm-up (also JIT/module load and slot allocation).
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
-            region.launch(inputs, out, s)
+            step()
     region.check_errors(s)
     torch.cuda.synchronize()
 
@@ -525,19 +585,20 @@ def main():
     sampler.start()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    begin, finish = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
     with torch.cuda.stream(stream):
+        begin.record(stream)
         for k in range(args.steps):
-            starts[k].record(stream)
-            region.launch(inputs, out, s)
-            ends[k].record(stream)
+            step(starts[k], ends[k])
+        finish.record(stream)
     torch.cuda.synchronize()
     barrier()
     clocks = sampler.stop()
     region.check_errors(s)
     per_launch_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
-    total_ms = starts[0].elapsed_time(ends[-1])
+    total_ms = begin.elapsed_time(finish)
     total_ms = max_over_ranks(total_ms)
     ms_per_step = total_ms / args.steps
     value = bytes_per_step_rank * world * args.steps / (total_ms / 1e3) / 1e9
@@ -559,7 +620,11 @@ def main():
     barrier()
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
-        region_host.execute(host_np, out=host_out_np)
+        partial = region_host.execute(host_np, out=host_out_np)
+        if combine:
+            combined = torch.tensor([float(partial)], dtype=torch.float64, device="cuda")
+            combine_partial_sums(combined, dist if world > 1 else None)
+            combined.item()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     e2e_value = bytes_per_step_rank * world * e2e_steps / e2e_s / 1e9
     h2d = sum(t.numel() * t.element_size() for t in inputs)
@@ -580,13 +645,13 @@ def main():
             "config": workload.config(world),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": "generated fused elementwise group (NVRTC, sm_100a)",
+                         "kernel": getattr(workload, "kernel", "generated fused elementwise group (NVRTC, sm_100a)"),
                          "algorithmic_bytes_per_launch": bytes_per_step_rank,
                          "avg_launch_ms": launch_ms, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
             "cpu_baseline": cpu_baseline,
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps, "api": "thb_region_execute (host buffers, pinned)"},
-            "gpu_launches": args.steps * 1,
+            "gpu_launches": args.steps * getattr(workload, "launches_per_step", 1),
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)

@@ -306,7 +306,8 @@ uint64_t thb_take_unobserved_errors(char* buffer, uint64_t capacity);
  * device pointers on the region's device; nothing is copied and nothing
  * synchronises. Checked failures latch into the region's error words until
  * thb_region_check_errors reads and clears them. `stream` is a cudaStream_t
- * (NULL = legacy default stream). This is the hot path the benchmark times. */
+ * (NULL = legacy default stream). This is the hot path the benchmark times.
+ * A scalar region output is written to a one-element device buffer. */
 int thb_region_launch(thb_region* region, const thb_abi_arg* args, uint64_t argc,
                       void* output, uint64_t output_count, void* stream,
                       char* failure, uint64_t failure_cap);
@@ -412,6 +413,14 @@ int thb_mlp_buffer(thb_mlp* session, uint32_t which, void** device_pointer, uint
  * the caller keeps it alive while the session uses it. The previous
  * contents are not copied. */
 int thb_mlp_bind(thb_mlp* session, uint32_t which, void* device_pointer);
+/* Data-parallel gradient reduction fused into the weight-gradient GEMM
+ * (THB_MLP_DW1 or THB_MLP_DW2): `multicast` is the NVLink multicast (NVLS)
+ * address of a buffer every rank maps; the GEMM epilogue adds each finished
+ * tile into it with multimem.red, so the switch sums all ranks' gradients into
+ * every rank's copy while the GEMM is still running. The caller zeroes its
+ * copy and synchronises the ranks before the step, and synchronises them again
+ * before reading the sum (apply_sgd). NULL restores the local store. */
+int thb_mlp_bind_reduction(thb_mlp* session, uint32_t which, void* multicast);
 /* CUDA-event timing of the session's GEMM launches, recorded on the stream
  * they are launched on (up to 512 launches between reads). */
 int thb_mlp_enable_timing(thb_mlp* session, int enabled);

@@ -415,22 +415,28 @@ int orc_region_eval(const thb_region_desc* r, const thb_abi_arg* args, uint64_t 
                 status = 1;
                 break;
             }
-            *v = *d0;
+            {
+                /* Scalar operands broadcast (Evaluator.cpp:95-124): the
+                 * result takes the tensor operand's shape. */
+                const value_t* d1 = n->dependency_count > 1 ? &vals[position_of(r, n->dependencies[1])] : NULL;
+                *v = (d0->tensor || !d1) ? *d0 : *d1;
+            }
             v->dtype = n->dtype;
             v->data = malloc((n->dtype == THB_DTYPE_I64 ? 8 : 4) * (v->count ? v->count : 1));
             v->owned = 1;
             for (uint64_t k = 0; k < v->count && status == 0; ++k) {
+                const value_t* d1 = n->dependency_count > 1 ? &vals[position_of(r, n->dependencies[1])] : NULL;
                 if (n->dtype == THB_DTYPE_I64) {
-                    const int64_t a = ((const int64_t*)d0->data)[k];
+                    const int64_t a = d0->tensor ? ((const int64_t*)d0->data)[k] : d0->i;
                     int64_t b = 0, out = 0;
-                    if (n->dependency_count > 1) b = ((const int64_t*)vals[position_of(r, n->dependencies[1])].data)[k];
+                    if (d1) b = d1->tensor ? ((const int64_t*)d1->data)[k] : d1->i;
                     if (checked((int)n->op, a, b, &out)) {
                         set_failure(failure, cap, "TH-SPEC-I64-OVERFLOW");
                         status = 2;
                     }
                     ((int64_t*)v->data)[k] = out;
                 } else {
-                    const float a = ((const float*)d0->data)[k];
+                    const float a = d0->tensor ? ((const float*)d0->data)[k] : d0->f;
                     float out = 0.0f;
                     if (n->op == THB_OP_EXTENSION || n->op == THB_OP_EXTENSION_GRADIENT) {
                         float in[10];
@@ -449,7 +455,7 @@ int orc_region_eval(const thb_region_desc* r, const thb_abi_arg* args, uint64_t 
                     } else if (n->op == THB_OP_RELU) {
                         out = relu(a);
                     } else {
-                        const float b = ((const float*)vals[position_of(r, n->dependencies[1])].data)[k];
+                        const float b = d1->tensor ? ((const float*)d1->data)[k] : d1->f;
                         out = n->op == THB_OP_ADD ? a + b : n->op == THB_OP_SUBTRACT ? a - b : a * b;
                     }
                     ((float*)v->data)[k] = out;

@@ -143,6 +143,7 @@ return z.*y
 }"""
 PICK = "fn pick(x: Tensor<i64,1>, i:i64)->i64{return x[i]}"
 CHAIN = open(os.path.join(ROOT, "oracle", "programs", "f32_chain.th")).read()
+CHAIN_LITERAL = "fn f(x: Tensor<f32,1>) -> Tensor<f32,1> {\nreturn ((x*1.5+0.25).*x - x)*0.5 + x\n}"
 I64_REGION = open(os.path.join(ROOT, "oracle", "programs", "i64_region.th")).read()
 SQUARE_LINEAR = "fn f(x: Tensor<f32,1>) -> Tensor<f32,1> {\nreturn research_square_linear(x)\n}"
 SUMS = """fn rows(A: Tensor<f32,2>) -> Tensor<f32,1> { return sum(A, 1) }
@@ -211,6 +212,9 @@ def main():
     assert s == 0
     arrays["chain_native_cpu"] = out
     fixtures["chain"] = {"groups_fused": groups_of(plan(CHAIN, "f"))}
+    status, value = evaluate(CHAIN_LITERAL, "f", [chain_x])
+    assert status == "ok"
+    arrays["chain_literal_eval"] = value
 
     rng = np.random.default_rng(1)
     ia = rng.integers(-1000, 1001, (64, 96), dtype=np.int64)

@@ -1,0 +1,119 @@
+"""Two-GPU tests (skipped with fewer than two devices): data-parallel MLP
+steps whose gradient reduction is fused into the weight-gradient GEMMs
+(multimem.red into NVLink multicast memory) or done by NCCL all-reduce both
+equal the single-process full-batch step; a row-sharded region equals the
+unsharded one. Each test runs two spawned ranks over NCCL."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def two_gpus():
+    return torch.cuda.is_available() and torch.cuda.device_count() >= 2
+
+
+def _mlp_rank(rank, world, port, mode, out_path):
+    import datetime
+    import sys
+    import torch.distributed as dist
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    import thiran_b200 as thb
+    from thiran_b200.distributed import MulticastGradients, allreduce_gradients
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    batch, d_in, hidden, d_out = 512, 256, 512, 256
+    rng = np.random.default_rng(8)
+    x = rng.standard_normal((batch, d_in)).astype(np.float32)
+    t = rng.standard_normal((batch, d_out)).astype(np.float32)
+    w1 = (rng.uniform(-1, 1, (d_in, hidden)) * 0.08).astype(np.float32)
+    w2 = (rng.uniform(-1, 1, (hidden, d_out)) * 0.08).astype(np.float32)
+    local = batch // world
+    xs = torch.from_numpy(x[rank * local:(rank + 1) * local].copy()).cuda()
+    ts = torch.from_numpy(t[rank * local:(rank + 1) * local].copy()).cuda()
+    s = thb.MlpSession(local, d_in, hidden, d_out, global_batch=batch, device=rank)
+    W1 = s.bind(thb.MLP_W1, torch.empty((d_in, hidden), device="cuda"))
+    W2 = s.bind(thb.MLP_W2, torch.empty((hidden, d_out), device="cuda"))
+    dw1 = s.bind(thb.MLP_DW1, torch.empty((d_in, hidden), device="cuda"))
+    dw2 = s.bind(thb.MLP_DW2, torch.empty((hidden, d_out), device="cuda"))
+    s.set_weights(torch.from_numpy(w1).cuda(), torch.from_numpy(w2).cuda())
+    mc = None
+    if mode == "nvls":
+        mc = MulticastGradients(s, dist)
+        if not mc.available:
+            dist.destroy_process_group()
+            if rank == 0:
+                open(out_path, "w").write("unavailable")
+            return
+        dw1, dw2 = mc.buffers[0][1], mc.buffers[1][1]
+    for _ in range(2):
+        if mc:
+            mc.before_step()
+        s.forward_backward(xs, ts)
+        if mc:
+            mc.after_backward()
+        else:
+            allreduce_gradients([dw1, dw2], dist)
+        s.apply_sgd(0.05)
+    thb.check_device_status(rank)
+    torch.cuda.synchronize()
+    if rank == 0:
+        np.savez(out_path, dw1=dw1.cpu().numpy(), dw2=dw2.cpu().numpy(), w1=W1.cpu().numpy(), w2=W2.cpu().numpy())
+    s.release()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def single_gpu_reference():
+    import thiran_b200 as thb
+    batch, d_in, hidden, d_out = 512, 256, 512, 256
+    rng = np.random.default_rng(8)
+    x = rng.standard_normal((batch, d_in)).astype(np.float32)
+    t = rng.standard_normal((batch, d_out)).astype(np.float32)
+    w1 = (rng.uniform(-1, 1, (d_in, hidden)) * 0.08).astype(np.float32)
+    w2 = (rng.uniform(-1, 1, (hidden, d_out)) * 0.08).astype(np.float32)
+    s = thb.MlpSession(batch, d_in, hidden, d_out)
+    W1 = s.bind(thb.MLP_W1, torch.empty((d_in, hidden), device="cuda"))
+    W2 = s.bind(thb.MLP_W2, torch.empty((hidden, d_out), device="cuda"))
+    dw1 = s.bind(thb.MLP_DW1, torch.empty((d_in, hidden), device="cuda"))
+    dw2 = s.bind(thb.MLP_DW2, torch.empty((hidden, d_out), device="cuda"))
+    s.set_weights(torch.from_numpy(w1).cuda(), torch.from_numpy(w2).cuda())
+    X, T = torch.from_numpy(x).cuda(), torch.from_numpy(t).cuda()
+    for _ in range(2):
+        s.step(X, T, 0.05)
+    torch.cuda.synchronize()
+    return dict(dw1=dw1.cpu().numpy(), dw2=dw2.cpu().numpy(), w1=W1.cpu().numpy(), w2=W2.cpu().numpy())
+
+
+def rel(a, b):
+    return float(np.linalg.norm(a.astype(np.float64) - b) / np.linalg.norm(b))
+
+
+@pytest.mark.skipif(not two_gpus(), reason="needs two GPUs")
+@pytest.mark.parametrize("mode", ["nvls", "nccl"])
+def test_data_parallel_mlp_matches_full_batch(tmp_path, mode):
+    import torch.multiprocessing as mp
+    out = str(tmp_path / f"{mode}.npz")
+    mp.start_processes(_mlp_rank, args=(2, free_port(), mode, out), nprocs=2, join=True, start_method="spawn")
+    if mode == "nvls" and os.path.exists(out) and open(out, "rb").read(11) == b"unavailable":
+        pytest.skip("no NVLink multicast on this system")
+    got = dict(np.load(out))
+    ref = single_gpu_reference()
+    # Same arithmetic, different batch split of the f32 reductions.
+    for k in ("dw1", "dw2"):
+        assert rel(got[k], ref[k]) <= 1e-2, k
+    for k in ("w1", "w2"):
+        assert rel(got[k], ref[k]) <= 1e-4, k

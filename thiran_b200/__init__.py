@@ -165,6 +165,7 @@ SIGNATURES = {
     "thb_mlp_step": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_char_p, C.c_uint64]),
     "thb_mlp_buffer": (C.c_int, [C.c_void_p, C.c_uint32, C.POINTER(C.c_void_p), C.POINTER(C.c_uint64)]),
     "thb_mlp_bind": (C.c_int, [C.c_void_p, C.c_uint32, C.c_void_p]),
+    "thb_mlp_bind_reduction": (C.c_int, [C.c_void_p, C.c_uint32, C.c_void_p]),
     "thb_mlp_enable_timing": (C.c_int, [C.c_void_p, C.c_int]),
     "thb_mlp_read_timing": (C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
     "thb_sum_all_f32_noalloc": (C.c_int, [C.c_int, C.c_void_p, C.c_uint64, C.c_void_p, C.c_void_p, C.c_void_p,
@@ -214,6 +215,12 @@ class MlpSession:
         if lib().thb_mlp_read_timing(self.handle, C.byref(ms), C.byref(n)) != STATUS_OK:
             raise GpuError(STATUS_BACKEND, "GPU-RUNTIME: cannot read timing events")
         return ms.value, int(n.value)
+
+    def bind_reduction(self, which, multicast_ptr):
+        """Fuses the data-parallel reduction of dW1 / dW2 into its GEMM: tiles
+        are added through the NVLink multicast address `multicast_ptr`."""
+        if lib().thb_mlp_bind_reduction(self.handle, which, C.c_void_p(multicast_ptr)) != STATUS_OK:
+            raise GpuError(STATUS_ABI, "GPU-MLP-ARGUMENT: cannot bind the reduction target")
 
     def bind(self, which, tensor):
         """Makes the session use `tensor`'s device memory for buffer `which`."""
@@ -415,14 +422,20 @@ class RegionBuilder:
     def neg(self, a):
         return self._add(OP_NEGATE, *self._like(a), deps=[a])
 
+    def _binary(self, a, b):
+        """dtype and shape of an elementwise result: a scalar operand
+        broadcasts, so the tensor operand decides the shape."""
+        da, sa = self._like(a)
+        return (da, sa) if sa or not self._like(b)[1] else self._like(b)
+
     def add(self, a, b):
-        return self._add(OP_ADD, *self._like(a), deps=[a, b])
+        return self._add(OP_ADD, *self._binary(a, b), deps=[a, b])
 
     def sub(self, a, b):
-        return self._add(OP_SUBTRACT, *self._like(a), deps=[a, b])
+        return self._add(OP_SUBTRACT, *self._binary(a, b), deps=[a, b])
 
     def mul(self, a, b):
-        return self._add(OP_ELEMENT_MULTIPLY, *self._like(a), deps=[a, b])
+        return self._add(OP_ELEMENT_MULTIPLY, *self._binary(a, b), deps=[a, b])
 
     def extension(self, operation: Operation, *args):
         return self._add(OP_EXTENSION, *self._like(args[0]), deps=list(args), extension=operation)
@@ -536,8 +549,8 @@ class RegionSpec:
                 s = [deps[0][0], deps[1][1]]
             elif op in (OP_BROADCAST_TO_SHAPE, OP_REDUCE_TO_SHAPE):
                 s = list(deps[1])
-            else:
-                s = list(deps[0]) if deps else list(n["shape"])
+            else:  # elementwise and row ops: the first tensor operand's shape
+                s = next((list(d) for d in deps if len(d)), list(n["shape"]) if not deps else [])
             shapes[n["id"]] = s
         return [int(e) for e in shapes[self._output]]
 

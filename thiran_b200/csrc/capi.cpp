@@ -481,9 +481,21 @@ int thb_region_launch(thb_region* region, const thb_abi_arg* args, uint64_t argc
         thb_evidence ev{};
         auto inputs = bind(r, args, argc, false, static_cast<cudaStream_t>(stream), ev, nullptr);
         const Node& outNode = r.region().at(r.region().output);
-        if (!outNode.tensor()) fail(Category::Unsupported, "GPU-OUTPUT-SHAPE", "device launch needs a tensor output");
-        r.run(inputs, static_cast<cudaStream_t>(stream), ev, output,
-              [&](const Value& o) { checkOutputCount(o, outputCount, true, output); });
+        auto s = static_cast<cudaStream_t>(stream);
+        Value out = r.run(inputs, s, ev, outNode.tensor() ? output : nullptr,
+                          [&](const Value& o) { checkOutputCount(o, outputCount, true, output); });
+        if (!outNode.tensor()) {
+            // A scalar result (for example a full-tensor Sum) is copied into
+            // the caller's one-element device buffer.
+            const std::size_t w = width(out.dtype);
+            if (out.onDevice)
+                cudaCheck(cudaMemcpyAsync(output, out.data, w, cudaMemcpyDeviceToDevice, s), "cudaMemcpyAsync(scalar)");
+            else
+                cudaCheck(cudaMemcpy(output, out.dtype == DType::I64 ? static_cast<const void*>(&out.i64)
+                                                                     : static_cast<const void*>(&out.f32),
+                                     w, cudaMemcpyHostToDevice),
+                          "cudaMemcpy(scalar)");
+        }
         return THB_STATUS_OK;
     });
 }
@@ -670,6 +682,14 @@ int thb_mlp_read_timing(thb_mlp* s, double* gemmMs, uint64_t* gemmLaunches) {
     *gemmLaunches = s->timer.launches;
     s->timer.used = 0;
     s->timer.launches = 0;
+    return THB_STATUS_OK;
+}
+
+int thb_mlp_bind_reduction(thb_mlp* s, uint32_t which, void* multicast) {
+    if (!s || reinterpret_cast<std::uintptr_t>(multicast) % 16) return THB_STATUS_ABI;
+    if (which == THB_MLP_DW1) s->b.dw1Reduce = static_cast<float*>(multicast);
+    else if (which == THB_MLP_DW2) s->b.dw2Reduce = static_cast<float*>(multicast);
+    else return THB_STATUS_ABI;
     return THB_STATUS_OK;
 }
 

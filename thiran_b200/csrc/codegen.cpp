@@ -120,8 +120,24 @@ void emitBody(std::ostringstream& out, const Region& region, const FusionGroup& 
         out << (i ? ", " : "") << type << " a" << i;
         names[group.inputs[i]] = "a" + std::to_string(i);
     }
+    for (std::size_t i = 0; i < group.scalars.size(); ++i) {
+        out << ", " << type << " s" << i;
+        names[group.scalars[i]] = "s" + std::to_string(i);
+    }
     out << ", thb_u32& flag) {\n";
-    auto operand = [&](std::uint32_t id) { return names.at(region.canonical(id)); };
+    // Tensor operands and runtime scalars are parameters; Float / Integer
+    // literals become exact constants in the generated source.
+    auto operand = [&](std::uint32_t id) {
+        const std::uint32_t c = region.canonical(id);
+        const Node& n = region.at(c);
+        if (n.op == Op::Float && !names.count(c)) return floatLiteral(n.floating);
+        if (n.op == Op::Integer && !names.count(c)) {
+            std::ostringstream lit;
+            lit << "(thb_i64)" << static_cast<unsigned long long>(n.integer) << "ULL";
+            return lit.str();
+        }
+        return names.at(c);
+    };
     for (auto id : group.nodes) {
         const Node& n = region.at(id);
         const std::string v = "v" + std::to_string(id);
@@ -190,9 +206,13 @@ void emitKernels(std::ostringstream& out, const FusionGroup& group, const std::s
         std::ostringstream p;
         p << type << "* __restrict__ out";
         for (std::size_t i = 0; i < k; ++i) p << ", const " << type << "* __restrict__ in" << i;
+        for (std::size_t i = 0; i < group.scalars.size(); ++i) p << ", " << type << " s" << i;
         p << ", thb_u64 n, thb_u32* __restrict__ err";
         return p.str();
     };
+    // Runtime scalars are passed through to every body call.
+    std::string scalarArgs;
+    for (std::size_t i = 0; i < group.scalars.size(); ++i) scalarArgs += "s" + std::to_string(i) + ", ";
     const std::string body = "thb_g" + std::to_string(group.id) + "_body";
 
     out << "extern \"C\" __global__ void __launch_bounds__(" << kBlock << ") " << vectorName << "(" << params() << ") {\n"
@@ -212,20 +232,20 @@ void emitKernels(std::ostringstream& out, const FusionGroup& group, const std::s
         << "            " << packet << " r;\n"
         << "#pragma unroll\n            for (int l = 0; l < " << lanes << "; ++l) r.v[l] = " << body << "(";
     for (std::size_t j = 0; j < k; ++j) out << "x" << j << "[u].v[l], ";
-    out << "flag);\n            thb_store(o + i + u * stride, r);\n        }\n    }\n";
+    out << scalarArgs << "flag);\n            thb_store(o + i + u * stride, r);\n        }\n    }\n";
     // Remainder packets.
     out << "    for (; i < packets; i += stride) {\n";
     for (std::size_t j = 0; j < k; ++j) out << "        const " << packet << " x" << j << " = thb_load(p" << j << " + i);\n";
     out << "        " << packet << " r;\n#pragma unroll\n        for (int l = 0; l < " << lanes << "; ++l) r.v[l] = "
         << body << "(";
     for (std::size_t j = 0; j < k; ++j) out << "x" << j << ".v[l], ";
-    out << "flag);\n        thb_store(o + i, r);\n    }\n";
+    out << scalarArgs << "flag);\n        thb_store(o + i, r);\n    }\n";
     // Tail elements.
     out << "    if (blockIdx.x == 0) {\n"
         << "        const thb_u64 t = packets * " << lanes << " + threadIdx.x;\n"
         << "        if (t < n) out[t] = " << body << "(";
     for (std::size_t j = 0; j < k; ++j) out << "in" << j << "[t], ";
-    out << "flag);\n    }\n"
+    out << scalarArgs << "flag);\n    }\n"
         << "    if (flag) atomicOr(err, flag);\n}\n";
 
     out << "extern \"C\" __global__ void __launch_bounds__(" << kBlock << ") " << scalarName << "(" << params() << ") {\n"
@@ -234,7 +254,7 @@ void emitKernels(std::ostringstream& out, const FusionGroup& group, const std::s
         << "    for (thb_u64 i = (thb_u64)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)\n"
         << "        out[i] = " << body << "(";
     for (std::size_t j = 0; j < k; ++j) out << "in" << j << "[i], ";
-    out << "flag);\n    if (flag) atomicOr(err, flag);\n}\n";
+    out << scalarArgs << "flag);\n    if (flag) atomicOr(err, flag);\n}\n";
 }
 
 std::string cacheDirectory() {

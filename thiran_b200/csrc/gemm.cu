@@ -302,7 +302,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float v[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = epilogueValue<EPI>(__uint_as_float(r[j]), aux[j]);
-                if constexpr (EPI == kEpiF32) {
+                if constexpr (EPI == kEpiRedF32) {
+                    // Reduction through the NVLink switch: the multicast
+                    // address maps the same buffer on every rank; each add
+                    // lands, summed, in all of them.
+                    float* dst = static_cast<float*>(p.c) + grow * p.ldc + col0;
+                    if (full32 && reinterpret_cast<uintptr_t>(dst) % 16 == 0) {
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            asm volatile("multimem.red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(
+                                             dst + 4 * q),
+                                         "f"(v[4 * q]), "f"(v[4 * q + 1]), "f"(v[4 * q + 2]), "f"(v[4 * q + 3])
+                                         : "memory");
+                    } else {
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < p.n)
+                                asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(dst + j), "f"(v[j])
+                                             : "memory");
+                    }
+                } else if constexpr (EPI == kEpiF32) {
                     float* dst = static_cast<float*>(p.c) + grow * p.ldc + col0;
                     if (full32 && reinterpret_cast<uintptr_t>(dst) % 16 == 0) {
 #pragma unroll
@@ -338,6 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbarArrive(&tmemEmpty[acc]);
             if (++acc == 2) { acc = 0; accPhase ^= 1u; }
         }
+        if constexpr (EPI == kEpiRedF32) asm volatile("fence.acq_rel.sys;" ::: "memory");
     }
     __syncthreads();
     if (threadIdx.x == 0 && abortFlag) atomicOr(p.status, kWaitStatus);
@@ -393,6 +412,7 @@ cudaError_t launchEpi(int epi, const CUtensorMap& a, const CUtensorMap& b, const
     case kEpiBf16: return launchTyped<A_MN, B_MN, kEpiBf16>(a, b, p, sm, s);
     case kEpiReluBf16: return launchTyped<A_MN, B_MN, kEpiReluBf16>(a, b, p, sm, s);
     case kEpiMaskBf16: return launchTyped<A_MN, B_MN, kEpiMaskBf16>(a, b, p, sm, s);
+    case kEpiRedF32: return launchTyped<A_MN, B_MN, kEpiRedF32>(a, b, p, sm, s);
     }
     return cudaErrorInvalidValue;
 }
@@ -408,7 +428,9 @@ const char* validate(const Problem& q) {
     if (q.lda < (q.aMajorMN ? q.m : q.k) || q.ldb < (q.bMajorMN ? q.n : q.k)) return "leading dimension too small";
     if (q.ldc < q.n) return "ldc smaller than N";
     if (q.epilogue == kEpiMaskBf16 && (!q.aux || q.ldAux < q.n)) return "mask epilogue needs an auxiliary bf16 matrix";
-    if (q.epilogue < kEpiF32 || q.epilogue > kEpiMaskBf16) return "unknown epilogue";
+    if (q.epilogue < kEpiF32 || q.epilogue > kEpiRedF32) return "unknown epilogue";
+    if (q.epilogue == kEpiRedF32 && (reinterpret_cast<uintptr_t>(q.c) % 16 || q.ldc % 4))
+        return "the multicast reduction target must be 16-byte aligned with ldc a multiple of 4";
     return nullptr;
 }
 

@@ -13,6 +13,8 @@ enum : int {
     kEpiBf16 = 1,      // C (bf16) = acc
     kEpiReluBf16 = 2,  // C (bf16) = max(acc, 0)            (forward ReLU)
     kEpiMaskBf16 = 3,  // C (bf16) = aux > 0 ? acc : 0       (ReLU backward mask, aux bf16 [M][N])
+    kEpiRedF32 = 4,    // C (f32) += acc on every GPU: `c` is an NVLink multicast address and the
+                       // epilogue issues multimem.red.add, so the switch sums all ranks' tiles
 };
 
 struct Problem {

@@ -23,6 +23,10 @@ struct Buffers {
     float* dw2 = nullptr;      // f32 [hidden][out]
     double* lossPartials = nullptr;
     double* lossSum = nullptr; // sum over this rank's batch of (Y - T)^2
+    // Data-parallel gradient reduction fused into the dW GEMMs: NVLink
+    // multicast addresses of the dW buffers (null = store locally).
+    float* dw1Reduce = nullptr;
+    float* dw2Reduce = nullptr;
 };
 
 // Optional CUDA-event timing of the GEMM launches of a step (recorded on the

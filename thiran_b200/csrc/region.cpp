@@ -324,11 +324,18 @@ std::vector<std::string> verifyRegion(const Region& region) {
         case Op::Add: case Op::Subtract: case Op::ElementMultiply: {
             if (!numericTensor(n)) errors.push_back("TRV04 elementwise result is not Tensor<i64/f32,R>");
             const Node* l = dep(0); const Node* r = dep(1);
-            if (n.dependencies.size() != 2 || !l || !r || !numericTensor(*l) || !numericTensor(*r) ||
-                !l->sameType(*r) || !l->sameType(n))
+            // Tensor (x) tensor of one type, or tensor (x) scalar of the same
+            // element type: the scalar broadcasts (Evaluator.cpp:95-124); the
+            // reference's native extractor rejects the scalar form.
+            const bool both = l && r && numericTensor(*l) && numericTensor(*r) && l->sameType(*r) && l->sameType(n);
+            const bool scalarRight = l && r && numericTensor(*l) && r->rank == 0 && r->dtype == l->dtype && l->sameType(n);
+            const bool scalarLeft = l && r && numericTensor(*r) && l->rank == 0 && l->dtype == r->dtype && r->sameType(n);
+            if (n.dependencies.size() != 2 || !(both || scalarRight || scalarLeft))
                 errors.push_back("TRV05 elementwise input type mismatch");
-            if (l && r && (l->knownShapeMismatch(*r) || n.knownShapeMismatch(*l)))
+            if (both && (l->knownShapeMismatch(*r) || n.knownShapeMismatch(*l)))
                 errors.push_back("TRV06 elementwise known shape mismatch");
+            if (scalarRight && n.knownShapeMismatch(*l)) errors.push_back("TRV06 elementwise known shape mismatch");
+            if (scalarLeft && n.knownShapeMismatch(*r)) errors.push_back("TRV06 elementwise known shape mismatch");
             break;
         }
         case Op::Extension: {
@@ -565,7 +572,8 @@ std::vector<FusionGroup> makeGroups(const Region& region, const PlanOptions& opt
                 for (auto d : current.dependencies) {
                     const auto c = region.canonical(d);
                     if (c == tail.id) ++occurrences;
-                    else if (region.position(c) > groupStart) intervening = true;
+                    // Scalars are kernel constants/parameters, not materialised tensors.
+                    else if (region.at(c).tensor() && region.position(c) > groupStart) intervening = true;
                 }
                 extend = oneConsumer && occurrences == 1 && !intervening;
             }
@@ -596,7 +604,10 @@ std::vector<FusionGroup> makeGroups(const Region& region, const PlanOptions& opt
             if (g.kind == GroupKind::Index) continue;
             for (auto d : n.dependencies) {
                 const auto c = region.canonical(d);
-                if (!inside.count(c) && seenInputs.insert(c).second) g.inputs.push_back(c);
+                if (inside.count(c) || !seenInputs.insert(c).second) continue;
+                const Node& operand = region.at(c);
+                if (operand.tensor()) g.inputs.push_back(c);
+                else if (operand.op != Op::Integer && operand.op != Op::Float) g.scalars.push_back(c);
             }
         }
     }

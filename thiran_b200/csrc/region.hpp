@@ -133,6 +133,7 @@ struct FusionGroup {
     GroupKind kind = GroupKind::Elementwise;
     std::vector<std::uint32_t> nodes;
     std::vector<std::uint32_t> inputs;  // canonical external tensor operands, first-use order
+    std::vector<std::uint32_t> scalars; // runtime scalar operands (kernel parameters); literals are constants
     std::uint32_t output = 0;
     DType dtype = DType::F32;
     bool fused = false;

@@ -258,8 +258,9 @@ void* CompiledRegion::slotPointer(std::uint32_t value, std::size_t bytes, thb_ev
     return buffer->ptr;
 }
 
-void CompiledRegion::launchElementwise(const FusionGroup& group, const std::vector<const Value*>& operands, Value& out,
-                                       cudaStream_t stream, thb_evidence& ev) {
+void CompiledRegion::launchElementwise(const FusionGroup& group, const std::vector<const Value*>& operands,
+                                       const std::vector<const Value*>& scalars, Value& out, cudaStream_t stream,
+                                       thb_evidence& ev) {
     const GroupKernel* kernel = nullptr;
     for (const auto& k : kernels_)
         if (k.group == group.id) kernel = &k;
@@ -271,6 +272,8 @@ void CompiledRegion::launchElementwise(const FusionGroup& group, const std::vect
     const unsigned lanes = group.dtype == DType::F32 ? 4 : 2;
     const std::uint64_t work = aligned ? std::max<std::uint64_t>(1, n / lanes) : n;
     const std::uint64_t perBlock = static_cast<std::uint64_t>(kBlock) * (aligned ? kUnroll : 1);
+    // Eight CTAs per SM: about two resident waves of the streaming kernel,
+    // which measured faster than one occupancy-sized persistent wave.
     const std::uint64_t cap = static_cast<std::uint64_t>(info_->smCount) * 8;
     const unsigned blocks = static_cast<unsigned>(std::max<std::uint64_t>(1, std::min(cap, (work + perBlock - 1) / perBlock)));
     std::vector<void*> args;
@@ -281,6 +284,16 @@ void CompiledRegion::launchElementwise(const FusionGroup& group, const std::vect
     std::uint32_t* errorWord = static_cast<std::uint32_t*>(errors_.ptr) + (group.id - 1);
     args.push_back(&outPtr);
     for (auto& p : inPtrs) args.push_back(&p);
+    // Runtime scalar operands, by value, in the group's parameter order.
+    std::vector<std::int64_t> scalarI64(scalars.size());
+    std::vector<float> scalarF32(scalars.size());
+    for (std::size_t i = 0; i < scalars.size(); ++i) {
+        if (scalars[i]->onDevice)
+            fail(Category::Unsupported, "GPU-UNSUPPORTED-OP", "device-computed scalars cannot feed an elementwise chain");
+        scalarI64[i] = scalars[i]->i64;
+        scalarF32[i] = scalars[i]->f32;
+        args.push_back(group.dtype == DType::I64 ? static_cast<void*>(&scalarI64[i]) : static_cast<void*>(&scalarF32[i]));
+    }
     args.push_back(&count);
     args.push_back(&errorWord);
     const void* fn = aligned ? kernel->vectorKernel : kernel->scalarKernel;
@@ -492,9 +505,14 @@ Value CompiledRegion::run(const std::vector<Value>& inputs, cudaStream_t stream,
         case Op::ZeroLike:
             v.shape[0] = dep(0).shape[0]; v.shape[1] = dep(0).shape[1]; break;
         case Op::Add: case Op::Subtract: case Op::ElementMultiply: case Op::Extension: case Op::ExtensionGradient: {
-            const Value& a = dep(0);
-            for (std::size_t k = 1; k < n.dependencies.size(); ++k) {
+            // The result takes the first tensor operand's shape; scalar
+            // operands broadcast.
+            std::size_t first = 0;
+            while (first + 1 < n.dependencies.size() && !dep(first).tensor) ++first;
+            const Value& a = dep(first);
+            for (std::size_t k = 0; k < n.dependencies.size(); ++k) {
                 const Value& b = dep(k);
+                if (!b.tensor) continue;
                 if (b.rank != a.rank || b.shape[0] != a.shape[0] || b.shape[1] != a.shape[1])
                     fail(Category::Unsupported, "GPU-RUNTIME-SHAPE",
                          "runtime fused elementwise inputs require equal dtype and shape");
@@ -633,7 +651,9 @@ Value CompiledRegion::run(const std::vector<Value>& inputs, cudaStream_t stream,
             if (group->kind == GroupKind::Elementwise) {
                 std::vector<const Value*> operands;
                 for (auto id : group->inputs) operands.push_back(&values.at(id));
-                launchElementwise(*group, operands, out, stream, ev);
+                std::vector<const Value*> scalars;
+                for (auto id : group->scalars) scalars.push_back(&values.at(id));
+                launchElementwise(*group, operands, scalars, out, stream, ev);
             } else if (group->kind == GroupKind::Kernel) {
                 std::vector<const Value*> operands;
                 for (auto d : n.dependencies) operands.push_back(&values.at(region_.canonical(d)));

@@ -126,8 +126,9 @@ public:
     Lane& lane(std::size_t k);
 
 private:
-    void launchElementwise(const FusionGroup&, const std::vector<const Value*>& operands, Value& out,
-                           cudaStream_t stream, thb_evidence& evidence);
+    void launchElementwise(const FusionGroup&, const std::vector<const Value*>& operands,
+                           const std::vector<const Value*>& scalars, Value& out, cudaStream_t stream,
+                           thb_evidence& evidence);
     void launchReduction(const FusionGroup&, const Value& operand, Value& out, cudaStream_t stream,
                          thb_evidence& evidence);
     void launchKernel(const FusionGroup&, const std::vector<const Value*>& operands, Value& out,

@@ -110,6 +110,23 @@ def f32_chain(n=None):
     return b.build(y)
 
 
+def f32_chain_literal(n=None):
+    """fn f(x: Tensor<f32,1>) -> Tensor<f32,1> { return ((x*1.5+0.25).*x - x)*0.5 + x }
+    in its literal form: scalar constants broadcast inside the chain. The
+    reference runs this only in its Evaluator (its native extractor rejects
+    tensor-scalar operands); here it is one fused kernel with the constants
+    compiled in."""
+    b = RegionBuilder("f")
+    x = b.input(F32, [n])
+    t = b.mul(b.alias(x), b.float(1.5))
+    t = b.add(t, b.float(0.25))
+    t = b.mul(t, b.alias(x))
+    t = b.sub(t, b.alias(x))
+    t = b.mul(t, b.float(0.5))
+    t = b.add(t, b.alias(x))
+    return b.build(t)
+
+
 def i64_region(rows=None, cols=None):
     """fn f(a,b: Tensor<i64,2>) { let s = a + b; let m = s .* a; return m - b }"""
     b = RegionBuilder("f")
