@@ -200,24 +200,27 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
     loss = session.bind(thb.MLP_LOSS_SUM, torch.zeros(2, dtype=torch.float64, device="cuda"))
     session.set_weights(w1, w2, s)
     lr = 1e-3
-    multicast = None
-    if world > 1 and args.dp_collective == "nvls":
-        from thiran_b200.distributed import MulticastGradients
+    fused = None
+    if world > 1 and args.dp_collective != "nccl":
+        from thiran_b200.distributed import FusedGradientAllReduce
+        mode = {"fused": None, "fused-peer": "peer", "fused-switch": "switch"}[args.dp_collective]
         with torch.cuda.stream(stream):
-            multicast = MulticastGradients(session, dist)
-        if not multicast.available:
-            multicast = None
-    collective = ("fused GEMM epilogue multimem.red into NVLS multicast buffers" if multicast
-                  else "NCCL all-reduce of dW1+dW2" if world > 1 else None)
+            fused = FusedGradientAllReduce(session, dist, mode=mode)
+        if not fused.available:
+            fused = None
+    collective = None
+    if fused:
+        collective = ("all-reduce fused into the dW GEMMs: per-tile announce, owner rank sums "
+                      + ("with NVLink peer loads and stores" if fused.mode == "peer"
+                         else "in NVSwitch (multimem.ld_reduce + multimem.st)"))
+    elif world > 1:
+        collective = "NCCL all-reduce of dW1+dW2"
 
     def step():
-        if multicast:
-            with torch.cuda.stream(stream):
-                multicast.before_step()
         session.forward_backward(x, t, s)
-        if multicast:
+        if fused:
             with torch.cuda.stream(stream):
-                multicast.after_backward()
+                fused.after_backward()
         elif world > 1:
             with torch.cuda.stream(stream):
                 dist.all_reduce(dw1)
@@ -511,9 +514,9 @@ def main():
     p.add_argument("--workload", default="i64_region", choices=sorted(WORKLOADS))
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--dp-collective", default="nvls", choices=["nvls", "nccl"],
-                   help="MLP data-parallel gradient reduction: fused into the dW GEMMs through NVLink "
-                        "multicast (falls back to NCCL when unsupported) or NCCL all-reduce")
+    p.add_argument("--dp-collective", default="fused", choices=["fused", "fused-peer", "fused-switch", "nccl"],
+                   help="MLP data-parallel gradient reduction: fused into the dW GEMMs (peer loads/stores at "
+                        "2 ranks, in-switch from 3; or forced), or NCCL all-reduce after the backward pass")
     p.add_argument("--shrink", type=int, default=1,
                    help="divide the leading extent (small cases for profiler captures; not a bench line)")
     args = p.parse_args()

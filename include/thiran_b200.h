@@ -413,14 +413,28 @@ int thb_mlp_buffer(thb_mlp* session, uint32_t which, void** device_pointer, uint
  * the caller keeps it alive while the session uses it. The previous
  * contents are not copied. */
 int thb_mlp_bind(thb_mlp* session, uint32_t which, void* device_pointer);
-/* Data-parallel gradient reduction fused into the weight-gradient GEMM
- * (THB_MLP_DW1 or THB_MLP_DW2): `multicast` is the NVLink multicast (NVLS)
- * address of a buffer every rank maps; the GEMM epilogue adds each finished
- * tile into it with multimem.red, so the switch sums all ranks' gradients into
- * every rank's copy while the GEMM is still running. The caller zeroes its
- * copy and synchronises the ranks before the step, and synchronises them again
- * before reading the sum (apply_sgd). NULL restores the local store. */
-int thb_mlp_bind_reduction(thb_mlp* session, uint32_t which, void* multicast);
+/* Data-parallel gradient all-reduce fused into the weight-gradient GEMM
+ * (THB_MLP_DW1 or THB_MLP_DW2) over NVLink. `peers[k]` is rank k's dW
+ * buffer as mapped on this GPU (peer access or symmetric memory; peers[rank]
+ * becomes the session's dW buffer) and `flag_peers[k]` rank k's
+ * thb_mlp_reduction_flag_words() zeroed u32 signal words, for k < world <= 8.
+ * Each finished dW tile is stored locally and announced to its owner rank,
+ * whose reducer warps sum it over all ranks and write the total into every
+ * rank's dW while later tiles still compute: with plain NVLink loads and
+ * stores (summed in rank order) when `multicast` is NULL, or inside NVSwitch
+ * (multimem.ld_reduce / multimem.st) through `multicast`, the NVLS multicast
+ * address of the dW buffers. Waits on other ranks are bounded: on expiry the
+ * status word gets bit 4 (thb_device_check_status) and the step's gradients
+ * are incomplete. The caller synchronises the ranks after forward_backward
+ * and before reading dW (apply_sgd); every rank binds the same way and runs
+ * the same steps. NULL `peers` restores the local store. Binding restarts the
+ * step count the signal words are checked against, so they must be zero again
+ * on every rank. */
+int thb_mlp_bind_reduction(thb_mlp* session, uint32_t which, void* const* peers, void* multicast,
+                           uint32_t* const* flag_peers, uint32_t rank, uint32_t world);
+/* Signal words thb_mlp_bind_reduction needs for `which` (0 for an unknown
+ * buffer or session). */
+uint64_t thb_mlp_reduction_flag_words(thb_mlp* session, uint32_t which);
 /* CUDA-event timing of the session's GEMM launches, recorded on the stream
  * they are launched on (up to 512 launches between reads). */
 int thb_mlp_enable_timing(thb_mlp* session, int enabled);

@@ -1,8 +1,8 @@
 """Two-GPU tests (skipped with fewer than two devices): data-parallel MLP
-steps whose gradient reduction is fused into the weight-gradient GEMMs
-(multimem.red into NVLink multicast memory) or done by NCCL all-reduce both
-equal the single-process full-batch step; a row-sharded region equals the
-unsharded one. Each test runs two spawned ranks over NCCL."""
+steps whose gradient all-reduce is fused into the weight-gradient GEMMs (peer
+loads/stores or in-switch reduction over NVLink) or done by NCCL after the
+backward pass equal the single-process full-batch step. Each test runs two
+spawned ranks over NCCL."""
 import os
 import socket
 
@@ -30,7 +30,7 @@ def _mlp_rank(rank, world, port, mode, out_path):
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, root)
     import thiran_b200 as thb
-    from thiran_b200.distributed import MulticastGradients, allreduce_gradients
+    from thiran_b200.distributed import FusedGradientAllReduce, allreduce_gradients
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
@@ -51,17 +51,15 @@ def _mlp_rank(rank, world, port, mode, out_path):
     dw2 = s.bind(thb.MLP_DW2, torch.empty((hidden, d_out), device="cuda"))
     s.set_weights(torch.from_numpy(w1).cuda(), torch.from_numpy(w2).cuda())
     mc = None
-    if mode == "nvls":
-        mc = MulticastGradients(s, dist)
+    if mode != "nccl":
+        mc = FusedGradientAllReduce(s, dist, mode=mode)
         if not mc.available:
             dist.destroy_process_group()
             if rank == 0:
                 open(out_path, "w").write("unavailable")
             return
         dw1, dw2 = mc.buffers[0][1], mc.buffers[1][1]
-    for _ in range(2):
-        if mc:
-            mc.before_step()
+    for _ in range(3):
         s.forward_backward(xs, ts)
         if mc:
             mc.after_backward()
@@ -92,7 +90,7 @@ def single_gpu_reference():
     dw2 = s.bind(thb.MLP_DW2, torch.empty((hidden, d_out), device="cuda"))
     s.set_weights(torch.from_numpy(w1).cuda(), torch.from_numpy(w2).cuda())
     X, T = torch.from_numpy(x).cuda(), torch.from_numpy(t).cuda()
-    for _ in range(2):
+    for _ in range(3):
         s.step(X, T, 0.05)
     torch.cuda.synchronize()
     return dict(dw1=dw1.cpu().numpy(), dw2=dw2.cpu().numpy(), w1=W1.cpu().numpy(), w2=W2.cpu().numpy())
@@ -103,12 +101,12 @@ def rel(a, b):
 
 
 @pytest.mark.skipif(not two_gpus(), reason="needs two GPUs")
-@pytest.mark.parametrize("mode", ["nvls", "nccl"])
+@pytest.mark.parametrize("mode", ["peer", "switch", "nccl"])
 def test_data_parallel_mlp_matches_full_batch(tmp_path, mode):
     import torch.multiprocessing as mp
     out = str(tmp_path / f"{mode}.npz")
     mp.start_processes(_mlp_rank, args=(2, free_port(), mode, out), nprocs=2, join=True, start_method="spawn")
-    if mode == "nvls" and os.path.exists(out) and open(out, "rb").read(11) == b"unavailable":
+    if os.path.exists(out) and open(out, "rb").read(11) == b"unavailable":
         pytest.skip("no NVLink multicast on this system")
     got = dict(np.load(out))
     ref = single_gpu_reference()

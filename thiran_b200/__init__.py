@@ -165,7 +165,9 @@ SIGNATURES = {
     "thb_mlp_step": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_char_p, C.c_uint64]),
     "thb_mlp_buffer": (C.c_int, [C.c_void_p, C.c_uint32, C.POINTER(C.c_void_p), C.POINTER(C.c_uint64)]),
     "thb_mlp_bind": (C.c_int, [C.c_void_p, C.c_uint32, C.c_void_p]),
-    "thb_mlp_bind_reduction": (C.c_int, [C.c_void_p, C.c_uint32, C.c_void_p]),
+    "thb_mlp_bind_reduction": (C.c_int, [C.c_void_p, C.c_uint32, C.POINTER(C.c_void_p), C.c_void_p,
+                                         C.POINTER(C.c_void_p), C.c_uint32, C.c_uint32]),
+    "thb_mlp_reduction_flag_words": (C.c_uint64, [C.c_void_p, C.c_uint32]),
     "thb_mlp_enable_timing": (C.c_int, [C.c_void_p, C.c_int]),
     "thb_mlp_read_timing": (C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
     "thb_sum_all_f32_noalloc": (C.c_int, [C.c_int, C.c_void_p, C.c_uint64, C.c_void_p, C.c_void_p, C.c_void_p,
@@ -216,11 +218,23 @@ class MlpSession:
             raise GpuError(STATUS_BACKEND, "GPU-RUNTIME: cannot read timing events")
         return ms.value, int(n.value)
 
-    def bind_reduction(self, which, multicast_ptr):
-        """Fuses the data-parallel reduction of dW1 / dW2 into its GEMM: tiles
-        are added through the NVLink multicast address `multicast_ptr`."""
-        if lib().thb_mlp_bind_reduction(self.handle, which, C.c_void_p(multicast_ptr)) != STATUS_OK:
+    def bind_reduction(self, which, peer_ptrs, flag_peer_ptrs, rank, world, multicast_ptr=None):
+        """Fuses the data-parallel all-reduce of dW1 / dW2 into its GEMM
+        (thb_mlp_bind_reduction): `peer_ptrs[k]` / `flag_peer_ptrs[k]` are
+        rank k's dW buffer and zeroed signal words as mapped on this GPU;
+        `multicast_ptr` (NVLS address of the dW buffers) selects the in-switch
+        reduction. `peer_ptrs=None` restores the local store."""
+        peers = flags = None
+        if peer_ptrs is not None:
+            peers = (C.c_void_p * len(peer_ptrs))(*peer_ptrs)
+            flags = (C.c_void_p * len(flag_peer_ptrs))(*flag_peer_ptrs)
+        if lib().thb_mlp_bind_reduction(self.handle, which, peers, C.c_void_p(multicast_ptr), flags, rank,
+                                        world) != STATUS_OK:
             raise GpuError(STATUS_ABI, "GPU-MLP-ARGUMENT: cannot bind the reduction target")
+
+    def reduction_flag_words(self, which):
+        """Number of u32 signal words bind_reduction needs for `which`."""
+        return int(lib().thb_mlp_reduction_flag_words(self.handle, which))
 
     def bind(self, which, tensor):
         """Makes the session use `tensor`'s device memory for buffer `which`."""

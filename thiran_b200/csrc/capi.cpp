@@ -21,6 +21,7 @@ struct thb_mlp {
     int smCount = 148;
     thb::mlp::Buffers b;
     thb::mlp::GemmTimer timer;
+    std::uint32_t reduceEpoch = 0;  // forward/backward passes since the all-reduce was bound
     std::vector<std::unique_ptr<thb::DeviceBuffer>> owned;
     ~thb_mlp() {
         for (auto& e : timer.events)
@@ -618,6 +619,10 @@ int thb_mlp_forward_backward(thb_mlp* s, const float* x, const float* t, void* s
         if ((reinterpret_cast<std::uintptr_t>(x) | reinterpret_cast<std::uintptr_t>(t)) % 16)
             fail(Category::Validation, "GPU-MLP-ARGUMENT", "x and t must be 16-byte aligned");
         useDevice(s->device);
+        // Each step's announcements raise every signal word by `world`.
+        ++s->reduceEpoch;
+        s->b.dw1Reduce.target = s->b.dw1Reduce.world * s->reduceEpoch;
+        s->b.dw2Reduce.target = s->b.dw2Reduce.world * s->reduceEpoch;
         cudaCheck(mlp::forwardBackward(s->b, x, t, s->smCount, deviceStatus(s->device), static_cast<cudaStream_t>(stream),
                                        &s->timer),
                   "MLP forward/backward");
@@ -685,12 +690,36 @@ int thb_mlp_read_timing(thb_mlp* s, double* gemmMs, uint64_t* gemmLaunches) {
     return THB_STATUS_OK;
 }
 
-int thb_mlp_bind_reduction(thb_mlp* s, uint32_t which, void* multicast) {
-    if (!s || reinterpret_cast<std::uintptr_t>(multicast) % 16) return THB_STATUS_ABI;
-    if (which == THB_MLP_DW1) s->b.dw1Reduce = static_cast<float*>(multicast);
-    else if (which == THB_MLP_DW2) s->b.dw2Reduce = static_cast<float*>(multicast);
-    else return THB_STATUS_ABI;
+int thb_mlp_bind_reduction(thb_mlp* s, uint32_t which, void* const* peers, void* multicast, uint32_t* const* flagPeers,
+                           uint32_t rank, uint32_t world) {
+    if (!s || (which != THB_MLP_DW1 && which != THB_MLP_DW2)) return THB_STATUS_ABI;
+    thb::gemm::AllReduce r;
+    if (peers) {
+        if (!flagPeers || world == 0 || world > static_cast<uint32_t>(thb::gemm::kMaxRanks) || rank >= world ||
+            reinterpret_cast<std::uintptr_t>(multicast) % 16)
+            return THB_STATUS_ABI;
+        for (uint32_t k = 0; k < world; ++k) {
+            if (!peers[k] || !flagPeers[k] || reinterpret_cast<std::uintptr_t>(peers[k]) % 16 ||
+                reinterpret_cast<std::uintptr_t>(flagPeers[k]) % 4)
+                return THB_STATUS_ABI;
+            r.cPeers[k] = peers[k];
+            r.flagsPeers[k] = flagPeers[k];
+        }
+        r.cMulticast = multicast;
+        r.rank = rank;
+        r.world = world;
+        (which == THB_MLP_DW1 ? s->b.dw1 : s->b.dw2) = static_cast<float*>(peers[rank]);
+    }
+    (which == THB_MLP_DW1 ? s->b.dw1Reduce : s->b.dw2Reduce) = r;
+    s->reduceEpoch = 0;  // fresh (zeroed) signal words
     return THB_STATUS_OK;
+}
+
+uint64_t thb_mlp_reduction_flag_words(thb_mlp* s, uint32_t which) {
+    if (!s) return 0;
+    if (which == THB_MLP_DW1) return 4 * thb::gemm::tileCount(s->b.in, s->b.hidden);
+    if (which == THB_MLP_DW2) return 4 * thb::gemm::tileCount(s->b.hidden, s->b.out);
+    return 0;
 }
 
 int thb_mlp_bind(thb_mlp* s, uint32_t which, void* pointer) {

@@ -11,10 +11,12 @@
 //   warp 1      TMEM owner (alloc/dealloc 512 columns) and MMA issuer (one
 //               lane): 4 x tcgen05.mma (M=128, N=256, K=16) per stage
 //   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, fused op, stores
+//   warps 6..9  (fused all-reduce only) reducers: sum the tiles this rank
+//               owns over all ranks and write the totals to every rank
 // Two TMEM accumulators (2 x 256 columns) let the epilogue of tile i overlap
-// the MMAs of tile i+1. Every mbarrier wait is bounded: on expiry the CTA
-// raises bit 4 of the status word, drains its copies and MMAs, frees TMEM and
-// returns.
+// the MMAs of tile i+1. Every wait (mbarrier, tile queue, other ranks'
+// signal words) is bounded: on expiry the CTA raises bit 4 of the status
+// word, drains its copies and MMAs, frees TMEM and returns.
 //
 // The reference's only matmul is its Evaluator's sequential f32 triple loop
 // (src/semantic/v0/Evaluator.cpp:125-154); reverse-mode rules dA = dZ B^T,
@@ -34,6 +36,8 @@ namespace {
 
 constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
 constexpr int kThreads = 192;
+// The fused all-reduce adds 4 reducer warps (warps 6..9).
+constexpr int threadsFor(int epilogue) { return epilogue == kEpiAllReduceF32 ? kThreads + 128 : kThreads; }
 constexpr uint32_t kABytes = kBM * kBK * 2;  // 16 KB
 constexpr uint32_t kBBytes = kBN * kBK * 2;  // 32 KB
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
@@ -53,8 +57,9 @@ __device__ __forceinline__ void mbarExpect(uint64_t* b, uint32_t bytes) {
 __device__ __forceinline__ void mbarArrive(uint64_t* b) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem(b)) : "memory");
 }
-// True when the phase with parity `parity` has completed; false on timeout.
-__device__ __forceinline__ bool mbarWait(uint64_t* b, uint32_t parity) {
+// True when the phase with parity `parity` has completed; false on timeout,
+// or as soon as `abort` (when given) reads non-zero.
+__device__ __forceinline__ bool mbarWait(uint64_t* b, uint32_t parity, const volatile int* abort = nullptr) {
     const uint32_t addr = smem(b);
     for (uint64_t spin = 0; spin < kSpinLimit; ++spin) {
         uint32_t done;
@@ -64,6 +69,7 @@ __device__ __forceinline__ bool mbarWait(uint64_t* b, uint32_t parity) {
             : "r"(addr), "r"(parity)
             : "memory");
         if (done) return true;
+        if (abort && (spin & 255u) == 255u && *abort) return false;
     }
     return false;
 }
@@ -134,6 +140,12 @@ struct Params {
     uint64_t ldAux;
     void* c2;  // optional f32 copy of the epilogue result
     uint32_t* status;
+    uint32_t grid;  // persistent CTAs; CTA g takes tiles g, g + grid, ...
+    // kEpiAllReduceF32
+    float* cMc;                     // switch mode when non-null
+    float* cPeers[kMaxRanks];       // peer mode
+    uint32_t* flagsPeers[kMaxRanks];
+    uint32_t rank, world, target;
 };
 
 __device__ __forceinline__ void tileCoords(uint32_t tile, const Params& p, uint32_t& mb, uint32_t& nb) {
@@ -154,13 +166,216 @@ __device__ __forceinline__ float epilogueValue(float acc, float aux) {
     return acc;
 }
 
+// ---- fused all-reduce (kEpiAllReduceF32) ----
+constexpr uint32_t kNoTile = 0xffffffffu;
+constexpr uint64_t kSignalSpinLimit = 1ull << 21;  // polls of ~0.1-1 us each
+
+// Owned tiles pass from an epilogue warp to the reducer warp of the same TMEM
+// quadrant through a small ring in shared memory (lane 0 of each side; the
+// slot is written before the head moves).
+constexpr uint32_t kQueueDepth = 4;
+constexpr uint64_t kQueueSpinLimit = 1ull << 27;  // polls of >= 128 ns: > 15 s
+struct TileQueue {
+    uint32_t slot[kQueueDepth];
+    uint32_t head, tail;
+};
+
+__device__ __forceinline__ bool pushTile(TileQueue& q, uint32_t tile, uint32_t lane, const volatile int* abort) {
+    uint32_t ok = 0;
+    if (lane == 0) {
+        volatile uint32_t* head = &q.head;
+        volatile uint32_t* tail = &q.tail;
+        const uint32_t h = *head;
+        for (uint64_t spin = 0; spin < kQueueSpinLimit && !*abort; ++spin) {
+            if (h - *tail < kQueueDepth) {
+                ok = 1;
+                break;
+            }
+            __nanosleep(128);
+        }
+        if (ok) {
+            reinterpret_cast<volatile uint32_t*>(q.slot)[h % kQueueDepth] = tile;
+            __threadfence_block();
+            *head = h + 1;
+        }
+    }
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+// Next tile of the queue; kNoTile once the epilogue is done. A wait that runs
+// out or sees the CTA abort sets `abort` and ends the reducer.
+__device__ __forceinline__ uint32_t popTile(TileQueue& q, uint32_t lane, volatile int* abort) {
+    uint32_t tile = kNoTile;
+    if (lane == 0) {
+        volatile uint32_t* head = &q.head;
+        volatile uint32_t* tail = &q.tail;
+        const uint32_t t = *tail;
+        bool got = false;
+        for (uint64_t spin = 0; spin < kQueueSpinLimit && !*abort; ++spin) {
+            if (*head != t) {
+                __threadfence_block();
+                tile = reinterpret_cast<volatile uint32_t*>(q.slot)[t % kQueueDepth];
+                *tail = t + 1;
+                got = true;
+                break;
+            }
+            __nanosleep(128);
+        }
+        if (!got) *abort = 1;
+    }
+    return __shfl_sync(0xffffffffu, tile, 0);
+}
+
+// Owner rank of a tile: alternates along each CTA's tile sequence and across
+// neighbouring CTAs, so every CTA reduces about 1/world of its tiles.
+__device__ __forceinline__ uint32_t tileOwner(const Params& p, uint32_t tile) {
+    return (tile % p.grid + tile / p.grid) % p.world;
+}
+
+// Announces this warp's 32 rows of `tile` to the tile's owner rank. All
+// lanes' stores of the rows precede the announcement (warp barrier, then a
+// system-scope fence and a release add by lane 0 on the owner's word).
+__device__ __forceinline__ void announceRows(const Params& p, uint32_t tile, uint32_t quadrant, uint32_t lane) {
+    __syncwarp();
+    if (lane == 0) {
+        uint32_t* word = p.flagsPeers[tileOwner(p, tile)] + tile * 4u + quadrant;
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(word), "r"(1u) : "memory");
+    }
+}
+
+// Lane 0 polls this rank's signal word until every rank has announced
+// (wrap-safe compare); false after the poll limit or once another warp of
+// the CTA has aborted.
+__device__ __forceinline__ bool awaitRows(const Params& p, uint32_t tile, uint32_t quadrant, uint32_t lane,
+                                          const volatile int* abort) {
+    uint32_t ok = 1;
+    if (lane == 0) {
+        ok = 0;
+        const uint32_t* word = p.flagsPeers[p.rank] + tile * 4u + quadrant;
+        for (uint64_t spin = 0; spin < kSignalSpinLimit && !*abort; ++spin) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(word) : "memory");
+            if (static_cast<int32_t>(v - p.target) >= 0) {
+                ok = 1;
+                break;
+            }
+            __nanosleep(128);
+        }
+    }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    __syncwarp();
+    return ok != 0;
+}
+
+// Switch mode, full-width rows: the switch sums 16-byte vectors over all
+// ranks (multimem.ld_reduce) and writes the totals to all (multimem.st).
+// Lane takes vectors lane and lane + 32 of 8 rows per round: 16 in flight.
+__device__ __forceinline__ void switchReduceRows(float* base, uint64_t ldc, uint32_t rows, uint32_t lane) {
+    for (uint32_t r0 = 0; r0 < rows; r0 += 8) {
+        float4 v[16];
+#pragma unroll
+        for (uint32_t i = 0; i < 16; ++i) {
+            const uint32_t r = r0 + i / 2;
+            if (r < rows) {
+                const float* src = base + r * ldc + 4u * (lane + 32u * (i % 2));
+                asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+                             : "=f"(v[i].x), "=f"(v[i].y), "=f"(v[i].z), "=f"(v[i].w)
+                             : "l"(src)
+                             : "memory");
+            }
+        }
+#pragma unroll
+        for (uint32_t i = 0; i < 16; ++i) {
+            const uint32_t r = r0 + i / 2;
+            if (r < rows) {
+                float* dst = base + r * ldc + 4u * (lane + 32u * (i % 2));
+                asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "f"(v[i].x),
+                             "f"(v[i].y), "f"(v[i].z), "f"(v[i].w)
+                             : "memory");
+            }
+        }
+    }
+}
+
+// Peer mode, full-width rows: every rank's vectors are read over NVLink
+// (L2-only loads), summed in rank order (so all ranks get the same bits) and
+// stored to every rank. 8 vectors per lane per round.
+__device__ __forceinline__ void peerReduceRows(const Params& p, uint64_t offset, uint32_t rows, uint32_t lane) {
+    for (uint32_t r0 = 0; r0 < rows; r0 += 4) {
+        float4 acc[8];
+#pragma unroll
+        for (uint32_t i = 0; i < 8; ++i) acc[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (uint32_t k = 0; k < p.world; ++k) {
+            const float* src = p.cPeers[k] + offset;
+            float4 w[8];
+#pragma unroll
+            for (uint32_t i = 0; i < 8; ++i) {
+                const uint32_t r = r0 + i / 2;
+                if (r < rows) w[i] = __ldcg(reinterpret_cast<const float4*>(src + r * p.ldc + 4u * (lane + 32u * (i % 2))));
+            }
+#pragma unroll
+            for (uint32_t i = 0; i < 8; ++i) {
+                acc[i].x = __fadd_rn(acc[i].x, w[i].x);
+                acc[i].y = __fadd_rn(acc[i].y, w[i].y);
+                acc[i].z = __fadd_rn(acc[i].z, w[i].z);
+                acc[i].w = __fadd_rn(acc[i].w, w[i].w);
+            }
+        }
+        for (uint32_t k = 0; k < p.world; ++k) {
+            float* dst = p.cPeers[k] + offset;
+#pragma unroll
+            for (uint32_t i = 0; i < 8; ++i) {
+                const uint32_t r = r0 + i / 2;
+                if (r < rows) __stcg(reinterpret_cast<float4*>(dst + r * p.ldc + 4u * (lane + 32u * (i % 2))), acc[i]);
+            }
+        }
+    }
+}
+
+// Sums this warp's 32 rows of an owned tile over all ranks and writes the
+// totals to every rank, once all ranks have announced them. Ragged edge
+// tiles go element by element.
+__device__ __forceinline__ bool reduceRows(const Params& p, uint32_t tile, uint32_t quadrant, uint32_t lane,
+                                           const volatile int* abort) {
+    if (!awaitRows(p, tile, quadrant, lane, abort)) return false;
+    uint32_t mb, nb;
+    tileCoords(tile, p, mb, nb);
+    const uint64_t row0 = static_cast<uint64_t>(mb) * kBM + quadrant * 32u;
+    const uint64_t col0 = static_cast<uint64_t>(nb) * kBN;
+    if (row0 >= p.m) return true;
+    const uint32_t rows = p.m - row0 < 32 ? static_cast<uint32_t>(p.m - row0) : 32u;
+    const uint32_t cols = p.n - col0 < kBN ? static_cast<uint32_t>(p.n - col0) : kBN;
+    const uint64_t offset = row0 * p.ldc + col0;
+    if (cols == kBN) {
+        if (p.cMc) switchReduceRows(p.cMc + offset, p.ldc, rows, lane);
+        else peerReduceRows(p, offset, rows, lane);
+        return true;
+    }
+    for (uint32_t r = 0; r < rows; ++r)
+        for (uint32_t c = lane; c < cols; c += 32) {
+            const uint64_t at = offset + r * p.ldc + c;
+            if (p.cMc) {
+                float x;
+                asm volatile("multimem.ld_reduce.relaxed.sys.global.add.f32 %0, [%1];" : "=f"(x) : "l"(p.cMc + at) : "memory");
+                asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(p.cMc + at), "f"(x) : "memory");
+            } else {
+                float x = 0.0f;
+                for (uint32_t k = 0; k < p.world; ++k) x = __fadd_rn(x, __ldcg(p.cPeers[k] + at));
+                for (uint32_t k = 0; k < p.world; ++k) __stcg(p.cPeers[k] + at, x);
+            }
+        }
+    return true;
+}
+
 template <bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(threadsFor(EPI), 1)
     gemmKernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, const Params p) {
     extern __shared__ uint8_t dynamicSmem[];
     __shared__ __align__(8) uint64_t full[kStages], empty[kStages], tmemFull[2], tmemEmpty[2], mmaDone;
     __shared__ uint32_t tmemSlot;
     __shared__ volatile int abortFlag;
+    __shared__ TileQueue queues[4];  // kEpiAllReduceF32: one per TMEM quadrant
 
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dynamicSmem) + 1023) & ~uintptr_t(1023));
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -168,6 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         abortFlag = 0;
+        for (auto& q : queues) q.head = q.tail = 0;
         for (int s = 0; s < kStages; ++s) {
             mbarInit(&full[s], 1);
             mbarInit(&empty[s], 1);
@@ -199,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t mb, nb;
             tileCoords(tile, p, mb, nb);
             for (uint32_t kb = 0; kb < p.kBlocks; ++kb) {
-                if (!mbarWait(&empty[stage], phase ^ 1u)) { abortFlag = 1; break; }
+                if (!mbarWait(&empty[stage], phase ^ 1u, &abortFlag)) { abortFlag = 1; break; }
                 uint8_t* a = base + stage * kStageBytes;
                 uint8_t* b = a + kABytes;
                 mbarExpect(&full[stage], kStageBytes);
@@ -232,12 +448,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr uint32_t idesc = instrDesc<A_MN, B_MN>();
         uint32_t stage = 0, phase = 0, acc = 0, accPhase = 0;
         for (uint32_t tile = blockIdx.x; tile < tiles && !abortFlag; tile += gridDim.x) {
-            if (!mbarWait(&tmemEmpty[acc], accPhase ^ 1u)) { abortFlag = 1; break; }
+            if (!mbarWait(&tmemEmpty[acc], accPhase ^ 1u, &abortFlag)) { abortFlag = 1; break; }
             fenceAfter();
             const uint32_t d = tmemBase + acc * kBN;
             bool ok = true;
             for (uint32_t kb = 0; kb < p.kBlocks; ++kb) {
-                if (!mbarWait(&full[stage], phase)) { abortFlag = 1; ok = false; break; }
+                if (!mbarWait(&full[stage], phase, &abortFlag)) { abortFlag = 1; ok = false; break; }
                 fenceAfter();
                 const uint32_t a = smem(base + stage * kStageBytes);
                 const uint32_t b = a + kABytes;
@@ -257,15 +473,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         // All MMAs issued by this thread complete before TMEM is released.
         mmaCommit(&mmaDone);
         if (!mbarWait(&mmaDone, 0)) abortFlag = 1;
-    } else if (warp >= 2) {
+    } else if (warp >= 2 && warp < 6) {
         // ---- epilogue ----
         const uint32_t quadrant = warp % 4;  // TMEM lanes 32*quadrant .. +31
         const uint32_t row = quadrant * 32 + lane;
         uint32_t acc = 0, accPhase = 0;
+        TileQueue& queue = queues[quadrant];
+        (void)queue;
         for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
             uint32_t mb, nb;
             tileCoords(tile, p, mb, nb);
-            if (!mbarWait(&tmemFull[acc], accPhase)) abortFlag = 1;
+            if (!mbarWait(&tmemFull[acc], accPhase, &abortFlag)) abortFlag = 1;
             if (abortFlag) break;
             fenceAfter();
             const uint64_t grow = static_cast<uint64_t>(mb) * kBM + row;
@@ -302,25 +520,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float v[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = epilogueValue<EPI>(__uint_as_float(r[j]), aux[j]);
-                if constexpr (EPI == kEpiRedF32) {
-                    // Reduction through the NVLink switch: the multicast
-                    // address maps the same buffer on every rank; each add
-                    // lands, summed, in all of them.
-                    float* dst = static_cast<float*>(p.c) + grow * p.ldc + col0;
-                    if (full32 && reinterpret_cast<uintptr_t>(dst) % 16 == 0) {
-#pragma unroll
-                        for (int q = 0; q < 8; ++q)
-                            asm volatile("multimem.red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(
-                                             dst + 4 * q),
-                                         "f"(v[4 * q]), "f"(v[4 * q + 1]), "f"(v[4 * q + 2]), "f"(v[4 * q + 3])
-                                         : "memory");
-                    } else {
-                        for (int j = 0; j < 32; ++j)
-                            if (col0 + j < p.n)
-                                asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(dst + j), "f"(v[j])
-                                             : "memory");
-                    }
-                } else if constexpr (EPI == kEpiF32) {
+                if constexpr (EPI == kEpiF32 || EPI == kEpiAllReduceF32) {
                     float* dst = static_cast<float*>(p.c) + grow * p.ldc + col0;
                     if (full32 && reinterpret_cast<uintptr_t>(dst) % 16 == 0) {
 #pragma unroll
@@ -355,8 +555,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             fenceBefore();
             mbarArrive(&tmemEmpty[acc]);
             if (++acc == 2) { acc = 0; accPhase ^= 1u; }
+            if constexpr (EPI == kEpiAllReduceF32) {
+                // Announce this tile; owned tiles go to this quadrant's reducer warp.
+                announceRows(p, tile, quadrant, lane);
+                if (tileOwner(p, tile) == p.rank && !pushTile(queue, tile, lane, &abortFlag)) abortFlag = 1;
+                if (abortFlag) break;
+            }
         }
-        if constexpr (EPI == kEpiRedF32) asm volatile("fence.acq_rel.sys;" ::: "memory");
+        if constexpr (EPI == kEpiAllReduceF32) (void)pushTile(queue, kNoTile, lane, &abortFlag);
+    } else if (EPI == kEpiAllReduceF32 && warp >= 6) {
+        // ---- reducers: owned tiles, summed over ranks in the switch ----
+        const uint32_t quadrant = warp % 4;
+        TileQueue& queue = queues[quadrant];
+        for (;;) {
+            const uint32_t tile = popTile(queue, lane, &abortFlag);
+            if (tile == kNoTile) break;
+            if (!reduceRows(p, tile, quadrant, lane, &abortFlag)) {
+                abortFlag = 1;
+                break;
+            }
+        }
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
     }
     __syncthreads();
     if (threadIdx.x == 0 && abortFlag) atomicOr(p.status, kWaitStatus);
@@ -399,9 +618,7 @@ cudaError_t launchTyped(const CUtensorMap& a, const CUtensorMap& b, const Params
     auto kernel = gemmKernel<A_MN, B_MN, EPI>;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
-    const uint32_t tiles = p.mTiles * p.nTiles;
-    const uint32_t grid = tiles < static_cast<uint32_t>(smCount) ? tiles : static_cast<uint32_t>(smCount);
-    kernel<<<grid, kThreads, kSmemBytes, stream>>>(a, b, p);
+    kernel<<<p.grid, threadsFor(EPI), kSmemBytes, stream>>>(a, b, p);
     return cudaGetLastError();
 }
 
@@ -412,7 +629,7 @@ cudaError_t launchEpi(int epi, const CUtensorMap& a, const CUtensorMap& b, const
     case kEpiBf16: return launchTyped<A_MN, B_MN, kEpiBf16>(a, b, p, sm, s);
     case kEpiReluBf16: return launchTyped<A_MN, B_MN, kEpiReluBf16>(a, b, p, sm, s);
     case kEpiMaskBf16: return launchTyped<A_MN, B_MN, kEpiMaskBf16>(a, b, p, sm, s);
-    case kEpiRedF32: return launchTyped<A_MN, B_MN, kEpiRedF32>(a, b, p, sm, s);
+    case kEpiAllReduceF32: return launchTyped<A_MN, B_MN, kEpiAllReduceF32>(a, b, p, sm, s);
     }
     return cudaErrorInvalidValue;
 }
@@ -428,11 +645,24 @@ const char* validate(const Problem& q) {
     if (q.lda < (q.aMajorMN ? q.m : q.k) || q.ldb < (q.bMajorMN ? q.n : q.k)) return "leading dimension too small";
     if (q.ldc < q.n) return "ldc smaller than N";
     if (q.epilogue == kEpiMaskBf16 && (!q.aux || q.ldAux < q.n)) return "mask epilogue needs an auxiliary bf16 matrix";
-    if (q.epilogue < kEpiF32 || q.epilogue > kEpiRedF32) return "unknown epilogue";
-    if (q.epilogue == kEpiRedF32 && (reinterpret_cast<uintptr_t>(q.c) % 16 || q.ldc % 4))
-        return "the multicast reduction target must be 16-byte aligned with ldc a multiple of 4";
+    if (q.epilogue < kEpiF32 || q.epilogue > kEpiAllReduceF32) return "unknown epilogue";
+    if (q.epilogue == kEpiAllReduceF32) {
+        const AllReduce& r = q.reduce;
+        if (r.world == 0 || r.world > static_cast<uint32_t>(kMaxRanks) || r.rank >= r.world)
+            return "the all-reduce needs 1..8 ranks and a rank inside the world";
+        if ((reinterpret_cast<uintptr_t>(q.c) | reinterpret_cast<uintptr_t>(r.cMulticast)) % 16 || q.ldc % 4)
+            return "the all-reduce target must be 16-byte aligned with ldc a multiple of 4";
+        if (r.cPeers[r.rank] != q.c) return "the all-reduce's own peer entry must be C";
+        for (uint32_t k = 0; k < r.world; ++k) {
+            if (!r.cPeers[k] || !r.flagsPeers[k]) return "the all-reduce needs every rank's C and signal words";
+            if (reinterpret_cast<uintptr_t>(r.cPeers[k]) % 16 || reinterpret_cast<uintptr_t>(r.flagsPeers[k]) % 4)
+                return "peer C must be 16-byte and signal words 4-byte aligned";
+        }
+    }
     return nullptr;
 }
+
+std::uint64_t tileCount(std::uint64_t m, std::uint64_t n) { return ((m + kBM - 1) / kBM) * ((n + kBN - 1) / kBN); }
 
 cudaError_t run(const Problem& q, int smCount, uint32_t* status, cudaStream_t stream) {
     CUtensorMap a, b;
@@ -452,6 +682,16 @@ cudaError_t run(const Problem& q, int smCount, uint32_t* status, cudaStream_t st
     p.ldAux = q.ldAux;
     p.c2 = q.c2;
     p.status = status;
+    const uint32_t tiles = p.mTiles * p.nTiles;
+    p.grid = tiles < static_cast<uint32_t>(smCount) ? tiles : static_cast<uint32_t>(smCount);
+    p.cMc = static_cast<float*>(q.reduce.cMulticast);
+    for (int r = 0; r < kMaxRanks; ++r) {
+        p.cPeers[r] = static_cast<float*>(q.reduce.cPeers[r]);
+        p.flagsPeers[r] = q.reduce.flagsPeers[r];
+    }
+    p.rank = q.reduce.rank;
+    p.world = q.reduce.world ? q.reduce.world : 1;
+    p.target = q.reduce.target;
     if (q.aMajorMN) {
         if (q.bMajorMN) return launchEpi<true, true>(q.epilogue, a, b, p, smCount, stream);
         return launchEpi<true, false>(q.epilogue, a, b, p, smCount, stream);

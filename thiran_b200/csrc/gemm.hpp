@@ -13,9 +13,32 @@ enum : int {
     kEpiBf16 = 1,      // C (bf16) = acc
     kEpiReluBf16 = 2,  // C (bf16) = max(acc, 0)            (forward ReLU)
     kEpiMaskBf16 = 3,  // C (bf16) = aux > 0 ? acc : 0       (ReLU backward mask, aux bf16 [M][N])
-    kEpiRedF32 = 4,    // C (f32) += acc on every GPU: `c` is an NVLink multicast address and the
-                       // epilogue issues multimem.red.add, so the switch sums all ranks' tiles
+    kEpiAllReduceF32 = 4,  // C (f32) = sum over ranks of acc, on every rank (see AllReduce)
 };
+
+// Cross-GPU all-reduce fused into the epilogue (kEpiAllReduceF32). Every rank
+// runs the same GEMM on its own rows of K (its part of the batch); C and the
+// signal words are symmetric buffers every rank maps. Each finished tile is
+// stored locally and announced by a release add on its owner rank's signal
+// word; the owner's reducer warps wait for all ranks' announcements, sum the
+// tile and write the total into every rank's C while later tiles compute:
+//  - peer mode (cMulticast null): plain NVLink loads of every rank's tile,
+//    summed in rank order, and plain stores to every rank. Each GPU moves
+//    2(world-1)/world of C each way, as a ring all-reduce does.
+//  - switch mode: multimem.ld_reduce sums the tile inside NVSwitch and
+//    multimem.st writes the total to all ranks; about (1 + 1/world) of C each
+//    way, less than peer mode from 3 ranks up.
+constexpr int kMaxRanks = 8;
+struct AllReduce {
+    void* cMulticast = nullptr;                   // switch mode: NVLS multicast address of C
+    void* cPeers[kMaxRanks] = {};                 // C as mapped on this GPU, for every rank
+    std::uint32_t* flagsPeers[kMaxRanks] = {};    // signal words (4 per tile), for every rank
+    std::uint32_t rank = 0, world = 1;
+    std::uint32_t target = 0;                     // each signal word's value once this launch's ranks all announced
+};
+
+// Tiles of an M x N output (signal words needed: 4 per tile).
+std::uint64_t tileCount(std::uint64_t m, std::uint64_t n);
 
 struct Problem {
     std::uint64_t m = 0, n = 0, k = 0;
@@ -31,6 +54,7 @@ struct Problem {
     const void* aux = nullptr;  // bf16 [M][N] for kEpiMaskBf16
     std::uint64_t ldAux = 0;
     void* c2 = nullptr;         // optional f32 copy (bf16 epilogues), ld = ldc
+    AllReduce reduce;           // kEpiAllReduceF32
 };
 
 // Returns an error text for an invalid problem, or nullptr.

@@ -187,7 +187,7 @@ cudaError_t forwardBackward(const Buffers& b, const float* x, const float* t, in
     q.a = b.h; q.aMajorMN = true; q.lda = b.hidden;
     q.b = b.dy; q.bMajorMN = true; q.ldb = b.out;
     q.c = b.dw2; q.ldc = b.out; q.epilogue = gemm::kEpiF32;
-    if (b.dw2Reduce) { q.c = b.dw2Reduce; q.epilogue = gemm::kEpiRedF32; }
+    if (b.dw2Reduce.cPeers[0]) { q.epilogue = gemm::kEpiAllReduceF32; q.reduce = b.dw2Reduce; }
     if ((e = runGemm(q)) != cudaSuccess) return e;
     // dW1 = Xb^T dH: A = Xb stored [B][in] (MN-major), B = dH stored [B][hidden] (MN-major).
     q = {};
@@ -195,7 +195,7 @@ cudaError_t forwardBackward(const Buffers& b, const float* x, const float* t, in
     q.a = b.xb; q.aMajorMN = true; q.lda = b.in;
     q.b = b.dh; q.bMajorMN = true; q.ldb = b.hidden;
     q.c = b.dw1; q.ldc = b.hidden; q.epilogue = gemm::kEpiF32;
-    if (b.dw1Reduce) { q.c = b.dw1Reduce; q.epilogue = gemm::kEpiRedF32; }
+    if (b.dw1Reduce.cPeers[0]) { q.epilogue = gemm::kEpiAllReduceF32; q.reduce = b.dw1Reduce; }
     return runGemm(q);
 }
 

@@ -5,6 +5,8 @@
 
 #include <cstdint>
 
+#include "gemm.hpp"
+
 namespace thb::mlp {
 
 // Device buffers of one training session (all owned by the session).
@@ -23,10 +25,10 @@ struct Buffers {
     float* dw2 = nullptr;      // f32 [hidden][out]
     double* lossPartials = nullptr;
     double* lossSum = nullptr; // sum over this rank's batch of (Y - T)^2
-    // Data-parallel gradient reduction fused into the dW GEMMs: NVLink
-    // multicast addresses of the dW buffers (null = store locally).
-    float* dw1Reduce = nullptr;
-    float* dw2Reduce = nullptr;
+    // Data-parallel gradient all-reduce fused into the dW GEMMs (no peers =
+    // plain local store). The caller advances `target` every step.
+    gemm::AllReduce dw1Reduce;
+    gemm::AllReduce dw2Reduce;
 };
 
 // Optional CUDA-event timing of the GEMM launches of a step (recorded on the

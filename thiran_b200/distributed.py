@@ -5,9 +5,8 @@ CPU/GPU partition, src/distributed/PartitionPlanner.cpp:6-32). Here regions
 shard along the leading axis with no data-path collective; the full-tensor
 sum combines one f64 partial per rank, and MLP data parallelism all-reduces
 the weight gradients, either by NCCL all-reduce after the backward pass or
-inside the weight-gradient GEMM epilogues through NVLink multicast memory
-(MulticastGradients). The process group is torch.distributed (NCCL on GPUs,
-gloo for the CPU tests).
+inside the weight-gradient GEMMs over NVLink (FusedGradientAllReduce). The
+process group is torch.distributed (NCCL on GPUs, gloo for the CPU tests).
 """
 from __future__ import annotations
 
@@ -41,44 +40,62 @@ def combine_partial_sums(partial, dist=None):
     return partial
 
 
-class MulticastGradients:
-    """Weight-gradient buffers in NVLink multicast (NVLS) memory for the fused
-    GEMM -> cross-GPU reduction of an MlpSession: every rank maps the same
-    buffers, the dW GEMM epilogues add their tiles through the multicast
-    address (multimem.red), and each rank reads the summed gradients from its
-    own copy. Built on torch symmetric memory; `available` is False when the
-    device or fabric has no multicast support (callers then all-reduce)."""
+def fused_reduction_mode(world: int) -> str:
+    """Transport of the fused gradient all-reduce for `world` ranks: plain
+    peer loads/stores ("peer") move 2(world-1)/world of the gradients each
+    way per GPU, the in-switch reduction ("switch") about 1 + 1/world, so
+    peer mode wins at 2 ranks and switch mode from 3 up. Measured on 256 MiB
+    of f32 over NVLink 5: 2 ranks 0.41 ms peer vs 0.70 ms switch; 8 ranks
+    0.90 ms peer vs 0.62 ms switch."""
+    return "peer" if world <= 2 else "switch"
+
+
+class FusedGradientAllReduce:
+    """Weight gradients all-reduced inside the dW GEMMs of an MlpSession: the
+    dW buffers and their per-tile signal words live in torch symmetric memory
+    that every rank maps; each GEMM stores and announces its tiles, and each
+    tile's owner rank sums it over all ranks and writes the total to every
+    rank (thb_mlp_bind_reduction), by plain NVLink loads/stores or inside
+    NVSwitch (`mode`, default fused_reduction_mode(world)). `available` is
+    False when switch mode was asked for and the fabric has no multicast
+    (callers then all-reduce with NCCL)."""
 
     BARRIER_TIMEOUT_MS = 60000
 
-    def __init__(self, session, dist, group=None):
+    def __init__(self, session, dist, group=None, mode=None):
         import torch
         import torch.distributed._symmetric_memory as symm_mem
         from . import MLP_DW1, MLP_DW2
         self.group = group or dist.group.WORLD
+        rank, world = dist.get_rank(self.group), dist.get_world_size(self.group)
+        self.mode = mode or fused_reduction_mode(world)
+        if self.mode not in ("peer", "switch"):
+            raise ValueError(f"unknown fused all-reduce mode {self.mode!r}")
         self.buffers, self.handles = [], []
         shapes = [(MLP_DW1, (session.d_in, session.hidden)), (MLP_DW2, (session.hidden, session.d_out))]
+        words = [session.reduction_flag_words(which) for which, _ in shapes]
+        self.flags = symm_mem.empty((sum(words),), dtype=torch.int32, device="cuda")
+        self.flags.zero_()
+        self.flag_handle = symm_mem.rendezvous(self.flags, self.group)
         for which, shape in shapes:
             t = symm_mem.empty(shape, dtype=torch.float32, device="cuda")
             h = symm_mem.rendezvous(t, self.group)
             self.buffers.append((which, t))
             self.handles.append(h)
-        self.available = all(h.multicast_ptr for h in self.handles)
+        self.available = self.mode == "peer" or all(h.multicast_ptr for h in self.handles)
+        # Every rank's signal words are zero before any rank can announce.
+        self.flag_handle.barrier(channel=0, timeout_ms=self.BARRIER_TIMEOUT_MS)
         if self.available:
-            for (which, t), h in zip(self.buffers, self.handles):
-                session.bind(which, t)
-                session.bind_reduction(which, h.multicast_ptr)
-
-    def before_step(self):
-        """Zero this rank's copies, then wait until every rank has (so no
-        rank's reductions land in a buffer another rank is still reading)."""
-        for _, t in self.buffers:
-            t.zero_()
-        self.handles[0].barrier(channel=0, timeout_ms=self.BARRIER_TIMEOUT_MS)
+            offset = 0
+            flag_ptrs = [int(p) for p in self.flag_handle.buffer_ptrs]
+            for ((which, t), h), n in zip(zip(self.buffers, self.handles), words):
+                session.bind_reduction(which, [int(p) for p in h.buffer_ptrs], [p + 4 * offset for p in flag_ptrs],
+                                       rank, world, h.multicast_ptr if self.mode == "switch" else None)
+                offset += n
 
     def after_backward(self):
-        """Wait until every rank's reductions have landed."""
-        self.handles[0].barrier(channel=1, timeout_ms=self.BARRIER_TIMEOUT_MS)
+        """Wait until every rank's owned tiles hold their totals everywhere."""
+        self.flag_handle.barrier(channel=1, timeout_ms=self.BARRIER_TIMEOUT_MS)
 
 
 def allreduce_gradients(tensors, dist=None):
