@@ -1,9 +1,10 @@
 """Benchmark of the B200 TensorRegion engine (one JSON line on rank 0).
 
 Default workload: the i64 elementwise region out = (a + b) * a - b on
-[8192, 8192] i64 with a, b uniform integers in [-1000, 1000] (seed 1), checked
-for overflow, row-sharded over the ranks (8192 / N rows each, no collective).
-A step is one pass of the fused region kernel over the rank's shard.
+[8192, 8192] i64 per GPU with a, b uniform integers in [-1000, 1000] (seed
+1 + 1000 * rank), checked for overflow. N ranks process N such row blocks of
+an [8192 N, 8192] region (weak scaling, no collective). A step is one pass of
+the fused region kernel over the rank's block.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
                     [--workload i64_region|f32_chain|softmax]
@@ -79,18 +80,18 @@ class I64Region(Workload):
 
     def build(self, torch, rank, world):
         from thiran_b200 import regions
-        rows = self.rows // world
         g = torch.Generator(device="cuda").manual_seed(1 + 1000 * rank)
-        a = torch.randint(-1000, 1001, (rows, self.cols), dtype=torch.int64, device="cuda", generator=g)
-        b = torch.randint(-1000, 1001, (rows, self.cols), dtype=torch.int64, device="cuda", generator=g)
+        a = torch.randint(-1000, 1001, (self.rows, self.cols), dtype=torch.int64, device="cuda", generator=g)
+        b = torch.randint(-1000, 1001, (self.rows, self.cols), dtype=torch.int64, device="cuda", generator=g)
         out = torch.empty_like(a)
         return regions.i64_region(), [a, b], out
 
     def config(self, world):
-        return {"workload": "i64 region (a+b)*a-b, [8192,8192] i64, uniform ints [-1000,1000] seed 1, overflow-checked",
-                "global_shape": [self.rows, self.cols], "shard": f"rows/{world} per rank",
+        return {"workload": "i64 region (a+b)*a-b, [8192,8192] i64 per GPU, uniform ints [-1000,1000] "
+                            "seed 1+1000*rank, overflow-checked",
+                "global_shape": [self.rows * world, self.cols], "shard": "one [8192,8192] row block per rank",
                 "parallelism": f"row-sharded x{world}, no collective",
-                "l2": "working set 1.5 GiB/step >> 126 MB L2 (no flush needed)"}
+                "l2": "working set 1.5 GiB/step per GPU >> 126 MB L2 (no flush needed)"}
 
 
 class F32Chain(Workload):
@@ -103,13 +104,13 @@ class F32Chain(Workload):
     def build(self, torch, rank, world):
         from thiran_b200 import regions
         g = torch.Generator(device="cuda").manual_seed(2 + 1000 * rank)
-        x = torch.rand(self.n // world, device="cuda", generator=g) * 2 - 1
+        x = torch.rand(self.n, device="cuda", generator=g) * 2 - 1
         return regions.f32_chain(), [x], torch.empty_like(x)
 
     def config(self, world):
-        return {"workload": "f32 chain ((x*1.5+0.25)*x-x)*0.5+x on 2^28 f32, uniform[-1,1] seed 2",
-                "global_shape": [self.n], "shard": f"elements/{world} per rank",
-                "parallelism": f"sharded x{world}, no collective", "l2": "2 GiB/step >> L2"}
+        return {"workload": "f32 chain ((x*1.5+0.25)*x-x)*0.5+x on 2^28 f32 per GPU, uniform[-1,1] seed 2+1000*rank",
+                "global_shape": [self.n * world], "shard": "2^28 elements per rank",
+                "parallelism": f"sharded x{world}, no collective", "l2": "2 GiB/step per GPU >> L2"}
 
 
 class Softmax(Workload):
@@ -123,13 +124,13 @@ class Softmax(Workload):
     def build(self, torch, rank, world):
         from thiran_b200 import regions
         g = torch.Generator(device="cuda").manual_seed(3 + 1000 * rank)
-        x = torch.randn((self.rows // world, self.cols), device="cuda", generator=g)
+        x = torch.randn((self.rows, self.cols), device="cuda", generator=g)
         return regions.softmax_rows(), [x], torch.empty_like(x)
 
     def config(self, world):
-        return {"workload": "row softmax on [65536,4096] f32 ~ N(0,1) seed 3",
-                "global_shape": [self.rows, self.cols], "shard": f"rows/{world} per rank",
-                "parallelism": f"row-sharded x{world}, no collective", "l2": "2 GiB/step >> L2"}
+        return {"workload": "row softmax on [65536,4096] f32 per GPU ~ N(0,1) seed 3+1000*rank",
+                "global_shape": [self.rows * world, self.cols], "shard": "one [65536,4096] row block per rank",
+                "parallelism": f"row-sharded x{world}, no collective", "l2": "2 GiB/step per GPU >> L2"}
 
 
 class FullSum(Workload):
@@ -148,12 +149,13 @@ class FullSum(Workload):
     def build(self, torch, rank, world):
         from thiran_b200 import regions
         g = torch.Generator(device="cuda").manual_seed(3 + 1000 * rank)
-        x = torch.randn((self.rows // world) * self.cols, device="cuda", generator=g)
+        x = torch.randn(self.rows * self.cols, device="cuda", generator=g)
         return regions.full_sum(), [x], torch.empty(1, device="cuda")
 
     def config(self, world):
-        return {"workload": "full-tensor sum of [65536,4096] f32 ~ N(0,1) seed 3 (f64 accumulation)",
-                "global_shape": [self.rows, self.cols], "shard": f"rows/{world} per rank",
+        return {"workload": "full-tensor sum of [65536,4096] f32 per GPU ~ N(0,1) seed 3+1000*rank "
+                            "(f64 accumulation)",
+                "global_shape": [self.rows * world, self.cols], "shard": "one [65536,4096] row block per rank",
                 "parallelism": f"row-sharded x{world}, NCCL all-reduce of one f64 partial per rank"
                                if world > 1 else "single GPU",
                 "l2": "1 GiB/step >> L2"}

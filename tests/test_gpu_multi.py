@@ -1,8 +1,8 @@
-"""Two-GPU tests (skipped with fewer than two devices): data-parallel MLP
-steps whose gradient all-reduce is fused into the weight-gradient GEMMs (peer
-loads/stores or in-switch reduction over NVLink) or done by NCCL after the
-backward pass equal the single-process full-batch step. Each test runs two
-spawned ranks over NCCL."""
+"""Multi-GPU tests (each skipped with fewer devices than its ranks):
+data-parallel MLP steps whose gradient all-reduce is fused into the
+weight-gradient GEMMs (peer loads/stores or in-switch reduction over NVLink)
+or done by NCCL after the backward pass equal the single-process full-batch
+step, at 2, 4 and 8 ranks. Each test runs spawned ranks over NCCL."""
 import os
 import socket
 
@@ -19,8 +19,8 @@ def free_port():
         return s.getsockname()[1]
 
 
-def two_gpus():
-    return torch.cuda.is_available() and torch.cuda.device_count() >= 2
+def gpus():
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
 def _mlp_rank(rank, world, port, mode, out_path):
@@ -100,12 +100,15 @@ def rel(a, b):
     return float(np.linalg.norm(a.astype(np.float64) - b) / np.linalg.norm(b))
 
 
-@pytest.mark.skipif(not two_gpus(), reason="needs two GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("mode", ["peer", "switch", "nccl"])
-def test_data_parallel_mlp_matches_full_batch(tmp_path, mode):
+def test_data_parallel_mlp_matches_full_batch(tmp_path, mode, world):
+    if gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
-    out = str(tmp_path / f"{mode}.npz")
-    mp.start_processes(_mlp_rank, args=(2, free_port(), mode, out), nprocs=2, join=True, start_method="spawn")
+    out = str(tmp_path / f"{mode}{world}.npz")
+    mp.start_processes(_mlp_rank, args=(world, free_port(), mode, out), nprocs=world, join=True,
+                       start_method="spawn")
     if os.path.exists(out) and open(out, "rb").read(11) == b"unavailable":
         pytest.skip("no NVLink multicast on this system")
     got = dict(np.load(out))
