@@ -176,6 +176,36 @@ static void transpose(const float* x, float* y, uint64_t rows, uint64_t cols) {
 
 double orc_mlp_step(const float* x, const float* t, float* w1, float* w2, uint64_t b, uint64_t i, uint64_t h,
                     uint64_t o, float lr, float* dw1, float* dw2, float* hidden, float* yout) {
+    return orc_mlp_step_ex(x, t, w1, w2, b, i, h, o, lr, dw1, dw2, hidden, yout, NULL);
+}
+
+/* Column sums of a [rows, cols] matrix, f64 accumulation in row order. */
+static void column_sums(const float* m, float* out, uint64_t rows, uint64_t cols) {
+    for (uint64_t c = 0; c < cols; ++c) {
+        double acc = 0.0;
+        for (uint64_t r = 0; r < rows; ++r) acc += (double)m[r * cols + c];
+        out[c] = (float)acc;
+    }
+}
+
+void orc_sgd_update(float* p, const float* g, float* v, float mu, float lr, uint64_t n) {
+    for (uint64_t k = 0; k < n; ++k) {
+        float d = g[k];
+        if (v) {
+            const float scaled = v[k] * mu;
+            d = scaled + g[k];
+            v[k] = d;
+        }
+        const float step = d * lr;
+        p[k] = p[k] - step;
+    }
+}
+
+double orc_mlp_step_ex(const float* x, const float* t, float* w1, float* w2, uint64_t b, uint64_t i, uint64_t h,
+                       uint64_t o, float lr, float* dw1, float* dw2, float* hidden, float* yout,
+                       const orc_mlp_extras* ex) {
+    const orc_mlp_extras none = {0};
+    if (!ex) ex = &none;
     float* xb = (float*)malloc(sizeof(float) * b * i);
     float* w1b = (float*)malloc(sizeof(float) * i * h);
     float* w2b = (float*)malloc(sizeof(float) * h * o);
@@ -191,9 +221,13 @@ double orc_mlp_step(const float* x, const float* t, float* w1, float* w2, uint64
     orc_round_bf16(w2, w2b, h * o);
     /* forward */
     orc_matmul_f64acc(xb, w1b, hidden, b, i, h);
+    if (ex->b1)
+        for (uint64_t k = 0; k < b * h; ++k) hidden[k] = hidden[k] + ex->b1[k % h];
     for (uint64_t k = 0; k < b * h; ++k) hidden[k] = relu(hidden[k]);
     orc_round_bf16(hidden, hb, b * h);
     orc_matmul_f64acc(hb, w2b, y, b, h, o);
+    if (ex->b2)
+        for (uint64_t k = 0; k < b * o; ++k) y[k] = y[k] + ex->b2[k % o];
     double loss = 0.0;
     const float scale = 2.0f / (float)(b * o);
     for (uint64_t k = 0; k < b * o; ++k) {
@@ -202,6 +236,9 @@ double orc_mlp_step(const float* x, const float* t, float* w1, float* w2, uint64
         dy[k] = d * scale;
     }
     loss /= (double)(b * o);
+    float* db1 = (float*)malloc(sizeof(float) * h);
+    float* db2 = (float*)malloc(sizeof(float) * o);
+    if (ex->b2) column_sums(dy, db2, b, o);
     orc_round_bf16(dy, dyb, b * o);
     /* backward: dW2 = H^T dY */
     transpose(hb, tr, b, h);
@@ -210,15 +247,22 @@ double orc_mlp_step(const float* x, const float* t, float* w1, float* w2, uint64
     transpose(w2b, tmp, h, o);
     orc_matmul_f64acc(dyb, tmp, dh, b, o, h);
     for (uint64_t k = 0; k < b * h; ++k) dh[k] = hidden[k] > 0.0f ? dh[k] : 0.0f;
+    if (ex->b1) column_sums(dh, db1, b, h);
     orc_round_bf16(dh, dh, b * h);
     /* dW1 = X^T dH */
     transpose(xb, tr, b, i);
     orc_matmul_f64acc(tr, dh, dw1, i, b, h);
-    /* SGD (Training.cpp:368-371): p = p - lr * g */
-    for (uint64_t k = 0; k < i * h; ++k) w1[k] = w1[k] - lr * dw1[k];
-    for (uint64_t k = 0; k < h * o; ++k) w2[k] = w2[k] - lr * dw2[k];
+    /* Optimizer (Training.cpp:366-372), parameters in W1, b1, W2, b2 order. */
+    const float mu = ex->momentum;
+    orc_sgd_update(w1, dw1, ex->v_w1, mu, lr, i * h);
+    if (ex->b1) orc_sgd_update(ex->b1, db1, ex->v_b1, mu, lr, h);
+    orc_sgd_update(w2, dw2, ex->v_w2, mu, lr, h * o);
+    if (ex->b2) orc_sgd_update(ex->b2, db2, ex->v_b2, mu, lr, o);
+    if (ex->db1 && ex->b1) memcpy(ex->db1, db1, sizeof(float) * h);
+    if (ex->db2 && ex->b2) memcpy(ex->db2, db2, sizeof(float) * o);
     if (yout) memcpy(yout, y, sizeof(float) * b * o);
     free(xb); free(w1b); free(w2b); free(hb); free(y); free(dy); free(dyb); free(dh); free(tmp); free(tr);
+    free(db1); free(db2);
     return loss;
 }
 

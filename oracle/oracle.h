@@ -75,6 +75,35 @@ void orc_round_bf16(const float* x, float* y, uint64_t n);
 double orc_mlp_step(const float* x, const float* t, float* w1, float* w2, uint64_t b, uint64_t i, uint64_t h,
                     uint64_t o, float lr, float* dw1, float* dw2, float* hidden, float* y);
 
+/* One optimizer update of n parameters (src/training/v0/Training.cpp:366-372):
+ * with a velocity v, d = v*mu + g and v = d (SGDMomentum); without, d = g
+ * (SGD); then p = p - d*lr. Each operation rounds to f32. */
+void orc_sgd_update(float* p, const float* g, float* v, float mu, float lr, uint64_t n);
+
+/* The same step with the optional parts of the examples/mlp.th structure and
+ * the reference optimizer:
+ *   biases (b1 [h], b2 [o], broadcast over rows, Evaluator.cpp:95-124):
+ *     H = relu(X W1 + b1), Y = H W2 + b2; their gradients are the column sums
+ *     of dH and dY (reduceToShape, Evaluator.cpp:258-277; f64 accumulation);
+ *   SGD with momentum mu (Training.cpp:366-372): d = v*mu + g; v = d;
+ *     p = p - d*lr, for every parameter (W1, b1, W2, b2).
+ * NULL b1/b2 = no biases; momentum 0 with NULL velocities = plain SGD. */
+typedef struct {
+    float* b1;        /* [h], updated in place */
+    float* b2;        /* [o], updated in place */
+    float momentum;
+    float* v_w1;      /* velocities, same shapes, updated in place */
+    float* v_b1;
+    float* v_w2;
+    float* v_b2;
+    float* db1;       /* out: bias gradients (optional) */
+    float* db2;
+} orc_mlp_extras;
+
+double orc_mlp_step_ex(const float* x, const float* t, float* w1, float* w2, uint64_t b, uint64_t i, uint64_t h,
+                       uint64_t o, float lr, float* dw1, float* dw2, float* hidden, float* y,
+                       const orc_mlp_extras* extras);
+
 #ifdef __cplusplus
 }
 #endif

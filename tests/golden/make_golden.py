@@ -159,6 +159,14 @@ let s = e .* e
 return sum(sum(s, 1), 0)
 }"""
 
+LINEAR_BIAS_LOSS = """fn loss(x: Tensor<f32,2>, w1: Tensor<f32,2>, b1: Tensor<f32,1>, w2: Tensor<f32,2>, b2: Tensor<f32,1>, t: Tensor<f32,2>) -> f32 {
+let h = x * w1 + b1
+let y = h * w2 + b2
+let e = y - t
+let s = e .* e
+return sum(sum(s, 1), 0)
+}"""
+
 
 def main():
     if not os.path.exists(DRIVER):
@@ -261,6 +269,18 @@ def main():
     loss, (gx, gw1, gw2, gt) = vjp(LINEAR_LOSS, "loss", np.float32(1.0), [lx, lw1, lw2, lt], 4)
     arrays.update(ad_lin_x=lx, ad_lin_w1=lw1, ad_lin_w2=lw2, ad_lin_t=lt, ad_lin_loss=np.float32(loss),
                   ad_lin_dx=gx, ad_lin_dw1=gw1, ad_lin_dw2=gw2, ad_lin_dt=gt)
+    # The same loss with broadcast biases (the examples/mlp.th structure).
+    bx = rng.standard_normal((16, 32)).astype(np.float32)
+    bw1 = (rng.standard_normal((32, 64)) * 0.2).astype(np.float32)
+    bb1 = (rng.standard_normal(64) * 0.1).astype(np.float32)
+    bw2 = (rng.standard_normal((64, 24)) * 0.2).astype(np.float32)
+    bb2 = (rng.standard_normal(24) * 0.1).astype(np.float32)
+    bt = rng.standard_normal((16, 24)).astype(np.float32)
+    loss, grads = vjp(LINEAR_BIAS_LOSS, "loss", np.float32(1.0), [bx, bw1, bb1, bw2, bb2, bt], 6)
+    arrays.update(ad_linb_x=bx, ad_linb_w1=bw1, ad_linb_b1=bb1, ad_linb_w2=bw2, ad_linb_b2=bb2, ad_linb_t=bt,
+                  ad_linb_loss=np.float32(loss))
+    for name, g in zip(("dx", "dw1", "db1", "dw2", "db2", "dt"), grads):
+        arrays[f"ad_linb_{name}"] = g
 
     np.savez_compressed(os.path.join(HERE, "reference_outputs.npz"), **arrays)
     with open(os.path.join(HERE, "reference_fixtures.json"), "w") as f:

@@ -32,6 +32,19 @@ _lib.orc_round_bf16.argtypes = [_f32p, _f32p, C.c_uint64]
 _lib.orc_mlp_step.restype = C.c_double
 _lib.orc_mlp_step.argtypes = [_f32p, _f32p, _f32p, _f32p, C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64, C.c_float,
                               _f32p, _f32p, _f32p, _f32p]
+_lib.orc_sgd_update.restype = None
+_lib.orc_sgd_update.argtypes = [_f32p, _f32p, C.c_void_p, C.c_float, C.c_float, C.c_uint64]
+
+
+class MlpExtras(C.Structure):
+    _fields_ = [("b1", C.c_void_p), ("b2", C.c_void_p), ("momentum", C.c_float), ("v_w1", C.c_void_p),
+                ("v_b1", C.c_void_p), ("v_w2", C.c_void_p), ("v_b2", C.c_void_p), ("db1", C.c_void_p),
+                ("db2", C.c_void_p)]
+
+
+_lib.orc_mlp_step_ex.restype = C.c_double
+_lib.orc_mlp_step_ex.argtypes = [_f32p, _f32p, _f32p, _f32p, C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64,
+                                 C.c_float, _f32p, _f32p, _f32p, _f32p, C.POINTER(MlpExtras)]
 
 
 class OracleFailure(RuntimeError):
@@ -117,3 +130,29 @@ def mlp_step(x, t, w1, w2, lr):
     y = np.empty((b, o), np.float32)
     loss = _lib.orc_mlp_step(x, t, w1, w2, b, i, h, o, lr, dw1, dw2, hidden, y)
     return loss, dw1, dw2, hidden, y
+
+
+def sgd_update(p, g, lr, v=None, momentum=0.0):
+    """orc_sgd_update in place on f32 arrays (v: velocity or None)."""
+    _lib.orc_sgd_update(p.reshape(-1), g.reshape(-1), None if v is None else v.ctypes.data, momentum, lr, p.size)
+
+
+def mlp_step_ex(x, t, w1, w2, lr, b1=None, b2=None, momentum=0.0, velocities=None):
+    """orc_mlp_step_ex: biases (updated in place) and SGD with momentum
+    (`velocities` = [vW1, vb1, vW2, vb2], updated in place). Returns
+    (loss, dW1, dW2, db1, db2, hidden, y)."""
+    b, i = x.shape
+    h = w1.shape[1]
+    o = w2.shape[1]
+    dw1 = np.empty((i, h), np.float32)
+    dw2 = np.empty((h, o), np.float32)
+    db1 = np.zeros(h, np.float32)
+    db2 = np.zeros(o, np.float32)
+    hidden = np.empty((b, h), np.float32)
+    y = np.empty((b, o), np.float32)
+    ptr = lambda a: None if a is None else a.ctypes.data
+    v = velocities or [None] * 4
+    ex = MlpExtras(ptr(b1), ptr(b2), momentum, ptr(v[0]), ptr(v[1]), ptr(v[2]), ptr(v[3]), db1.ctypes.data,
+                   db2.ctypes.data)
+    loss = _lib.orc_mlp_step_ex(x, t, w1, w2, b, i, h, o, lr, dw1, dw2, hidden, y, C.byref(ex))
+    return loss, dw1, dw2, db1, db2, hidden, y

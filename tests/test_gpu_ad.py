@@ -45,6 +45,16 @@ def test_linear_loss_backward_region(device, golden, name):
     assert rel(out, golden[f"ad_lin_{name}"]) <= 2e-2
 
 
+@pytest.mark.parametrize("name", ["dx", "dw1", "db1", "dw2", "db2", "dt"])
+def test_biased_linear_loss_backward_region(device, golden, name):
+    """Broadcast biases: BroadcastToShape in the forward, ReduceToShape onto
+    the bias in the backward; bf16 GEMM operands, so 2e-2 against the
+    reference's f32 vjp."""
+    args = [golden[f"ad_linb_{k}"] for k in ("x", "w1", "b1", "w2", "b2", "t")] + [1.0]
+    out = regions.linear_bias_loss_backward(name).compile(device).execute(args)
+    assert rel(out, golden[f"ad_linb_{name}"]) <= 2e-2
+
+
 @pytest.mark.parametrize("rows,cols,dtype", [(1, 1, np.float32), (33, 65, np.float32), (1000, 4096, np.float32),
                                              (257, 129, np.int64)])
 def test_transpose(device, rows, cols, dtype):

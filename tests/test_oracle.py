@@ -157,6 +157,65 @@ def test_ad_extension_gradients_match_reference(golden):
     assert out.view(np.uint32).tolist() == golden["ad_chain_grad"].view(np.uint32).tolist()
 
 
+@pytest.mark.parametrize("name", ["dx", "dw1", "db1", "dw2", "db2", "dt"])
+def test_ad_biased_linear_loss_backward_matches_reference(golden, name):
+    """With broadcast biases (the examples/mlp.th structure) the generated
+    backward adds ReduceToShape onto each bias; restated as a region it
+    reproduces the reference's vjp bit for bit."""
+    args = [golden[f"ad_linb_{k}"] for k in ("x", "w1", "b1", "w2", "b2", "t")] + [1.0]
+    out = orc.region_eval(regions.linear_bias_loss_backward(name), args)
+    assert out.view(np.uint32).tolist() == golden[f"ad_linb_{name}"].view(np.uint32).tolist()
+
+
+def test_momentum_update_matches_reference_training_tests():
+    """SGDMomentum known answers of the reference (TrainingTests.cpp:168-193,
+    204-210): lr 0.01, mu 0.5, parameters (bias, weight) from 0, gradients
+    (-32, -68) then (-21.28, -45.12); and lr 0.1 with v = 4, g = 0."""
+    p = np.zeros(2, np.float32)
+    v = np.zeros(2, np.float32)
+    orc.sgd_update(p, np.array([-32, -68], np.float32), 0.01, v, 0.5)
+    np.testing.assert_allclose(v, [-32, -68], rtol=0, atol=1e-6)
+    np.testing.assert_allclose(p, [0.32, 0.68], rtol=0, atol=1e-6)
+    plain = np.zeros(2, np.float32)
+    orc.sgd_update(plain, np.array([-32, -68], np.float32), 0.01)
+    assert plain.view(np.uint32).tolist() == p.view(np.uint32).tolist()  # TRAIN15
+    orc.sgd_update(p, np.array([-21.28, -45.12], np.float32), 0.01, v, 0.5)
+    np.testing.assert_allclose(v, [-37.28, -79.12], rtol=0, atol=2e-5)
+    np.testing.assert_allclose(p, [0.6928, 1.4712], rtol=0, atol=2e-5)
+    q = np.array([3.0], np.float32)
+    vq = np.array([4.0], np.float32)
+    orc.sgd_update(q, np.zeros(1, np.float32), 0.1, vq, 0.5)
+    np.testing.assert_allclose([vq[0], q[0]], [2.0, 2.8], rtol=0, atol=1e-6)
+
+
+def test_mlp_step_with_biases_matches_column_sum_rule():
+    """The oracle's biased MLP step: bias gradients are the column sums of
+    dY and the masked dH, and a momentum step from zero velocity equals the
+    plain SGD step."""
+    rng = np.random.default_rng(12)
+    x = rng.standard_normal((32, 16)).astype(np.float32)
+    t = rng.standard_normal((32, 8)).astype(np.float32)
+    w1 = (rng.uniform(-1, 1, (16, 24)) * 0.3).astype(np.float32)
+    w2 = (rng.uniform(-1, 1, (24, 8)) * 0.3).astype(np.float32)
+    b1 = (rng.standard_normal(24) * 0.1).astype(np.float32)
+    b2 = (rng.standard_normal(8) * 0.1).astype(np.float32)
+    runs = []
+    for momentum in (0.0, 0.9):
+        ws = [w1.copy(), w2.copy(), b1.copy(), b2.copy()]
+        vel = [np.zeros_like(a) for a in (w1, b1, w2, b2)] if momentum else None
+        loss, dw1, dw2, db1, db2, hidden, y = orc.mlp_step_ex(x, t, ws[0], ws[1], 0.05, ws[2], ws[3], momentum, vel)
+        runs.append(ws)
+    xb, w1b, w2b = (orc.round_bf16(a) for a in (x, w1, w2))
+    h = np.maximum(xb.astype(np.float64) @ w1b + b1, 0)
+    yy = orc.round_bf16(h.astype(np.float32)).astype(np.float64) @ w2b + b2
+    dy = 2 * (yy - t) / (32 * 8)
+    np.testing.assert_allclose(db2, dy.sum(0), rtol=1e-4, atol=1e-6)
+    dh = (orc.round_bf16(dy.astype(np.float32)).astype(np.float64) @ w2b.T) * (h > 0)
+    np.testing.assert_allclose(db1, dh.sum(0), rtol=1e-3, atol=1e-6)
+    for a, b in zip(*runs):
+        assert a.view(np.uint32).tolist() == b.view(np.uint32).tolist()
+
+
 @pytest.mark.parametrize("name", ["dx", "dw1", "dw2", "dt"])
 def test_ad_linear_loss_backward_matches_reference(golden, name):
     """The reference's generated backward (BroadcastToShape, ReduceToShape,

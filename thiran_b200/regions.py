@@ -101,6 +101,47 @@ def linear_loss_backward(output="dw1"):
     return b.build({"dx": dx, "dw1": dw1, "dw2": dw2, "dt": dt}[output])
 
 
+def linear_bias_loss_backward(output="dw1"):
+    """The reverse-mode backward the reference generates for the biased
+    two-layer loss (the examples/mlp.th structure without the ReLU, which the
+    V0 language lacks)
+        fn loss(x, w1, b1: Tensor<f32,1>, w2, b2: Tensor<f32,1>, t) -> f32 {
+            h = x*w1 + b1; y = h*w2 + b2; e = y - t; s = e.*e;
+            return sum(sum(s,1),0) }
+    Broadcast adds (Evaluator.cpp:95-124) run as BroadcastToShape + Add; the
+    bias gradients are ReduceToShape onto the bias (Evaluator.cpp:258-277).
+    `output` selects dx, dw1, db1, dw2, db2 or dt."""
+    b = RegionBuilder("loss_backward")
+    x = b.input(F32, [None, None])
+    w1 = b.input(F32, [None, None])
+    b1 = b.input(F32, [None])
+    w2 = b.input(F32, [None, None])
+    b2 = b.input(F32, [None])
+    t = b.input(F32, [None, None])
+    ct = b.input(F32, [])
+    xw1 = b.matmul(x, w1)
+    h = b.add(xw1, b.broadcast_to_shape(b1, xw1, 0))
+    hw2 = b.matmul(h, w2)
+    y = b.add(hw2, b.broadcast_to_shape(b2, hw2, 0))
+    e = b.sub(y, t)
+    s = b.mul(e, e)
+    rows = b.sum(s, 1)
+    d1 = b.broadcast_to_shape(ct, rows, 0)
+    d2 = b.broadcast_to_shape(d1, s, 1)
+    de = b.add(b.reduce_to_shape(b.mul(d2, e), e), b.reduce_to_shape(b.mul(d2, e), e))
+    dy = b.reduce_to_shape(de, y)
+    dt = b.neg(b.reduce_to_shape(de, t))
+    dhw2 = b.reduce_to_shape(dy, hw2)
+    db2 = b.reduce_to_shape(dy, b2)
+    dh = b.matmul(dhw2, b.transpose(w2))
+    dw2 = b.matmul(b.transpose(h), dhw2)
+    dxw1 = b.reduce_to_shape(dh, xw1)
+    db1 = b.reduce_to_shape(dh, b1)
+    dx = b.matmul(dxw1, b.transpose(w1))
+    dw1 = b.matmul(b.transpose(x), dxw1)
+    return b.build({"dx": dx, "dw1": dw1, "db1": db1, "dw2": dw2, "db2": db2, "dt": dt}[output])
+
+
 def f32_chain(n=None):
     """fn f(x: Tensor<f32,1>) -> Tensor<f32,1> { return research_chain(x) }"""
     b = RegionBuilder("f")
