@@ -173,10 +173,11 @@ class Mlp(Workload):
         return 5 * 2 * self.batch * self.d_in * self.hidden
 
     def config(self, world):
-        return {"workload": "2-layer MLP fwd+bwd+SGD: batch 8192, 4096->16384->4096, ReLU, MSE vs N(0,1) targets, "
+        return {"workload": "2-layer MLP fwd+bwd+SGD (examples/mlp.th structure): batch 8192, 4096->16384->4096, "
+                            "broadcast biases (zero-initialised, trained), ReLU, MSE vs N(0,1) targets, "
                             "Xavier-uniform weights, seed 4; bf16 GEMM operands, f32 accumulate",
                 "global_batch": self.batch, "dims": [self.d_in, self.hidden, self.d_out],
-                "parallelism": f"data-parallel x{world}, NCCL all-reduce of dW1+dW2" if world > 1 else "single GPU",
+                "parallelism": f"data-parallel x{world}" if world > 1 else "single GPU",
                 "l2": "weights 2x128 MiB bf16 + activations >> 126 MB L2"}
 
 
@@ -201,6 +202,7 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
     dw2 = session.bind(thb.MLP_DW2, torch.empty((hidden, d_out), device="cuda"))
     loss = session.bind(thb.MLP_LOSS_SUM, torch.zeros(2, dtype=torch.float64, device="cuda"))
     session.set_weights(w1, w2, s)
+    session.set_biases(stream=s)
     lr = 1e-3
     fused = None
     if world > 1 and args.dp_collective != "nccl":
@@ -210,13 +212,16 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
             fused = FusedGradientAllReduce(session, dist, mode=mode)
         if not fused.available:
             fused = None
+    from thiran_b200.distributed import bind_bias_gradients
+    bias_grads = fused.bias_grads if fused else bind_bias_gradients(session)
     collective = None
     if fused:
-        collective = ("all-reduce fused into the dW GEMMs: per-tile announce, owner rank sums "
+        collective = ("dW all-reduce fused into the dW GEMMs: per-tile announce, owner rank sums "
                       + ("with NVLink peer loads and stores" if fused.mode == "peer"
-                         else "in NVSwitch (multimem.ld_reduce + multimem.st)"))
+                         else "in NVSwitch (multimem.ld_reduce + multimem.st)")
+                      + "; bias gradients (80 KiB) by NCCL all-reduce")
     elif world > 1:
-        collective = "NCCL all-reduce of dW1+dW2"
+        collective = "NCCL all-reduce of dW1, dW2 and the bias gradients"
 
     def step():
         session.forward_backward(x, t, s)
@@ -227,6 +232,7 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
             with torch.cuda.stream(stream):
                 dist.all_reduce(dw1)
                 dist.all_reduce(dw2)
+                dist.all_reduce(bias_grads)
         session.apply_sgd(lr, s)
 
     for _ in range(args.warmup):
@@ -281,10 +287,11 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
         ts = rng.standard_normal((cb, co)).astype(np.float32)
         w1s = rng.uniform(-0.05, 0.05, (ci, ch)).astype(np.float32)
         w2s = rng.uniform(-0.05, 0.05, (ch, co)).astype(np.float32)
+        b1s, b2s = np.zeros(ch, np.float32), np.zeros(co, np.float32)
         reps = 3
         c0 = time.perf_counter()
         for _ in range(reps):
-            oracle_lib.mlp_step(xs, ts, w1s, w2s, lr)
+            oracle_lib.mlp_step_ex(xs, ts, w1s, w2s, lr, b1s, b2s)
         cpu_s = time.perf_counter() - c0
         cpu_baseline = {"value": 5 * 2 * cb * ci * ch * reps / cpu_s / 1e12, "unit": "TFLOP/s", "cores": 1,
                         "kind": "port",

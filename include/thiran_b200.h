@@ -388,7 +388,8 @@ int thb_device_check_status(int device, void* stream, char* failure, uint64_t fa
 typedef struct thb_mlp thb_mlp;
 enum {
     THB_MLP_W1 = 0, THB_MLP_W2 = 1, THB_MLP_DW1 = 2, THB_MLP_DW2 = 3,
-    THB_MLP_Y = 4, THB_MLP_H = 5, THB_MLP_LOSS_SUM = 6
+    THB_MLP_Y = 4, THB_MLP_H = 5, THB_MLP_LOSS_SUM = 6,
+    THB_MLP_B1 = 7, THB_MLP_B2 = 8, THB_MLP_DB1 = 9, THB_MLP_DB2 = 10
 };
 int thb_mlp_create(int device, uint64_t batch, uint64_t global_batch, uint64_t in, uint64_t hidden, uint64_t out,
                    thb_mlp** session, char* failure, uint64_t failure_cap);
@@ -400,13 +401,29 @@ int thb_mlp_set_weights(thb_mlp* session, const float* w1, const float* w2, void
  * aligned): fills Y, H, dW1, dW2 and the rank's loss sum. */
 int thb_mlp_forward_backward(thb_mlp* session, const float* x, const float* t, void* stream, char* failure,
                              uint64_t failure_cap);
-/* W -= lr dW for both layers (after any gradient all-reduce). */
+/* Optimizer update of every parameter (W1, W2 and, when enabled, b1, b2)
+ * after any gradient all-reduce: p -= lr * g, or with momentum (thb_mlp_
+ * set_momentum) v = mu * v + g; p -= lr * v (src/training/v0/Training.cpp:
+ * 343-381, applyOptimizer). */
 int thb_mlp_apply_sgd(thb_mlp* session, float lr, void* stream, char* failure, uint64_t failure_cap);
+/* Enables the broadcast biases of the examples/mlp.th structure:
+ * H = relu(X W1 + b1), Y = H W2 + b2, with b1 [hidden], b2 [out] copied from
+ * device memory (both NULL: zeros). Their gradients THB_MLP_DB1 / DB2 are the
+ * column sums of dH and dY (the reference's reduceToShape onto the bias,
+ * Evaluator.cpp:258-277) and lie adjacent in memory (DB2 = DB1 + hidden), so
+ * one all-reduce covers both. Re-setting resets their velocities. */
+int thb_mlp_set_biases(thb_mlp* session, const float* b1, const float* b2, void* stream, char* failure,
+                       uint64_t failure_cap);
+/* Selects SGD (momentum 0) or SGD with momentum (0 < momentum < 1, the
+ * reference's OPT05 / OPT06 bounds; otherwise status 2 with that id), and
+ * zeroes every velocity (the reference initialises them ZeroLike). */
+int thb_mlp_set_momentum(thb_mlp* session, float momentum, void* stream, char* failure, uint64_t failure_cap);
 /* One full single-device step: forward_backward then apply_sgd. */
 int thb_mlp_step(thb_mlp* session, const float* x, const float* t, float lr, void* stream, char* failure,
                  uint64_t failure_cap);
-/* Device pointer and element count of a session buffer (THB_MLP_*); Y and
- * dW are f32, H bf16, the loss sum one f64. */
+/* Device pointer and element count of a session buffer (THB_MLP_*); Y, dW,
+ * biases and their gradients are f32, H bf16, the loss sum one f64. Bias
+ * buffers are NULL with 0 elements until thb_mlp_set_biases. */
 int thb_mlp_buffer(thb_mlp* session, uint32_t which, void** device_pointer, uint64_t* elements);
 /* Replaces a session buffer by caller-owned device memory of the same size
  * and type (for example a tensor a collective library reduces in place);

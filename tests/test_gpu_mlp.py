@@ -101,6 +101,82 @@ def test_mlp_training_trajectory_matches_oracle(device):
     assert all(b < a for a, b in zip(gpu, gpu[1:]))
 
 
+@pytest.mark.parametrize("batch,d_in,hidden,d_out,momentum", [(256, 256, 512, 256, 0.0), (256, 256, 512, 256, 0.9),
+                                                              (200, 136, 520, 136, 0.5)])
+def test_mlp_biases_and_momentum_match_oracle(device, batch, d_in, hidden, d_out, momentum):
+    """The examples/mlp.th structure (broadcast biases, their gradients the
+    column sums of dH and dY) with SGD or SGD with momentum (Training.cpp:
+    366-372): three steps follow the oracle. The last shape leaves partial
+    M tiles (200 rows) and a partial N tile (520 columns), so rows past the
+    batch must add nothing to the bias gradient."""
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(21)
+    x = rng.standard_normal((batch, d_in)).astype(np.float32)
+    t = rng.standard_normal((batch, d_out)).astype(np.float32)
+    w1, w2 = xavier(rng, d_in, hidden), xavier(rng, hidden, d_out)
+    b1 = (rng.standard_normal(hidden) * 0.1).astype(np.float32)
+    b2 = (rng.standard_normal(d_out) * 0.1).astype(np.float32)
+    lr = 0.1
+    cuda = lambda a: torch.from_numpy(a).cuda()
+    s = thb.MlpSession(batch, d_in, hidden, d_out)
+    W1 = s.bind(thb.MLP_W1, torch.empty((d_in, hidden), device="cuda"))
+    W2 = s.bind(thb.MLP_W2, torch.empty((hidden, d_out), device="cuda"))
+    L = s.bind(thb.MLP_LOSS_SUM, torch.zeros(2, dtype=torch.float64, device="cuda"))
+    s.set_weights(cuda(w1), cuda(w2))
+    s.set_biases(cuda(b1), cuda(b2))
+    s.set_momentum(momentum)
+    B1 = s.bind(thb.MLP_B1, torch.empty(hidden, device="cuda"))
+    B2 = s.bind(thb.MLP_B2, torch.empty(d_out, device="cuda"))
+    B1.copy_(cuda(b1))
+    B2.copy_(cuda(b2))
+    DB1 = s.bind(thb.MLP_DB1, torch.empty(hidden, device="cuda"))
+    DB2 = s.bind(thb.MLP_DB2, torch.empty(d_out, device="cuda"))
+    X, T = cuda(x), cuda(t)
+    ws = [w1.copy(), w2.copy(), b1.copy(), b2.copy()]
+    vel = [np.zeros_like(a) for a in (w1, b1, w2, b2)] if momentum else None
+    for step in range(3):
+        s.step(X, T, lr)
+        torch.cuda.synchronize()
+        loss, dw1, dw2, db1, db2, _, _ = orc.mlp_step_ex(x, t, ws[0], ws[1], lr, ws[2], ws[3], momentum, vel)
+        assert abs(L[0].item() / (batch * d_out) - loss) <= 1e-2 * loss, step
+        assert rel(DB2.cpu().numpy(), db2) <= 1e-2, step
+        assert rel(DB1.cpu().numpy(), db1) <= 1e-2, step
+    thb.check_device_status(0)
+    assert rel(W1.cpu().numpy(), ws[0]) <= 1e-3
+    assert rel(W2.cpu().numpy(), ws[1]) <= 1e-3
+    assert rel(B1.cpu().numpy(), ws[2]) <= 1e-3
+    assert rel(B2.cpu().numpy(), ws[3]) <= 1e-3
+
+
+def test_mlp_bias_gradient_against_f32_column_sums(device):
+    """db2 is exactly what the f32 loss gradient sums to (no bf16 rounding
+    sits between Y and dY's column sums), 1e-5 relative per element."""
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(5)
+    batch, d_in, hidden, d_out = 512, 128, 256, 128
+    x = rng.standard_normal((batch, d_in)).astype(np.float32)
+    t = rng.standard_normal((batch, d_out)).astype(np.float32)
+    w1, w2 = xavier(rng, d_in, hidden), xavier(rng, hidden, d_out)
+    s = thb.MlpSession(batch, d_in, hidden, d_out)
+    s.set_weights(torch.from_numpy(w1).cuda(), torch.from_numpy(w2).cuda())
+    s.set_biases()
+    Y = s.bind(thb.MLP_Y, torch.empty((batch, d_out), device="cuda"))
+    DB2 = s.bind(thb.MLP_DB2, torch.empty(d_out, device="cuda"))
+    s.forward_backward(torch.from_numpy(x).cuda(), torch.from_numpy(t).cuda())
+    torch.cuda.synchronize()
+    y = Y.cpu().numpy()
+    g = ((y - t) * np.float32(2.0 / (batch * d_out))).astype(np.float32)
+    np.testing.assert_allclose(DB2.cpu().numpy(), g.astype(np.float64).sum(0), rtol=1e-5, atol=1e-9)
+
+
+def test_mlp_momentum_bounds(device):
+    s = thb.MlpSession(64, 64, 64, 64)
+    for bad, code in ((-0.1, "OPT05"), (float("nan"), "OPT05"), (1.0, "OPT06")):
+        with pytest.raises(thb.GpuError) as err:
+            s.set_momentum(bad)
+        assert err.value.code == code
+
+
 def test_mlp_rejects_bad_extents(device):
     with pytest.raises(thb.GpuError) as err:
         thb.MlpSession(100, 256, 512, 128)  # batch not a multiple of 8

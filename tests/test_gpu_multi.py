@@ -23,6 +23,37 @@ def gpus():
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
+MOMENTUM = 0.9
+LR = 0.05
+
+
+def problem():
+    """Shared synthetic problem: data, weights and (non-zero) biases."""
+    batch, d_in, hidden, d_out = 512, 256, 512, 256
+    rng = np.random.default_rng(8)
+    x = rng.standard_normal((batch, d_in)).astype(np.float32)
+    t = rng.standard_normal((batch, d_out)).astype(np.float32)
+    w1 = (rng.uniform(-1, 1, (d_in, hidden)) * 0.08).astype(np.float32)
+    w2 = (rng.uniform(-1, 1, (hidden, d_out)) * 0.08).astype(np.float32)
+    b1 = (rng.standard_normal(hidden) * 0.05).astype(np.float32)
+    b2 = (rng.standard_normal(d_out) * 0.05).astype(np.float32)
+    return x, t, w1, w2, b1, b2
+
+
+def session(thb, batch, global_batch, device, w1, w2, b1, b2):
+    """A biased, momentum-SGD session whose parameters live in torch tensors."""
+    d_in, hidden = w1.shape
+    d_out = w2.shape[1]
+    s = thb.MlpSession(batch, d_in, hidden, d_out, global_batch=global_batch, device=device)
+    cuda = lambda a: torch.from_numpy(a).cuda()
+    s.set_weights(cuda(w1), cuda(w2))
+    s.set_biases(cuda(b1), cuda(b2))
+    s.set_momentum(MOMENTUM)
+    params = {"w1": s.bind(thb.MLP_W1, cuda(w1)), "w2": s.bind(thb.MLP_W2, cuda(w2)),
+              "b1": s.bind(thb.MLP_B1, cuda(b1)), "b2": s.bind(thb.MLP_B2, cuda(b2))}
+    return s, params
+
+
 def _mlp_rank(rank, world, port, mode, out_path):
     import datetime
     import sys
@@ -30,26 +61,19 @@ def _mlp_rank(rank, world, port, mode, out_path):
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, root)
     import thiran_b200 as thb
-    from thiran_b200.distributed import FusedGradientAllReduce, allreduce_gradients
+    from thiran_b200.distributed import FusedGradientAllReduce, allreduce_gradients, bind_bias_gradients
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
-    batch, d_in, hidden, d_out = 512, 256, 512, 256
-    rng = np.random.default_rng(8)
-    x = rng.standard_normal((batch, d_in)).astype(np.float32)
-    t = rng.standard_normal((batch, d_out)).astype(np.float32)
-    w1 = (rng.uniform(-1, 1, (d_in, hidden)) * 0.08).astype(np.float32)
-    w2 = (rng.uniform(-1, 1, (hidden, d_out)) * 0.08).astype(np.float32)
+    x, t, w1, w2, b1, b2 = problem()
+    batch = x.shape[0]
     local = batch // world
     xs = torch.from_numpy(x[rank * local:(rank + 1) * local].copy()).cuda()
     ts = torch.from_numpy(t[rank * local:(rank + 1) * local].copy()).cuda()
-    s = thb.MlpSession(local, d_in, hidden, d_out, global_batch=batch, device=rank)
-    W1 = s.bind(thb.MLP_W1, torch.empty((d_in, hidden), device="cuda"))
-    W2 = s.bind(thb.MLP_W2, torch.empty((hidden, d_out), device="cuda"))
-    dw1 = s.bind(thb.MLP_DW1, torch.empty((d_in, hidden), device="cuda"))
-    dw2 = s.bind(thb.MLP_DW2, torch.empty((hidden, d_out), device="cuda"))
-    s.set_weights(torch.from_numpy(w1).cuda(), torch.from_numpy(w2).cuda())
+    s, params = session(thb, local, batch, rank, w1, w2, b1, b2)
+    dw1 = s.bind(thb.MLP_DW1, torch.empty(w1.shape, device="cuda"))
+    dw2 = s.bind(thb.MLP_DW2, torch.empty(w2.shape, device="cuda"))
     mc = None
     if mode != "nccl":
         mc = FusedGradientAllReduce(s, dist, mode=mode)
@@ -59,17 +83,21 @@ def _mlp_rank(rank, world, port, mode, out_path):
                 open(out_path, "w").write("unavailable")
             return
         dw1, dw2 = mc.buffers[0][1], mc.buffers[1][1]
+        dbias = mc.bias_grads
+    else:
+        dbias = bind_bias_gradients(s)
     for _ in range(3):
         s.forward_backward(xs, ts)
         if mc:
             mc.after_backward()
         else:
-            allreduce_gradients([dw1, dw2], dist)
-        s.apply_sgd(0.05)
+            allreduce_gradients([dw1, dw2, dbias], dist)
+        s.apply_sgd(LR)
     thb.check_device_status(rank)
     torch.cuda.synchronize()
     if rank == 0:
-        np.savez(out_path, dw1=dw1.cpu().numpy(), dw2=dw2.cpu().numpy(), w1=W1.cpu().numpy(), w2=W2.cpu().numpy())
+        np.savez(out_path, dw1=dw1.cpu().numpy(), dw2=dw2.cpu().numpy(), dbias=dbias.cpu().numpy(),
+                 **{k: v.cpu().numpy() for k, v in params.items()})
     s.release()
     dist.barrier()
     dist.destroy_process_group()
@@ -77,23 +105,18 @@ def _mlp_rank(rank, world, port, mode, out_path):
 
 def single_gpu_reference():
     import thiran_b200 as thb
-    batch, d_in, hidden, d_out = 512, 256, 512, 256
-    rng = np.random.default_rng(8)
-    x = rng.standard_normal((batch, d_in)).astype(np.float32)
-    t = rng.standard_normal((batch, d_out)).astype(np.float32)
-    w1 = (rng.uniform(-1, 1, (d_in, hidden)) * 0.08).astype(np.float32)
-    w2 = (rng.uniform(-1, 1, (hidden, d_out)) * 0.08).astype(np.float32)
-    s = thb.MlpSession(batch, d_in, hidden, d_out)
-    W1 = s.bind(thb.MLP_W1, torch.empty((d_in, hidden), device="cuda"))
-    W2 = s.bind(thb.MLP_W2, torch.empty((hidden, d_out), device="cuda"))
-    dw1 = s.bind(thb.MLP_DW1, torch.empty((d_in, hidden), device="cuda"))
-    dw2 = s.bind(thb.MLP_DW2, torch.empty((hidden, d_out), device="cuda"))
-    s.set_weights(torch.from_numpy(w1).cuda(), torch.from_numpy(w2).cuda())
+    from thiran_b200.distributed import bind_bias_gradients
+    x, t, w1, w2, b1, b2 = problem()
+    s, params = session(thb, x.shape[0], x.shape[0], 0, w1, w2, b1, b2)
+    dw1 = s.bind(thb.MLP_DW1, torch.empty(w1.shape, device="cuda"))
+    dw2 = s.bind(thb.MLP_DW2, torch.empty(w2.shape, device="cuda"))
+    dbias = bind_bias_gradients(s)
     X, T = torch.from_numpy(x).cuda(), torch.from_numpy(t).cuda()
     for _ in range(3):
-        s.step(X, T, 0.05)
+        s.step(X, T, LR)
     torch.cuda.synchronize()
-    return dict(dw1=dw1.cpu().numpy(), dw2=dw2.cpu().numpy(), w1=W1.cpu().numpy(), w2=W2.cpu().numpy())
+    return dict(dw1=dw1.cpu().numpy(), dw2=dw2.cpu().numpy(), dbias=dbias.cpu().numpy(),
+                **{k: v.cpu().numpy() for k, v in params.items()})
 
 
 def rel(a, b):
@@ -114,7 +137,7 @@ def test_data_parallel_mlp_matches_full_batch(tmp_path, mode, world):
     got = dict(np.load(out))
     ref = single_gpu_reference()
     # Same arithmetic, different batch split of the f32 reductions.
-    for k in ("dw1", "dw2"):
+    for k in ("dw1", "dw2", "dbias"):
         assert rel(got[k], ref[k]) <= 1e-2, k
-    for k in ("w1", "w2"):
+    for k in ("w1", "w2", "b1", "b2"):
         assert rel(got[k], ref[k]) <= 1e-4, k

@@ -162,6 +162,8 @@ SIGNATURES = {
     "thb_mlp_set_weights": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p, C.c_uint64]),
     "thb_mlp_forward_backward": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p, C.c_uint64]),
     "thb_mlp_apply_sgd": (C.c_int, [C.c_void_p, C.c_float, C.c_void_p, C.c_char_p, C.c_uint64]),
+    "thb_mlp_set_biases": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p, C.c_uint64]),
+    "thb_mlp_set_momentum": (C.c_int, [C.c_void_p, C.c_float, C.c_void_p, C.c_char_p, C.c_uint64]),
     "thb_mlp_step": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_char_p, C.c_uint64]),
     "thb_mlp_buffer": (C.c_int, [C.c_void_p, C.c_uint32, C.POINTER(C.c_void_p), C.POINTER(C.c_uint64)]),
     "thb_mlp_bind": (C.c_int, [C.c_void_p, C.c_uint32, C.c_void_p]),
@@ -174,12 +176,13 @@ SIGNATURES = {
                                           C.c_char_p, C.c_uint64]),
 }
 
-MLP_W1, MLP_W2, MLP_DW1, MLP_DW2, MLP_Y, MLP_H, MLP_LOSS_SUM = range(7)
+MLP_W1, MLP_W2, MLP_DW1, MLP_DW2, MLP_Y, MLP_H, MLP_LOSS_SUM, MLP_B1, MLP_B2, MLP_DB1, MLP_DB2 = range(11)
 
 
 class MlpSession:
-    """Two-layer MLP training session (thb_mlp): H = relu(X W1), Y = H W2,
-    L = mean((Y - T)^2), SGD. Tensors are torch CUDA tensors."""
+    """Two-layer MLP training session (thb_mlp): H = relu(X W1 [+ b1]),
+    Y = H W2 [+ b2], L = mean((Y - T)^2), SGD or SGD with momentum. Tensors
+    are torch CUDA tensors."""
 
     def __init__(self, batch, d_in, hidden, d_out, global_batch=None, device=0):
         self.batch, self.d_in, self.hidden, self.d_out = batch, d_in, hidden, d_out
@@ -203,6 +206,15 @@ class MlpSession:
 
     def apply_sgd(self, lr, stream=0):
         self._call("thb_mlp_apply_sgd", C.c_float(lr), C.c_void_p(stream))
+
+    def set_biases(self, b1=None, b2=None, stream=0):
+        """Enables the broadcast biases (zeros when not given)."""
+        self._call("thb_mlp_set_biases", None if b1 is None else b1.data_ptr(),
+                   None if b2 is None else b2.data_ptr(), C.c_void_p(stream))
+
+    def set_momentum(self, momentum, stream=0):
+        """SGD (0) or SGD with momentum; velocities restart at zero."""
+        self._call("thb_mlp_set_momentum", C.c_float(momentum), C.c_void_p(stream))
 
     def step(self, x, t, lr, stream=0):
         self._call("thb_mlp_step", x.data_ptr(), t.data_ptr(), C.c_float(lr), C.c_void_p(stream))

@@ -1,5 +1,6 @@
 // extern "C" surface of libthiran_b200.so (declared in include/thiran_b200.h).
 #include <chrono>
+#include <cmath>
 #include <cstring>
 #include <memory>
 #include <thread>
@@ -590,7 +591,7 @@ int thb_mlp_create(int device, uint64_t batch, uint64_t globalBatch, uint64_t in
         b.dh = s->alloc(batch * hidden * 2);
         b.dw1 = static_cast<float*>(s->alloc(in * hidden * 4));
         b.dw2 = static_cast<float*>(s->alloc(hidden * out * 4));
-        b.lossPartials = static_cast<double*>(s->alloc(mlp::lossPartialCount(info.smCount) * 8));
+        b.lossPartials = static_cast<double*>(s->alloc(mlp::lossPartialCount(batch, out, info.smCount) * 8));
         b.lossSum = static_cast<double*>(s->alloc(8));
         *session = s.release();
         return THB_STATUS_OK;
@@ -656,9 +657,71 @@ int thb_mlp_buffer(thb_mlp* s, uint32_t which, void** pointer, uint64_t* element
     case THB_MLP_Y: *pointer = b.y; if (elements) *elements = b.batch * b.out; break;
     case THB_MLP_H: *pointer = b.h; if (elements) *elements = b.batch * b.hidden; break;
     case THB_MLP_LOSS_SUM: *pointer = b.lossSum; if (elements) *elements = 1; break;
+    case THB_MLP_B1: *pointer = b.b1; if (elements) *elements = b.b1 ? b.hidden : 0; break;
+    case THB_MLP_B2: *pointer = b.b2; if (elements) *elements = b.b1 ? b.out : 0; break;
+    case THB_MLP_DB1: *pointer = b.db1; if (elements) *elements = b.b1 ? b.hidden : 0; break;
+    case THB_MLP_DB2: *pointer = b.db2; if (elements) *elements = b.b1 ? b.out : 0; break;
     default: return THB_STATUS_ABI;
     }
     return THB_STATUS_OK;
+}
+
+int thb_mlp_set_biases(thb_mlp* s, const float* b1, const float* b2, void* stream, char* failure, uint64_t cap) {
+    return guarded(failure, cap, [&] {
+        if (!s) fail(Category::Validation, "GPU-MLP-ARGUMENT", "null session");
+        if (!b1 != !b2) fail(Category::Validation, "GPU-MLP-ARGUMENT", "give both biases or neither");
+        useDevice(s->device);
+        auto st = static_cast<cudaStream_t>(stream);
+        auto& b = s->b;
+        if (!b.b1) {
+            b.b1 = static_cast<float*>(s->alloc(b.hidden * 4));
+            b.b2 = static_cast<float*>(s->alloc(b.out * 4));
+            // db1 and db2 adjacent, so one collective call can reduce both.
+            b.db1 = static_cast<float*>(s->alloc((b.hidden + b.out) * 4));
+            b.db2 = b.db1 + b.hidden;
+            b.dyColSums = static_cast<float*>(s->alloc(mlp::lossRowChunks(b.batch, b.out, s->smCount) * b.out * 4));
+            b.dhColSums = static_cast<float*>(s->alloc(gemm::colSumRows(b.batch) * b.hidden * 4));
+        }
+        if (b1) {
+            cudaCheck(cudaMemcpyAsync(b.b1, b1, b.hidden * 4, cudaMemcpyDeviceToDevice, st), "cudaMemcpyAsync(b1)");
+            cudaCheck(cudaMemcpyAsync(b.b2, b2, b.out * 4, cudaMemcpyDeviceToDevice, st), "cudaMemcpyAsync(b2)");
+        } else {
+            cudaCheck(cudaMemsetAsync(b.b1, 0, b.hidden * 4, st), "cudaMemsetAsync(b1)");
+            cudaCheck(cudaMemsetAsync(b.b2, 0, b.out * 4, st), "cudaMemsetAsync(b2)");
+        }
+        if (b.vb1) {
+            cudaCheck(cudaMemsetAsync(b.vb1, 0, b.hidden * 4, st), "cudaMemsetAsync(vb1)");
+            cudaCheck(cudaMemsetAsync(b.vb2, 0, b.out * 4, st), "cudaMemsetAsync(vb2)");
+        }
+        return THB_STATUS_OK;
+    });
+}
+
+int thb_mlp_set_momentum(thb_mlp* s, float momentum, void* stream, char* failure, uint64_t cap) {
+    return guarded(failure, cap, [&] {
+        if (!s) fail(Category::Validation, "GPU-MLP-ARGUMENT", "null session");
+        // The reference's optimizer checks (Training.cpp OPT05 / OPT06).
+        if (!std::isfinite(momentum) || momentum < 0.0f)
+            fail(Category::Semantic, "OPT05", "momentum must be finite and non-negative");
+        if (momentum >= 1.0f) fail(Category::Semantic, "OPT06", "momentum must be below 1");
+        useDevice(s->device);
+        auto st = static_cast<cudaStream_t>(stream);
+        auto& b = s->b;
+        if (momentum > 0.0f && !b.vw1) {
+            b.vw1 = static_cast<float*>(s->alloc(b.in * b.hidden * 4));
+            b.vw2 = static_cast<float*>(s->alloc(b.hidden * b.out * 4));
+            b.vb1 = static_cast<float*>(s->alloc(b.hidden * 4));
+            b.vb2 = static_cast<float*>(s->alloc(b.out * 4));
+        }
+        if (b.vw1) {  // velocities start at zero (ZeroLike, Training.cpp state init)
+            cudaCheck(cudaMemsetAsync(b.vw1, 0, b.in * b.hidden * 4, st), "cudaMemsetAsync(vW1)");
+            cudaCheck(cudaMemsetAsync(b.vw2, 0, b.hidden * b.out * 4, st), "cudaMemsetAsync(vW2)");
+            cudaCheck(cudaMemsetAsync(b.vb1, 0, b.hidden * 4, st), "cudaMemsetAsync(vb1)");
+            cudaCheck(cudaMemsetAsync(b.vb2, 0, b.out * 4, st), "cudaMemsetAsync(vb2)");
+        }
+        b.momentum = momentum;
+        return THB_STATUS_OK;
+    });
 }
 
 int thb_mlp_enable_timing(thb_mlp* s, int enabled) {
@@ -733,6 +796,10 @@ int thb_mlp_bind(thb_mlp* s, uint32_t which, void* pointer) {
     case THB_MLP_Y: b.y = static_cast<float*>(pointer); break;
     case THB_MLP_H: b.h = pointer; break;
     case THB_MLP_LOSS_SUM: b.lossSum = static_cast<double*>(pointer); break;
+    case THB_MLP_B1: if (!b.b1) return THB_STATUS_ABI; b.b1 = static_cast<float*>(pointer); break;
+    case THB_MLP_B2: if (!b.b1) return THB_STATUS_ABI; b.b2 = static_cast<float*>(pointer); break;
+    case THB_MLP_DB1: if (!b.b1) return THB_STATUS_ABI; b.db1 = static_cast<float*>(pointer); break;
+    case THB_MLP_DB2: if (!b.b1) return THB_STATUS_ABI; b.db2 = static_cast<float*>(pointer); break;
     default: return THB_STATUS_ABI;
     }
     return THB_STATUS_OK;

@@ -146,7 +146,26 @@ struct Params {
     float* cPeers[kMaxRanks];       // peer mode
     uint32_t* flagsPeers[kMaxRanks];
     uint32_t rank, world, target;
+    const float* bias;              // [n] or null
+    float* colSums;                 // [mTiles * 4][n] or null (kEpiMaskBf16)
 };
+
+// Lane j ends with the sum over the warp's 32 lanes of s[j] (a butterfly
+// transpose-reduce: 31 shuffles, fixed order, so the result is
+// reproducible). Destroys s.
+__device__ __forceinline__ float columnSum32(float (&s)[32], uint32_t lane) {
+#pragma unroll
+    for (int width = 16; width >= 1; width >>= 1) {
+        const bool upper = (lane & width) != 0;
+#pragma unroll
+        for (int i = 0; i < width; ++i) {
+            const float send = upper ? s[i] : s[i + width];
+            const float keep = upper ? s[i + width] : s[i];
+            s[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, width));
+        }
+    }
+    return s[0];
+}
 
 __device__ __forceinline__ void tileCoords(uint32_t tile, const Params& p, uint32_t& mb, uint32_t& nb) {
     constexpr uint32_t kGroup = 8;  // m-blocks per raster group (L2 reuse of B tiles)
@@ -492,12 +511,18 @@ __global__ void __launch_bounds__(threadsFor(EPI), 1)
                 uint32_t r[32];
                 tmemLoad32(tmemBase + ((quadrant * 32u) << 16) + acc * kBN + chunk * 32u, r);
                 const uint64_t col0 = static_cast<uint64_t>(nb) * kBN + chunk * 32u;
-                if (grow >= p.m || col0 >= p.n) continue;
+                const bool rowValid = grow < p.m;
+                // Column sums need every lane of the warp (rows past M add 0).
+                const bool sums = EPI == kEpiMaskBf16 && p.colSums != nullptr;
+                if (col0 >= p.n || (!rowValid && !sums)) continue;
                 const bool full32 = col0 + 32 <= p.n;
                 float aux[32];
                 if constexpr (EPI == kEpiMaskBf16) {
                     const __nv_bfloat16* src = p.aux + grow * p.ldAux + col0;
-                    if (full32 && (reinterpret_cast<uintptr_t>(src) % 16 == 0)) {
+                    if (!rowValid) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) aux[j] = 0.0f;
+                    } else if (full32 && (reinterpret_cast<uintptr_t>(src) % 16 == 0)) {
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
                             const uint4 v = *reinterpret_cast<const uint4*>(src + q * 8);
@@ -519,7 +544,36 @@ __global__ void __launch_bounds__(threadsFor(EPI), 1)
                 }
                 float v[32];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = epilogueValue<EPI>(__uint_as_float(r[j]), aux[j]);
+                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                if (p.bias) {
+                    const float* bsrc = p.bias + col0;
+                    if (full32 && reinterpret_cast<uintptr_t>(bsrc) % 16 == 0) {
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            const float4 bv = __ldg(reinterpret_cast<const float4*>(bsrc) + q);
+                            v[4 * q] = __fadd_rn(v[4 * q], bv.x);
+                            v[4 * q + 1] = __fadd_rn(v[4 * q + 1], bv.y);
+                            v[4 * q + 2] = __fadd_rn(v[4 * q + 2], bv.z);
+                            v[4 * q + 3] = __fadd_rn(v[4 * q + 3], bv.w);
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < p.n) v[j] = __fadd_rn(v[j], __ldg(bsrc + j));
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = epilogueValue<EPI>(v[j], aux[j]);
+                if constexpr (EPI == kEpiMaskBf16) {
+                    if (sums) {
+                        float s[32];
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) s[j] = rowValid ? v[j] : 0.0f;
+                        const float total = columnSum32(s, lane);
+                        if (col0 + lane < p.n) p.colSums[(static_cast<uint64_t>(mb) * 4 + quadrant) * p.n + col0 + lane] = total;
+                        if (!rowValid) continue;
+                    }
+                }
                 if constexpr (EPI == kEpiF32 || EPI == kEpiAllReduceF32) {
                     float* dst = static_cast<float*>(p.c) + grow * p.ldc + col0;
                     if (full32 && reinterpret_cast<uintptr_t>(dst) % 16 == 0) {
@@ -646,6 +700,9 @@ const char* validate(const Problem& q) {
     if (q.ldc < q.n) return "ldc smaller than N";
     if (q.epilogue == kEpiMaskBf16 && (!q.aux || q.ldAux < q.n)) return "mask epilogue needs an auxiliary bf16 matrix";
     if (q.epilogue < kEpiF32 || q.epilogue > kEpiAllReduceF32) return "unknown epilogue";
+    if (q.bias && (q.epilogue == kEpiMaskBf16 || q.epilogue == kEpiAllReduceF32))
+        return "a bias applies to the f32, bf16 and ReLU epilogues only";
+    if (q.colSums && q.epilogue != kEpiMaskBf16) return "column sums are produced by the mask epilogue only";
     if (q.epilogue == kEpiAllReduceF32) {
         const AllReduce& r = q.reduce;
         if (r.world == 0 || r.world > static_cast<uint32_t>(kMaxRanks) || r.rank >= r.world)
@@ -663,6 +720,8 @@ const char* validate(const Problem& q) {
 }
 
 std::uint64_t tileCount(std::uint64_t m, std::uint64_t n) { return ((m + kBM - 1) / kBM) * ((n + kBN - 1) / kBN); }
+
+std::uint64_t colSumRows(std::uint64_t m) { return 4 * ((m + kBM - 1) / kBM); }
 
 cudaError_t run(const Problem& q, int smCount, uint32_t* status, cudaStream_t stream) {
     CUtensorMap a, b;
@@ -692,6 +751,8 @@ cudaError_t run(const Problem& q, int smCount, uint32_t* status, cudaStream_t st
     p.rank = q.reduce.rank;
     p.world = q.reduce.world ? q.reduce.world : 1;
     p.target = q.reduce.target;
+    p.bias = q.bias;
+    p.colSums = q.colSums;
     if (q.aMajorMN) {
         if (q.bMajorMN) return launchEpi<true, true>(q.epilogue, a, b, p, smCount, stream);
         return launchEpi<true, false>(q.epilogue, a, b, p, smCount, stream);

@@ -55,7 +55,17 @@ struct Problem {
     std::uint64_t ldAux = 0;
     void* c2 = nullptr;         // optional f32 copy (bf16 epilogues), ld = ldc
     AllReduce reduce;           // kEpiAllReduceF32
+    // Optional f32 bias [N] added to every row before the epilogue op (F32,
+    // Bf16 and ReluBf16 epilogues): C = op(acc + bias).
+    const float* bias = nullptr;
+    // Optional column partial sums of the f32 epilogue result (MaskBf16):
+    // colSums[(mTile * 4 + q) * N + j] = sum over rows 32q..32q+31 of the
+    // M tile of C[row][j], rows past M counting 0. Fixed summation order.
+    float* colSums = nullptr;
 };
+
+// Rows of partial sums `colSums` receives for an M x N problem.
+std::uint64_t colSumRows(std::uint64_t m);
 
 // Returns an error text for an invalid problem, or nullptr.
 const char* validate(const Problem&);

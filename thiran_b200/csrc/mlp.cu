@@ -3,14 +3,19 @@
 // The reference trains only in its Evaluator: trainingStep
 // (src/training/v0/Training.cpp:382-432) runs the generated forward, the
 // reverse-AD backward (src/autodiff/v0/Autodiff.cpp:72-294; matmul rule
-// :216-227) and SGD p <- p - lr*g (Training.cpp:368-371). Here one step is
+// :216-227) and SGD, optionally with momentum (Training.cpp:366-372). Here
+// one step is
 //   Xb = bf16(X)
-//   H  = relu(Xb W1b)              GEMM, ReLU fused in the epilogue (bf16 out)
-//   Y  = H W2b                     GEMM (f32 out)
-//   D  = Y - T; loss += sum D^2; dY = bf16(D * 2/(B*O))   one fused pass
-//   dH = (dY W2b^T) * [H > 0]      GEMM, mask fused in the epilogue
+//   H  = relu(Xb W1b + b1)         GEMM, bias + ReLU fused in the epilogue (bf16 out)
+//   Y  = H W2b + b2                GEMM, bias fused (f32 out)
+//   D  = Y - T; loss += sum D^2; G = D * 2/(B*O); dY = bf16(G);
+//   db2 = column sums of G         one fused pass (+ a small partials reduce)
+//   dH = (dY W2b^T) * [H > 0]      GEMM, mask and db1 column partials fused
 //   dW2 = H^T dY ; dW1 = Xb^T dH   GEMMs with MN-major operands (no transposes)
-//   W -= lr dW ; Wb = bf16(W)      one fused pass per weight
+//   p -= lr * d (d = g, or v = mu v + g) ; Wb = bf16(W)   one fused pass per parameter
+// The biases b1 [hidden], b2 [out] broadcast over the rows (the
+// examples/mlp.th structure; their gradients are the reference's
+// reduceToShape, Evaluator.cpp:258-277) and are optional.
 // W1 is stored [in][hidden], W2 [hidden][out] (the reference's X*W1 layout).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -47,17 +52,32 @@ __device__ __forceinline__ T warpSum(T v) {
     return v;
 }
 
-// D = Y - T; partial[block] = sum D^2 (f64); dY = bf16(D * scale).
+// D = Y - T; G = D * scale; dY = bf16(G). Block (x, y) covers columns
+// 256x .. 256x+255 of the rows of chunk y (one column per thread, so a warp
+// reads 128 contiguous bytes per row): partial[block] = sum D^2 (f64) and,
+// when colSums is given, colSums[y][col] = sum over the chunk's rows of G
+// (f32, row order).
 __global__ void __launch_bounds__(kThreads) lossGradKernel(const float* __restrict__ y, const float* __restrict__ t,
                                                            __nv_bfloat16* __restrict__ dy, double* __restrict__ partials,
-                                                           std::uint64_t n, float scale) {
+                                                           float* __restrict__ colSums, std::uint64_t rows,
+                                                           std::uint64_t cols, std::uint64_t rowsPerChunk, float scale) {
     __shared__ double red[kThreads / 32];
     double acc = 0.0;
-    const std::uint64_t stride = static_cast<std::uint64_t>(gridDim.x) * kThreads;
-    for (std::uint64_t i = static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n; i += stride) {
-        const float d = __fsub_rn(y[i], t[i]);
-        acc += static_cast<double>(d) * static_cast<double>(d);
-        dy[i] = __float2bfloat16_rn(__fmul_rn(d, scale));
+    float colAcc = 0.0f;
+    const std::uint64_t col = static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
+    const std::uint64_t r0 = static_cast<std::uint64_t>(blockIdx.y) * rowsPerChunk;
+    const std::uint64_t r1 = r0 + rowsPerChunk < rows ? r0 + rowsPerChunk : rows;
+    if (col < cols) {
+#pragma unroll 4
+        for (std::uint64_t r = r0; r < r1; ++r) {
+            const std::uint64_t i = r * cols + col;
+            const float d = __fsub_rn(__ldcs(y + i), __ldcs(t + i));
+            acc += static_cast<double>(d) * static_cast<double>(d);
+            const float g = __fmul_rn(d, scale);
+            dy[i] = __float2bfloat16_rn(g);
+            colAcc = __fadd_rn(colAcc, g);
+        }
+        if (colSums) colSums[static_cast<std::uint64_t>(blockIdx.y) * cols + col] = colAcc;
     }
     acc = warpSum(acc);
     if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = acc;
@@ -65,8 +85,18 @@ __global__ void __launch_bounds__(kThreads) lossGradKernel(const float* __restri
     if (threadIdx.x == 0) {
         double s = red[0];
         for (unsigned w = 1; w < kThreads / 32; ++w) s += red[w];
-        partials[blockIdx.x] = s;
+        partials[static_cast<std::uint64_t>(blockIdx.y) * gridDim.x + blockIdx.x] = s;
     }
+}
+
+// out[col] = sum over r of partials[r][col], f64 in row order, rounded once.
+__global__ void __launch_bounds__(kThreads) columnReduceKernel(const float* __restrict__ partials, std::uint64_t rows,
+                                                               std::uint64_t cols, float* __restrict__ out) {
+    const std::uint64_t col = static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
+    if (col >= cols) return;
+    double acc = 0.0;
+    for (std::uint64_t r = 0; r < rows; ++r) acc += static_cast<double>(partials[r * cols + col]);
+    out[col] = static_cast<float>(acc);
 }
 
 __global__ void __launch_bounds__(kThreads) sumPartialsKernel(const double* __restrict__ partials, unsigned count,
@@ -84,29 +114,52 @@ __global__ void __launch_bounds__(kThreads) sumPartialsKernel(const double* __re
     }
 }
 
-// w = w - lr * g ; wb = bf16(w)   (Training.cpp:368-371 with plain SGD)
+// One parameter update (Training.cpp:366-372): d = g, or with momentum
+// d = v*mu + g and v = d; p = p - d*lr. Each operation rounds to f32.
+__device__ __forceinline__ float updateOne(float p, float g, float* v, float lr, float mu) {
+    float d = g;
+    if (v) {
+        d = __fadd_rn(__fmul_rn(*v, mu), g);
+        *v = d;
+    }
+    return __fsub_rn(p, __fmul_rn(d, lr));
+}
+
+// p = update(p, g, v); pb = bf16(p) when pb is given. Vectorised by 4.
 __global__ void __launch_bounds__(kThreads) sgdKernel(float* __restrict__ w, const float* __restrict__ g,
-                                                      __nv_bfloat16* __restrict__ wb, std::uint64_t n, float lr) {
+                                                      float* __restrict__ vel, __nv_bfloat16* __restrict__ wb,
+                                                      std::uint64_t n, float lr, float mu) {
     const std::uint64_t stride = static_cast<std::uint64_t>(gridDim.x) * kThreads;
     const std::uint64_t packets = n / 4;
     for (std::uint64_t i = static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x; i < packets; i += stride) {
-        float4 v = reinterpret_cast<float4*>(w)[i];
+        float4 p = reinterpret_cast<float4*>(w)[i];
         const float4 d = __ldcs(reinterpret_cast<const float4*>(g) + i);
-        v.x = __fsub_rn(v.x, __fmul_rn(lr, d.x));
-        v.y = __fsub_rn(v.y, __fmul_rn(lr, d.y));
-        v.z = __fsub_rn(v.z, __fmul_rn(lr, d.z));
-        v.w = __fsub_rn(v.w, __fmul_rn(lr, d.w));
-        reinterpret_cast<float4*>(w)[i] = v;
-        __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
-        uint2 packed;
-        packed.x = *reinterpret_cast<std::uint32_t*>(&lo);
-        packed.y = *reinterpret_cast<std::uint32_t*>(&hi);
-        reinterpret_cast<uint2*>(wb)[i] = packed;
+        if (vel) {
+            float4 v = reinterpret_cast<float4*>(vel)[i];
+            p.x = updateOne(p.x, d.x, &v.x, lr, mu);
+            p.y = updateOne(p.y, d.y, &v.y, lr, mu);
+            p.z = updateOne(p.z, d.z, &v.z, lr, mu);
+            p.w = updateOne(p.w, d.w, &v.w, lr, mu);
+            reinterpret_cast<float4*>(vel)[i] = v;
+        } else {
+            p.x = updateOne(p.x, d.x, nullptr, lr, mu);
+            p.y = updateOne(p.y, d.y, nullptr, lr, mu);
+            p.z = updateOne(p.z, d.z, nullptr, lr, mu);
+            p.w = updateOne(p.w, d.w, nullptr, lr, mu);
+        }
+        reinterpret_cast<float4*>(w)[i] = p;
+        if (wb) {
+            __nv_bfloat162 lo = __floats2bfloat162_rn(p.x, p.y), hi = __floats2bfloat162_rn(p.z, p.w);
+            uint2 packed;
+            packed.x = *reinterpret_cast<std::uint32_t*>(&lo);
+            packed.y = *reinterpret_cast<std::uint32_t*>(&hi);
+            reinterpret_cast<uint2*>(wb)[i] = packed;
+        }
     }
     if (blockIdx.x == 0 && threadIdx.x < n % 4) {
         const std::uint64_t k = packets * 4 + threadIdx.x;
-        w[k] = __fsub_rn(w[k], __fmul_rn(lr, g[k]));
-        wb[k] = __float2bfloat16_rn(w[k]);
+        w[k] = updateOne(w[k], g[k], vel ? vel + k : nullptr, lr, mu);
+        if (wb) wb[k] = __float2bfloat16_rn(w[k]);
     }
 }
 
@@ -118,7 +171,16 @@ unsigned gridFor(std::uint64_t work, int smCount) {
 
 } // namespace
 
-unsigned lossPartialCount(int smCount) { return static_cast<unsigned>(smCount) * 4; }
+unsigned lossRowChunks(std::uint64_t rows, std::uint64_t cols, int smCount) {
+    const std::uint64_t colBlocks = (cols + kThreads - 1) / kThreads;
+    std::uint64_t chunks = (static_cast<std::uint64_t>(smCount) * 4 + colBlocks - 1) / colBlocks;
+    if (chunks > rows) chunks = rows;
+    return static_cast<unsigned>(chunks < 1 ? 1 : chunks);
+}
+
+unsigned lossPartialCount(std::uint64_t rows, std::uint64_t cols, int smCount) {
+    return static_cast<unsigned>((cols + kThreads - 1) / kThreads) * lossRowChunks(rows, cols, smCount);
+}
 
 cudaError_t castToBf16(const float* x, void* y, std::uint64_t n, int smCount, cudaStream_t s) {
     if (n == 0) return cudaSuccess;
@@ -126,19 +188,34 @@ cudaError_t castToBf16(const float* x, void* y, std::uint64_t n, int smCount, cu
     return cudaGetLastError();
 }
 
+// Loss, dY and (when db is given) db = column sums of the f32 gradient G.
 cudaError_t lossAndGradient(const float* y, const float* t, void* dy, double* partials, double* lossSum,
-                            std::uint64_t n, float scale, int smCount, cudaStream_t s) {
-    const unsigned parts = lossPartialCount(smCount);
-    lossGradKernel<<<parts, kThreads, 0, s>>>(y, t, static_cast<__nv_bfloat16*>(dy), partials, n, scale);
+                            float* colSums, float* db, std::uint64_t rows, std::uint64_t cols, float scale, int smCount,
+                            cudaStream_t s) {
+    const unsigned chunks = lossRowChunks(rows, cols, smCount);
+    const unsigned colBlocks = static_cast<unsigned>((cols + kThreads - 1) / kThreads);
+    const std::uint64_t rowsPerChunk = (rows + chunks - 1) / chunks;
+    lossGradKernel<<<dim3(colBlocks, chunks), kThreads, 0, s>>>(y, t, static_cast<__nv_bfloat16*>(dy), partials,
+                                                                db ? colSums : nullptr, rows, cols, rowsPerChunk, scale);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    sumPartialsKernel<<<1, kThreads, 0, s>>>(partials, parts, lossSum);
+    sumPartialsKernel<<<1, kThreads, 0, s>>>(partials, colBlocks * chunks, lossSum);
+    if ((e = cudaGetLastError()) != cudaSuccess || !db) return e;
+    columnReduceKernel<<<colBlocks, kThreads, 0, s>>>(colSums, chunks, cols, db);
     return cudaGetLastError();
 }
 
-cudaError_t sgdUpdate(float* w, const float* g, void* wb, std::uint64_t n, float lr, int smCount, cudaStream_t s) {
+cudaError_t columnSums(const float* partials, std::uint64_t rows, std::uint64_t cols, float* out, cudaStream_t s) {
+    columnReduceKernel<<<static_cast<unsigned>((cols + kThreads - 1) / kThreads), kThreads, 0, s>>>(partials, rows, cols,
+                                                                                                 out);
+    return cudaGetLastError();
+}
+
+cudaError_t sgdUpdate(float* p, const float* g, float* v, void* pb, std::uint64_t n, float lr, float momentum,
+                      int smCount, cudaStream_t s) {
     if (n == 0) return cudaSuccess;
-    sgdKernel<<<gridFor(n / 4 + 1, smCount), kThreads, 0, s>>>(w, g, static_cast<__nv_bfloat16*>(wb), n, lr);
+    sgdKernel<<<gridFor(n / 4 + 1, smCount), kThreads, 0, s>>>(p, g, v, static_cast<__nv_bfloat16*>(pb), n, lr,
+                                                                 momentum);
     return cudaGetLastError();
 }
 
@@ -161,6 +238,7 @@ cudaError_t forwardBackward(const Buffers& b, const float* x, const float* t, in
     q.a = b.xb; q.lda = b.in;
     q.b = b.w1b; q.bMajorMN = true; q.ldb = b.hidden;
     q.c = b.h; q.ldc = b.hidden; q.epilogue = gemm::kEpiReluBf16;
+    q.bias = b.b1;  // relu(acc + b1)
     if ((e = runGemm(q)) != cudaSuccess) return e;
     // Y = H W2b: A = H [B][hidden] K-major, B = W2b [hidden][out] MN-major.
     q = {};
@@ -168,10 +246,12 @@ cudaError_t forwardBackward(const Buffers& b, const float* x, const float* t, in
     q.a = b.h; q.lda = b.hidden;
     q.b = b.w2b; q.bMajorMN = true; q.ldb = b.out;
     q.c = b.y; q.ldc = b.out; q.epilogue = gemm::kEpiF32;
+    q.bias = b.b2;  // acc + b2
     if ((e = runGemm(q)) != cudaSuccess) return e;
-    // Loss and dY = 2 (Y - T) / (global batch * out).
+    // Loss and dY = 2 (Y - T) / (global batch * out); db2 = column sums of dY.
     const float scale = 2.0f / static_cast<float>(b.globalBatch * b.out);
-    if ((e = lossAndGradient(b.y, t, b.dy, b.lossPartials, b.lossSum, b.batch * b.out, scale, smCount, s)) != cudaSuccess)
+    if ((e = lossAndGradient(b.y, t, b.dy, b.lossPartials, b.lossSum, b.dyColSums, b.b1 ? b.db2 : nullptr, b.batch,
+                             b.out, scale, smCount, s)) != cudaSuccess)
         return e;
     // dH = (dY W2b^T) * [H > 0]: A = dY [B][out] K-major, B = W2b [hidden][out] K-major (N=hidden).
     q = {};
@@ -180,7 +260,9 @@ cudaError_t forwardBackward(const Buffers& b, const float* x, const float* t, in
     q.b = b.w2b; q.ldb = b.out;
     q.c = b.dh; q.ldc = b.hidden; q.epilogue = gemm::kEpiMaskBf16;
     q.aux = b.h; q.ldAux = b.hidden;
+    if (b.b1) q.colSums = b.dhColSums;  // db1 = column sums of dH (f32, before rounding)
     if ((e = runGemm(q)) != cudaSuccess) return e;
+    if (b.b1 && (e = columnSums(b.dhColSums, gemm::colSumRows(b.batch), b.hidden, b.db1, s)) != cudaSuccess) return e;
     // dW2 = H^T dY: A = H stored [B][hidden] (MN-major), B = dY stored [B][out] (MN-major).
     q = {};
     q.m = b.hidden; q.n = b.out; q.k = b.batch;
@@ -200,9 +282,15 @@ cudaError_t forwardBackward(const Buffers& b, const float* x, const float* t, in
 }
 
 cudaError_t applySgd(const Buffers& b, float lr, int smCount, cudaStream_t s) {
-    cudaError_t e = sgdUpdate(b.w1, b.dw1, b.w1b, b.in * b.hidden, lr, smCount, s);
+    const float mu = b.momentum;
+    const bool m = mu > 0.0f;
+    cudaError_t e = sgdUpdate(b.w1, b.dw1, m ? b.vw1 : nullptr, b.w1b, b.in * b.hidden, lr, mu, smCount, s);
     if (e != cudaSuccess) return e;
-    return sgdUpdate(b.w2, b.dw2, b.w2b, b.hidden * b.out, lr, smCount, s);
+    if ((e = sgdUpdate(b.w2, b.dw2, m ? b.vw2 : nullptr, b.w2b, b.hidden * b.out, lr, mu, smCount, s)) != cudaSuccess)
+        return e;
+    if (!b.b1) return cudaSuccess;
+    if ((e = sgdUpdate(b.b1, b.db1, m ? b.vb1 : nullptr, nullptr, b.hidden, lr, mu, smCount, s)) != cudaSuccess) return e;
+    return sgdUpdate(b.b2, b.db2, m ? b.vb2 : nullptr, nullptr, b.out, lr, mu, smCount, s);
 }
 
 } // namespace thb::mlp

@@ -25,6 +25,20 @@ struct Buffers {
     float* dw2 = nullptr;      // f32 [hidden][out]
     double* lossPartials = nullptr;
     double* lossSum = nullptr; // sum over this rank's batch of (Y - T)^2
+    // Broadcast biases (examples/mlp.th structure), enabled by setting b1:
+    // H = relu(X W1 + b1), Y = H W2 + b2, gradients = column sums of dH, dY.
+    float* b1 = nullptr;       // f32 [hidden]
+    float* b2 = nullptr;       // f32 [out]
+    float* db1 = nullptr;      // f32 [hidden]
+    float* db2 = nullptr;      // f32 [out]
+    float* dyColSums = nullptr;  // f32 [lossRowChunks][out] partial column sums of dY
+    float* dhColSums = nullptr;  // f32 [colSumRows(batch)][hidden] partial column sums of dH
+    // SGD with momentum (Training.cpp:366-372) when momentum > 0: velocities.
+    float momentum = 0.0f;
+    float* vw1 = nullptr;
+    float* vw2 = nullptr;
+    float* vb1 = nullptr;
+    float* vb2 = nullptr;
     // Data-parallel gradient all-reduce fused into the dW GEMMs (no peers =
     // plain local store). The caller advances `target` every step.
     gemm::AllReduce dw1Reduce;
@@ -50,9 +64,15 @@ struct GemmTimer {
     }
 };
 
-unsigned lossPartialCount(int smCount);
+// Loss kernel layout: column blocks of 256 x row chunks; one f64 loss
+// partial per block.
+unsigned lossRowChunks(std::uint64_t rows, std::uint64_t cols, int smCount);
+unsigned lossPartialCount(std::uint64_t rows, std::uint64_t cols, int smCount);
 cudaError_t castToBf16(const float* x, void* y, std::uint64_t n, int smCount, cudaStream_t s);
-cudaError_t sgdUpdate(float* w, const float* g, void* wb, std::uint64_t n, float lr, int smCount, cudaStream_t s);
+// p -= lr * d with d = g (v null) or d = v * momentum + g, v = d; refreshes
+// the bf16 copy pb when given.
+cudaError_t sgdUpdate(float* p, const float* g, float* v, void* pb, std::uint64_t n, float lr, float momentum,
+                      int smCount, cudaStream_t s);
 // Forward, loss and backward: fills h, y, dy, dh, dw1, dw2 and lossSum.
 cudaError_t forwardBackward(const Buffers&, const float* x, const float* t, int smCount, std::uint32_t* status,
                             cudaStream_t s, GemmTimer* timer = nullptr);

@@ -92,10 +92,29 @@ class FusedGradientAllReduce:
                 session.bind_reduction(which, [int(p) for p in h.buffer_ptrs], [p + 4 * offset for p in flag_ptrs],
                                        rank, world, h.multicast_ptr if self.mode == "switch" else None)
                 offset += n
+        self.dist = dist
+        self.bias_grads = bind_bias_gradients(session)
 
     def after_backward(self):
-        """Wait until every rank's owned tiles hold their totals everywhere."""
+        """Wait until every rank's owned tiles hold their totals everywhere;
+        the bias gradients (hidden + out floats) are summed by NCCL."""
         self.flag_handle.barrier(channel=1, timeout_ms=self.BARRIER_TIMEOUT_MS)
+        if self.bias_grads is not None:
+            self.dist.all_reduce(self.bias_grads, group=self.group)
+
+
+def bind_bias_gradients(session):
+    """When the session has biases, binds db1 and db2 to one torch tensor
+    [hidden + out] (db2 right after db1) so one collective sums both, and
+    returns it; otherwise None."""
+    import torch
+    from . import MLP_B1, MLP_DB1, MLP_DB2
+    if session.buffer(MLP_B1)[1] == 0:
+        return None
+    grads = torch.empty(session.hidden + session.d_out, dtype=torch.float32, device="cuda")
+    session.bind(MLP_DB1, grads[:session.hidden])
+    session.bind(MLP_DB2, grads[session.hidden:])
+    return grads
 
 
 def allreduce_gradients(tensors, dist=None):
