@@ -336,6 +336,42 @@ int thb_region_plan_counts(const thb_region* region, uint64_t* fusion_groups, ui
  * counts (optional, 3 entries): fusion groups, fused groups, kernel groups. */
 enum { THB_DESCRIBE_PLAN = 0, THB_DESCRIBE_SOURCE = 1, THB_DESCRIBE_CUBIN = 2 };
 
+/* ---- `.tha` artifacts (src/artifact/v0/NativeArtifacts.cpp) -------------
+ * The reference's container ("THIRAN16" + little-endian manifest + serialized
+ * TensorRegion + payload, NativeArtifacts.cpp:547-572) is read and written
+ * byte-compatibly. Accepted: GPU artifacts with the reference's generated PTX
+ * payload (payload kind 2; the region is verified and planned onto this
+ * engine, the PTX is integrity-checked but never executed) and this engine's
+ * own artifacts (payload kind 3, target "sm_100a", runtime requirement
+ * "thiran-b200-runtime-abi=1;libcudart;sm_100a": the generated CUDA source
+ * and its sm_100a cubin, so compiling one runs no NVRTC). CPU artifacts (ELF
+ * payload) are refused with ARTIFACT-BACKEND. Failure ids follow
+ * loadArtifactBytes / validateArtifact (NativeArtifacts.cpp:574-630,
+ * 1100-1140): ARTIFACT-MAGIC, ARTIFACT-TRUNCATED, ARTIFACT-TRAILING-DATA,
+ * ARTIFACT-FORMAT-VERSION, ARTIFACT-PAYLOAD-KIND, ARTIFACT-TARGET,
+ * ARTIFACT-RUNTIME-REQUIREMENT, ARTIFACT-REGION-INTEGRITY, ARTIFACT-REGION,
+ * ARTIFACT-SIGNATURE, ARTIFACT-PAYLOAD-INTEGRITY, ARTIFACT-PLAN-INTEGRITY,
+ * ARTIFACT-PAYLOAD-MISMATCH, ... (status THB_STATUS_ABI). */
+typedef struct thb_artifact thb_artifact;
+/* loadArtifactBytes (NativeArtifacts.hpp:120): parse and validate; device-free. */
+int thb_artifact_load(const void* bytes, uint64_t size, thb_artifact** out, char* failure, uint64_t failure_cap);
+/* loadArtifact (NativeArtifacts.hpp:119). */
+int thb_artifact_load_file(const char* path, thb_artifact** out, char* failure, uint64_t failure_cap);
+void thb_artifact_release(thb_artifact* artifact);
+/* inspectArtifact (NativeArtifacts.hpp:122) as JSON: manifest, region dump
+ * and this engine's physical plan. */
+int thb_artifact_inspect(const thb_artifact* artifact, char* buffer, uint64_t capacity, uint64_t* needed);
+/* The compiled region of an artifact on `device`, used with
+ * thb_region_execute / submit / launch like any compiled region
+ * (executeArtifact / submitArtifactGpu, NativeArtifacts.hpp:125-136). */
+int thb_artifact_compile(const thb_artifact* artifact, int device, thb_region** out, char* failure,
+                         uint64_t failure_cap);
+/* buildGpuAot (NativeArtifacts.hpp:117) for this engine: writes a payload
+ * kind 3 artifact of `region` into `buffer` (device-free: NVRTC only).
+ * `needed` receives the size; a NULL buffer only reports it. */
+int thb_artifact_build(const thb_region_desc* region, thb_plan_options options, void* buffer, uint64_t capacity,
+                       uint64_t* needed, char* failure, uint64_t failure_cap);
+
 /* ---- tensor-core GEMM ----------------------------------------------------
  * Engine addition: the reference's only matmul is its Evaluator's sequential
  * f32 triple loop (src/semantic/v0/Evaluator.cpp:125-154), rejected by the

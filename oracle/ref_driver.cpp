@@ -12,12 +12,17 @@
 //       its tensor shapes from the arguments.
 //   ref_driver plan <program.th> <function> [nofusion]
 //       prints the region and buildPhysicalPlan dump (PhysicalPlan.cpp:366).
+//   ref_driver tha <program.th> <function> <out.tha> [nofusion]
+//       writes the reference's GPU artifact of the region: buildGpuAot
+//       (src/artifact/v0/NativeArtifacts.cpp:1056-1097), THIRAN16 manifest,
+//       serialized region and its generated PTX payload.
 //
 // Programs may call the extension operations `research_chain` (the
 // ((x*1.5+0.25)*x - x)*0.5 + x recipe) and `research_square_linear` (x*x + x).
 //
 // Tensor files: "THB1", u32 dtype (1 i64, 2 f32), u32 rank, u64 shape[rank],
 // little-endian elements; rank 0 is a scalar.
+#include "artifact/v0/NativeArtifacts.hpp"
 #include "autodiff/v0/Autodiff.hpp"
 #include "backend/v0/NativeCpu.hpp"
 #include "backend/v0/PhysicalPlan.hpp"
@@ -306,6 +311,18 @@ int main(int argc, char** argv) {
             auto plan = b::buildPhysicalPlan(region, b::PhysicalDevice::Gpu, options);
             if (!plan.ok()) throw std::runtime_error(plan.errors.front());
             std::cout << region.dump() << plan.plan->dump();
+            return 0;
+        }
+        if (mode == "tha") {
+            if (argc < 5) throw std::runtime_error("tha needs an output path");
+            const auto region = extract(module, function);
+            artifact::ArtifactBuildOptions options;
+            options.output = argv[4];
+            if (argc > 5 && std::string(argv[5]) == "nofusion") options.planning.enableFusion = false;
+            const auto built = artifact::buildGpuAot(region, options);
+            if (!built.success)
+                throw std::runtime_error(built.error ? built.error->code + ": " + built.error->message : "build failed");
+            std::cout << "{\"status\":\"ok\"}\n";
             return 0;
         }
         throw std::runtime_error("unknown mode " + mode);

@@ -282,6 +282,15 @@ def main():
     for name, g in zip(("dx", "dw1", "db1", "dw2", "db2", "dt"), grads):
         arrays[f"ad_linb_{name}"] = g
 
+    # The reference's own GPU artifacts (buildGpuAot, NativeArtifacts.cpp:1056-1097):
+    # THIRAN16 container, serialized region, generated PTX payload.
+    for program, stem in (("f32_chain", "ref_f32_chain"), ("i64_region", "ref_i64_region")):
+        for suffix, extra in (("", []), ("_nofusion", ["nofusion"])):
+            out = os.path.join(HERE, f"{stem}{suffix}.tha")
+            subprocess.run([DRIVER, "tha", os.path.join(ROOT, "oracle", "programs", f"{program}.th"), "f", out] + extra,
+                           check=True, capture_output=True)
+            os.chmod(out, 0o644)
+
     np.savez_compressed(os.path.join(HERE, "reference_outputs.npz"), **arrays)
     with open(os.path.join(HERE, "reference_fixtures.json"), "w") as f:
         json.dump(fixtures, f, indent=1, sort_keys=True)

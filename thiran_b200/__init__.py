@@ -154,6 +154,13 @@ SIGNATURES = {
                                          C.POINTER(C.c_uint64)]),
     "thb_region_describe": (C.c_int, [C.POINTER(RegionDesc), PlanOptions, C.c_uint32, C.c_char_p, C.c_uint64,
                                       C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.c_char_p, C.c_uint64]),
+    "thb_artifact_load": (C.c_int, [C.c_void_p, C.c_uint64, C.POINTER(C.c_void_p), C.c_char_p, C.c_uint64]),
+    "thb_artifact_load_file": (C.c_int, [C.c_char_p, C.POINTER(C.c_void_p), C.c_char_p, C.c_uint64]),
+    "thb_artifact_release": (None, [C.c_void_p]),
+    "thb_artifact_inspect": (C.c_int, [C.c_void_p, C.c_char_p, C.c_uint64, C.POINTER(C.c_uint64)]),
+    "thb_artifact_compile": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_void_p), C.c_char_p, C.c_uint64]),
+    "thb_artifact_build": (C.c_int, [C.POINTER(RegionDesc), PlanOptions, C.c_void_p, C.c_uint64,
+                                     C.POINTER(C.c_uint64), C.c_char_p, C.c_uint64]),
     "thb_gemm_bf16": (C.c_int, [C.c_int, C.POINTER(GemmDesc), C.c_void_p, C.c_char_p, C.c_uint64]),
     "thb_device_check_status": (C.c_int, [C.c_int, C.c_void_p, C.c_char_p, C.c_uint64]),
     "thb_mlp_create": (C.c_int, [C.c_int, C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64,
@@ -748,3 +755,85 @@ class CompiledRegion:
             self.release()
         except Exception:
             pass
+
+
+class _ArtifactSpec:
+    """Output dtype and shape rule of an artifact's region, from its entry
+    signature (the manifest): a scalar result, the declared extents when all
+    are known, else the first tensor parameter of the result's dtype and rank
+    (specializeEntry, src/artifact/v0/NativeArtifacts.cpp:891-922)."""
+
+    def __init__(self, manifest: dict):
+        self.result = manifest["result"]
+        self.parameters = manifest["parameters"]
+        self.output_dtype = I64 if self.result["dtype"] == "i64" else F32
+
+    def infer_output_shape(self, inputs):
+        if self.result["kind"] == "scalar":
+            return []
+        if all(e is not None for e in self.result["extents"]):
+            return list(self.result["extents"])
+        for p, v in zip(self.parameters, inputs):
+            if p["kind"] == "tensor" and p["dtype"] == self.result["dtype"] and p["rank"] == self.result["rank"]:
+                return list(np.shape(v))
+        raise GpuError(STATUS_ABI, "ARTIFACT-SIGNATURE: result extents are not known from the inputs")
+
+
+class Artifact:
+    """A loaded `.tha` artifact (thb_artifact): the reference's GPU artifacts
+    (PTX payload, planned onto this engine) or this engine's own (cubin
+    payload). `manifest` is the inspect JSON."""
+
+    def __init__(self, handle: C.c_void_p):
+        import json
+        self.handle = handle
+        needed = C.c_uint64(0)
+        lib().thb_artifact_inspect(handle, None, 0, C.byref(needed))
+        buf = C.create_string_buffer(int(needed.value))
+        lib().thb_artifact_inspect(handle, buf, len(buf), C.byref(needed))
+        self.manifest = json.loads(buf.value.decode())
+
+    @classmethod
+    def load(cls, source) -> "Artifact":
+        """From a path or from bytes."""
+        handle = C.c_void_p()
+        fail = _failure()
+        if isinstance(source, (bytes, bytearray)):
+            data = bytes(source)
+            status = lib().thb_artifact_load(data, len(data), C.byref(handle), fail, len(fail))
+        else:
+            status = lib().thb_artifact_load_file(os.fsencode(source), C.byref(handle), fail, len(fail))
+        _raise(status, fail)
+        return cls(handle)
+
+    def compile(self, device: int = 0) -> CompiledRegion:
+        handle = C.c_void_p()
+        fail = _failure()
+        _raise(lib().thb_artifact_compile(self.handle, device, C.byref(handle), fail, len(fail)), fail)
+        return CompiledRegion(_ArtifactSpec(self.manifest), handle)
+
+    def release(self):
+        if self.handle:
+            lib().thb_artifact_release(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
+
+
+def build_artifact(spec: RegionSpec, reuse=True, fusion=True) -> bytes:
+    """This engine's `.tha` artifact of `spec` (payload: generated source and
+    sm_100a cubin; device-free)."""
+    needed = C.c_uint64(0)
+    fail = _failure()
+    options = PlanOptions(int(reuse), int(fusion))
+    buf = C.create_string_buffer(1 << 20)
+    status = lib().thb_artifact_build(C.byref(spec.desc), options, buf, len(buf), C.byref(needed), fail, len(fail))
+    if status != STATUS_OK and needed.value > len(buf):
+        buf = C.create_string_buffer(int(needed.value))
+        status = lib().thb_artifact_build(C.byref(spec.desc), options, buf, len(buf), C.byref(needed), fail, len(fail))
+    _raise(status, fail)
+    return buf.raw[:needed.value]

@@ -2,9 +2,11 @@
 #include <chrono>
 #include <cmath>
 #include <cstring>
+#include <fstream>
 #include <memory>
 #include <thread>
 
+#include "artifact.hpp"
 #include "gemm.hpp"
 #include "mlp.hpp"
 #include "runtime.hpp"
@@ -321,6 +323,88 @@ int thb_region_compile(const thb_region_desc* desc, thb_plan_options options, in
 }
 
 void thb_region_release(thb_region* region) { delete region; }
+
+// ---- artifacts ------------------------------------------------------------------------
+
+struct thb_artifact {
+    thb::artifact::Artifact impl;
+};
+
+int thb_artifact_load(const void* bytes, uint64_t size, thb_artifact** out, char* failure, uint64_t cap) {
+    return guarded(failure, cap, [&] {
+        if (!out || (!bytes && size)) fail(Category::Validation, "ARTIFACT-IO", "null artifact bytes or result");
+        *out = nullptr;
+        auto a = std::make_unique<thb_artifact>();
+        a->impl = thb::artifact::load(std::string(static_cast<const char*>(bytes), static_cast<std::size_t>(size)));
+        *out = a.release();
+        return THB_STATUS_OK;
+    });
+}
+
+int thb_artifact_load_file(const char* path, thb_artifact** out, char* failure, uint64_t cap) {
+    return guarded(failure, cap, [&] {
+        if (!path || !out) fail(Category::Validation, "ARTIFACT-IO", "null path or result");
+        *out = nullptr;
+        std::ifstream in(path, std::ios::binary | std::ios::ate);
+        if (!in) fail(Category::Validation, "ARTIFACT-IO", std::string("cannot open ") + path);
+        const auto end = in.tellg();
+        // The reference's file limit: payload + region + 4 MiB of manifest.
+        if (end < 0 || static_cast<std::uint64_t>(end) > (512ull << 20) + (64ull << 20) + (4ull << 20))
+            fail(Category::Validation, "ARTIFACT-IO", "file size exceeds V0 limit");
+        std::string bytes(static_cast<std::size_t>(end), '\0');
+        in.seekg(0);
+        if (!bytes.empty() && !in.read(bytes.data(), end)) fail(Category::Validation, "ARTIFACT-IO", "short file read");
+        auto a = std::make_unique<thb_artifact>();
+        a->impl = thb::artifact::load(bytes);
+        *out = a.release();
+        return THB_STATUS_OK;
+    });
+}
+
+void thb_artifact_release(thb_artifact* artifact) { delete artifact; }
+
+int thb_artifact_inspect(const thb_artifact* artifact, char* buffer, uint64_t capacity, uint64_t* needed) {
+    if (!artifact) return THB_STATUS_ABI;
+    try {
+        const std::string text = thb::artifact::inspect(artifact->impl);
+        if (needed) *needed = text.size() + 1;
+        writeText(buffer, capacity, text);
+        return (capacity >= text.size() + 1 || !buffer) ? THB_STATUS_OK : THB_STATUS_ABI;
+    } catch (...) {
+        return THB_STATUS_UNKNOWN;
+    }
+}
+
+int thb_artifact_compile(const thb_artifact* artifact, int device, thb_region** out, char* failure, uint64_t cap) {
+    return guarded(failure, cap, [&] {
+        if (!artifact || !out) fail(Category::Validation, "ARTIFACT-IO", "null artifact or result");
+        *out = nullptr;
+        const auto& a = artifact->impl;
+        PlanOptions opts;
+        opts.enableReuse = a.manifest.enableReuse;
+        opts.enableFusion = a.manifest.enableFusion;
+        const std::string* cubin = a.engineCubin.empty() ? nullptr : &a.engineCubin;
+        auto impl = std::make_shared<CompiledRegion>(a.region, opts, device, cubin);
+        *out = new thb_region{std::move(impl)};
+        return THB_STATUS_OK;
+    });
+}
+
+int thb_artifact_build(const thb_region_desc* desc, thb_plan_options options, void* buffer, uint64_t capacity,
+                       uint64_t* needed, char* failure, uint64_t cap) {
+    return guarded(failure, cap, [&] {
+        if (!desc || !needed) fail(Category::Validation, "ARTIFACT-INVALID-REGION", "null region or size result");
+        PlanOptions opts;
+        opts.enableReuse = options.enable_reuse != 0;
+        opts.enableFusion = options.enable_fusion != 0;
+        const std::string bytes = thb::artifact::build(importRegion(*desc), opts);
+        *needed = bytes.size();
+        if (!buffer) return THB_STATUS_OK;
+        if (capacity < bytes.size()) fail(Category::Validation, "ARTIFACT-IO", "artifact buffer too small");
+        std::memcpy(buffer, bytes.data(), bytes.size());
+        return THB_STATUS_OK;
+    });
+}
 
 int thb_region_execute(thb_region* region, const thb_abi_arg* args, uint64_t argc, void* output, uint64_t outputCount,
                        thb_evidence* evidence, char* failure, uint64_t cap) {

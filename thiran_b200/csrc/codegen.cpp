@@ -345,12 +345,23 @@ std::string generateSource(const Region& region, const Plan& plan, std::vector<G
 }
 
 std::shared_ptr<Module> compileAndLoad(const std::string& source, int device, std::vector<GroupKernel>& kernels,
-                                       bool& jitted, bool& loaded) {
+                                       bool& jitted, bool& loaded, const std::string* prebuiltCubin) {
     jitted = false;
     loaded = false;
     const std::uint64_t digest = fnv1a(source);
     std::lock_guard<std::mutex> lock(cacheMutex);
     std::shared_ptr<Module> module = liveModules[{digest, device}].lock();
+    if (!module && prebuiltCubin) {
+        // An artifact's cubin of exactly this source: no NVRTC, no disk cache.
+        module = std::make_shared<Module>();
+        module->device = device;
+        const cudaError_t e =
+            cudaLibraryLoadData(&module->library, prebuiltCubin->data(), nullptr, nullptr, 0, nullptr, nullptr, 0);
+        if (e != cudaSuccess)
+            fail(Category::Runtime, "GPU-MODULE-LOAD", std::string("artifact cubin: ") + cudaGetErrorString(e));
+        loaded = true;
+        liveModules[{digest, device}] = module;
+    }
     if (!module) {
         std::ostringstream name;
         name << std::hex << std::setw(16) << std::setfill('0') << digest;

@@ -39,10 +39,12 @@ struct Module;  // compiled NVRTC library (opaque)
 std::string generateSource(const Region&, const Plan&, std::vector<GroupKernel>& kernels);
 
 // Compiles `source` for sm_100a with NVRTC (or takes it from the in-process /
-// on-disk cache) and loads it on the current device. Fills the kernel
-// handles. `jitted` reports whether NVRTC ran (a cache miss).
+// on-disk cache, or from `prebuiltCubin`, an artifact's cubin of this exact
+// source) and loads it on the current device. Fills the kernel handles.
+// `jitted` reports whether NVRTC ran (a cache miss).
 std::shared_ptr<Module> compileAndLoad(const std::string& source, int device,
-                                       std::vector<GroupKernel>& kernels, bool& jitted, bool& loaded);
+                                       std::vector<GroupKernel>& kernels, bool& jitted, bool& loaded,
+                                       const std::string* prebuiltCubin = nullptr);
 
 std::uint64_t fnv1a(const std::string&);
 

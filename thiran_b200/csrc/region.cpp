@@ -3,6 +3,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <iomanip>
 #include <sstream>
 
 namespace thb {
@@ -152,6 +153,27 @@ std::string validateOperation(const Operation& op) {
     return {};
 }
 
+std::string canonicalIdentity(const Operation& op) {
+    return op.extensionId + "::" + op.name + "@" + op.semanticVersion + "/abi" + std::to_string(op.abiVersion);
+}
+
+std::string descriptorDigest(const Operation& op) {
+    Fnv h;
+    h.text(op.extensionId); h.text(op.extensionVersion); h.text(op.name); h.text(op.semanticVersion);
+    h.value(op.abiVersion); h.value(op.arity); h.value(op.minimumRank); h.value(op.maximumRank);
+    h.value(op.resultLikeInput); h.byte(op.sameShape); h.byte(op.effect); h.value(op.backends); h.byte(op.fusible);
+    h.recipe(op.forward);
+    h.byte(op.derivative.has_value());
+    if (op.derivative) {
+        h.value(op.derivative->differentiableInputs); h.value(op.derivative->savedInputs);
+        h.byte(op.derivative->savesOutput); h.value<std::uint64_t>(op.derivative->gradients.size());
+        for (const auto& g : op.derivative->gradients) h.recipe(g);
+    }
+    std::ostringstream out;
+    out << "fnv1a64:" << std::hex << std::setw(16) << std::setfill('0') << h.h;
+    return out.str();
+}
+
 Operation importOperation(const thb_operation& raw) {
     Operation op;
     op.name = raw.name ? raw.name : "";
@@ -175,14 +197,18 @@ Operation importOperation(const thb_operation& raw) {
                 d.gradients.push_back(importRecipe(raw.derivative->gradients[i]));
         op.derivative = std::move(d);
     }
+    op.digest = engineDigest(op);
+    return op;
+}
+
+std::string engineDigest(const Operation& op) {
     Fnv h;
     h.text(op.name); h.text(op.semanticVersion); h.value(op.arity); h.value(op.minimumRank);
     h.value(op.maximumRank); h.value(op.resultLikeInput); h.byte(op.sameShape); h.byte(op.effect);
     h.value(op.backends); h.byte(op.fusible); h.recipe(op.forward);
     std::ostringstream out;
     out << "fnv1a64:" << std::hex << h.h;
-    op.digest = out.str();
-    return op;
+    return out.str();
 }
 
 // ---- region IR ------------------------------------------------------------------

@@ -77,13 +77,26 @@ struct Operation {
     Recipe forward;
     std::optional<Derivative> derivative;
     std::string digest;  // FNV-1a over the descriptor fields
+    // Registry identity (include/extension/v0/Extension.hpp:81-93): carried
+    // by artifacts. Descriptors passed in directly get extensionId "inline".
+    std::string extensionId = "inline", extensionVersion = "1.0.0";
+    std::uint32_t abiVersion = 1;
 };
+
+// "<extension>::<name>@<version>/abi<N>" (src/extension/v0/Extension.cpp:203).
+std::string canonicalIdentity(const Operation&);
+// FNV-1a 64 over the identity and descriptor fields in the reference's order
+// (operationDigest, src/extension/v0/Extension.cpp:135-149), "fnv1a64:%016x".
+std::string descriptorDigest(const Operation&);
 
 // Validation of a descriptor; the rules of validateRecipe / validateOperation
 // (src/extension/v0/Extension.cpp:51-133). Returns an empty string when valid.
 std::string validateRecipe(const Recipe&, std::uint32_t inputs, bool allowDivide);
 std::string validateOperation(const Operation&);
 Operation importOperation(const thb_operation&);
+// The engine's short descriptor digest (`Operation::digest`: name, version,
+// contract and forward recipe), shown in region dumps.
+std::string engineDigest(const Operation&);
 
 struct Node {
     std::uint32_t id = 0;

@@ -137,12 +137,16 @@ Pending::~Pending() {
 // ---- compiled region --------------------------------------------------------
 
 CompiledRegion::CompiledRegion(const thb_region_desc& desc, PlanOptions options, int device)
-    : region_(importRegion(desc)), plan_(buildPlan(region_, options)), device_(device) {
+    : CompiledRegion(importRegion(desc), options, device, nullptr) {}
+
+CompiledRegion::CompiledRegion(Region region, PlanOptions options, int device, const std::string* prebuiltCubin)
+    : region_(std::move(region)), plan_(buildPlan(region_, options)), device_(device) {
     // Planning and code generation need no device: a malformed region fails
     // before any driver call (NativeGpuTests.cpp:175-198 contract).
     source_ = generateSource(region_, plan_, kernels_);
     info_ = &useDevice(device);
-    if (!kernels_.empty()) module_ = compileAndLoad(source_, device, kernels_, moduleJitted_, moduleLoaded_);
+    if (!kernels_.empty())
+        module_ = compileAndLoad(source_, device, kernels_, moduleJitted_, moduleLoaded_, prebuiltCubin);
     check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreateWithFlags");
     errors_.reserve(std::max<std::size_t>(1, plan_.groups.size()) * sizeof(std::uint32_t) + 64, device_);
     check(cudaMemsetAsync(errors_.ptr, 0, errors_.bytes, stream_), "cudaMemsetAsync");

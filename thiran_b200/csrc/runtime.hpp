@@ -81,6 +81,9 @@ struct Value {
 class CompiledRegion {
 public:
     CompiledRegion(const thb_region_desc&, PlanOptions, int device);
+    // From an imported region (an artifact's); `prebuiltCubin`, when given,
+    // is the cubin of exactly the source this region generates.
+    CompiledRegion(Region region, PlanOptions, int device, const std::string* prebuiltCubin);
     ~CompiledRegion();
 
     const Region& region() const { return region_; }
