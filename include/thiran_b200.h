@@ -366,6 +366,40 @@ int thb_artifact_inspect(const thb_artifact* artifact, char* buffer, uint64_t ca
  * (executeArtifact / submitArtifactGpu, NativeArtifacts.hpp:125-136). */
 int thb_artifact_compile(const thb_artifact* artifact, int device, thb_region** out, char* failure,
                          uint64_t failure_cap);
+/* ---- `.thm` model bundles (src/model/v0/ModelBundle.cpp) ---------------
+ * The reference's container ("THIRANMB", versions, FNV-1a 64 payload digest,
+ * identity, entry, frozen parameters, public ABI, bindings, embedded
+ * artifacts) is read byte-compatibly and validated with validateModelBundle's
+ * MODEL-* ids (ModelBundle.cpp:242-326, 362-430). A compiled model uploads
+ * its frozen parameters to HBM once and keeps them there; each
+ * thb_model_execute uploads only the public inputs. (The reference's
+ * submitModelGpu, ModelBundle.cpp:461-474, binds every parameter as a host
+ * value and uploads it on every call.) Without an embedded GPU artifact
+ * compilation fails with MODEL-BACKEND-UNAVAILABLE; there is no CPU
+ * fallback. */
+typedef struct thb_model thb_model;
+typedef struct thb_model_session thb_model_session;
+/* loadModelBundle(path, expectedModelIdentity) (ModelBundle.hpp:98-99);
+ * `identity` may be NULL. */
+int thb_model_load(const void* bytes, uint64_t size, const char* identity, thb_model** out, char* failure,
+                   uint64_t failure_cap);
+int thb_model_load_file(const char* path, const char* identity, thb_model** out, char* failure,
+                        uint64_t failure_cap);
+void thb_model_release(thb_model* model);
+/* inspectModelBundle (ModelBundle.hpp:100) as JSON. */
+int thb_model_inspect(const thb_model* model, char* buffer, uint64_t capacity, uint64_t* needed);
+/* Compiles the embedded GPU artifact on `device` and uploads the frozen
+ * parameters (evidence counts that upload). */
+int thb_model_compile(const thb_model* model, int device, thb_model_session** out, thb_evidence* evidence,
+                      char* failure, uint64_t failure_cap);
+void thb_model_session_release(thb_model_session* session);
+/* executeModel(bundle, Gpu, publicInputs) (ModelBundle.hpp:101-103): host
+ * public inputs in bundle order (checked like validateRuntimeValue:
+ * MODEL-PUBLIC-INPUT-COUNT / MODEL-PUBLIC-INPUT-ABI), host output; the
+ * frozen parameters come from HBM. */
+int thb_model_execute(thb_model_session* session, const thb_abi_arg* public_args, uint64_t argc, void* output,
+                      uint64_t output_count, thb_evidence* evidence, char* failure, uint64_t failure_cap);
+
 /* buildGpuAot (NativeArtifacts.hpp:117) for this engine: writes a payload
  * kind 3 artifact of `region` into `buffer` (device-free: NVRTC only).
  * `needed` receives the size; a NULL buffer only reports it. */

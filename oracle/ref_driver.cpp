@@ -16,6 +16,12 @@
 //       writes the reference's GPU artifact of the region: buildGpuAot
 //       (src/artifact/v0/NativeArtifacts.cpp:1056-1097), THIRAN16 manifest,
 //       serialized region and its generated PTX payload.
+//   ref_driver thm <program.th> <function> <out.thm> <public-count> <in.bin ...>
+//       writes the reference's model bundle (createModelBundle /
+//       writeModelBundle, src/model/v0/ModelBundle.cpp:328-360): the first
+//       <public-count> inputs are public, the rest frozen parameters (ids 1..,
+//       names p1..) with the given values; one GPU artifact specialised to
+//       these shapes (specializeEntry, NativeArtifacts.cpp:891-922).
 //
 // Programs may call the extension operations `research_chain` (the
 // ((x*1.5+0.25)*x - x)*0.5 + x recipe) and `research_square_linear` (x*x + x).
@@ -24,6 +30,7 @@
 // little-endian elements; rank 0 is a scalar.
 #include "artifact/v0/NativeArtifacts.hpp"
 #include "autodiff/v0/Autodiff.hpp"
+#include "model/v0/ModelBundle.hpp"
 #include "backend/v0/NativeCpu.hpp"
 #include "backend/v0/PhysicalPlan.hpp"
 #include "extension/v0/Extension.hpp"
@@ -322,6 +329,67 @@ int main(int argc, char** argv) {
             const auto built = artifact::buildGpuAot(region, options);
             if (!built.success)
                 throw std::runtime_error(built.error ? built.error->code + ": " + built.error->message : "build failed");
+            std::cout << "{\"status\":\"ok\"}\n";
+            return 0;
+        }
+        if (mode == "thm") {
+            if (argc < 6) throw std::runtime_error("thm needs an output path and a public-input count");
+            const auto region = extract(module, function);
+            const std::size_t publicCount = std::stoul(argv[5]);
+            std::vector<artifact::ArtifactValue> values;
+            std::vector<persistence::StoredParameter> parameters;
+            for (int k = 6; k < argc; ++k) {
+                const auto value = readValue(argv[k]);
+                const auto* tensor = std::get_if<s::RuntimeTensor>(&value.data);
+                if (!tensor) throw std::runtime_error("thm inputs must be tensors");
+                std::vector<std::uint64_t> shape(tensor->shape.begin(), tensor->shape.end());
+                persistence::StoredValue stored;
+                stored.kind = persistence::StoredValueKind::Tensor;
+                stored.shape = shape;
+                if (tensor->dtype == s::TypeKind::I64) {
+                    values.emplace_back(storage::Tensor::materializeI64(shape, tensor->values));
+                    stored.dtype = storage::DType::I64;
+                    const auto* p = reinterpret_cast<const std::byte*>(tensor->values.data());
+                    stored.bytes.assign(p, p + tensor->values.size() * 8);
+                } else {
+                    values.emplace_back(storage::Tensor::materializeF32(shape, tensor->f32Values));
+                    stored.dtype = storage::DType::F32;
+                    const auto* p = reinterpret_cast<const std::byte*>(tensor->f32Values.data());
+                    stored.bytes.assign(p, p + tensor->f32Values.size() * 4);
+                }
+                const std::size_t index = static_cast<std::size_t>(k - 6);
+                if (index >= publicCount)
+                    parameters.push_back({index - publicCount + 1, "p" + std::to_string(index - publicCount + 1), stored});
+            }
+            const std::string temporary = std::string(argv[4]) + ".artifact.tmp";
+            artifact::ArtifactBuildOptions options;
+            options.output = temporary;
+            options.specializedEntry = artifact::specializeEntry(region, values);
+            const auto built = artifact::buildGpuAot(region, options);
+            if (!built.success)
+                throw std::runtime_error(built.error ? built.error->code + ": " + built.error->message : "build failed");
+            auto loaded = artifact::loadArtifact(temporary);
+            std::remove(temporary.c_str());
+            if (!loaded.ok()) throw std::runtime_error("artifact reload: " + loaded.error->code);
+            model::DeploymentSnapshot snapshot;
+            snapshot.modelIdentity = "research-model@1";
+            snapshot.inferenceEntry = loaded.artifact->manifest.entry.name;
+            snapshot.parameters = parameters;
+            const auto& entry = loaded.artifact->manifest.entry;
+            for (std::size_t i = 0; i < entry.parameters.size(); ++i) {
+                if (i < publicCount) {
+                    snapshot.publicInputs.push_back(entry.parameters[i]);
+                    snapshot.publicBindings.push_back({static_cast<std::uint32_t>(i), static_cast<std::uint32_t>(i)});
+                } else {
+                    snapshot.parameterBindings.push_back({i - publicCount + 1, static_cast<std::uint32_t>(i)});
+                }
+            }
+            snapshot.result = entry.result;
+            snapshot.parameterDigest = persistence::parameterDigest(parameters);
+            auto bundle = model::createModelBundle(snapshot, {{snapshot.modelIdentity, *loaded.artifact}});
+            if (!bundle.ok()) throw std::runtime_error("bundle: " + bundle.error->code + " " + bundle.error->message);
+            const auto written = model::writeModelBundle(*bundle.bundle, argv[4]);
+            if (!written.ok()) throw std::runtime_error("bundle write: " + written.error->code);
             std::cout << "{\"status\":\"ok\"}\n";
             return 0;
         }

@@ -291,6 +291,31 @@ def main():
                            check=True, capture_output=True)
             os.chmod(out, 0o644)
 
+    # The reference's model bundle (createModelBundle + writeModelBundle,
+    # src/model/v0/ModelBundle.cpp:328-360): public x, frozen parameters w, b
+    # of fn f(x, w, b) = research_chain(x) .* w + b, one GPU artifact; and the
+    # reference Evaluator's result on a second public input.
+    rng = np.random.default_rng(13)
+    mx = rng.uniform(-1, 1, (96, 200)).astype(np.float32)
+    mw = rng.standard_normal((96, 200)).astype(np.float32)
+    mb = rng.standard_normal((96, 200)).astype(np.float32)
+    mx2 = rng.uniform(-1, 1, (96, 200)).astype(np.float32)
+    model_program = os.path.join(ROOT, "oracle", "programs", "research_model.th")
+    with tempfile.TemporaryDirectory() as tmp:
+        paths = []
+        for k, v in enumerate([mx, mw, mb]):
+            p = os.path.join(tmp, f"m{k}.bin")
+            write_thb(p, v)
+            paths.append(p)
+        out = os.path.join(HERE, "ref_research_model.thm")
+        subprocess.run([DRIVER, "thm", model_program, "f", out, "1"] + paths, check=True, capture_output=True)
+        os.chmod(out, 0o644)
+    program = open(model_program).read()
+    for name, x in (("model_x", mx), ("model_x2", mx2)):
+        status, value = evaluate(program, "f", [x, mw, mb])
+        assert status == "ok"
+        arrays[name], arrays[name + "_eval"] = x, value
+
     np.savez_compressed(os.path.join(HERE, "reference_outputs.npz"), **arrays)
     with open(os.path.join(HERE, "reference_fixtures.json"), "w") as f:
         json.dump(fixtures, f, indent=1, sort_keys=True)

@@ -161,6 +161,16 @@ SIGNATURES = {
     "thb_artifact_compile": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_void_p), C.c_char_p, C.c_uint64]),
     "thb_artifact_build": (C.c_int, [C.POINTER(RegionDesc), PlanOptions, C.c_void_p, C.c_uint64,
                                      C.POINTER(C.c_uint64), C.c_char_p, C.c_uint64]),
+    "thb_model_load": (C.c_int, [C.c_void_p, C.c_uint64, C.c_char_p, C.POINTER(C.c_void_p), C.c_char_p,
+                                 C.c_uint64]),
+    "thb_model_load_file": (C.c_int, [C.c_char_p, C.c_char_p, C.POINTER(C.c_void_p), C.c_char_p, C.c_uint64]),
+    "thb_model_release": (None, [C.c_void_p]),
+    "thb_model_inspect": (C.c_int, [C.c_void_p, C.c_char_p, C.c_uint64, C.POINTER(C.c_uint64)]),
+    "thb_model_compile": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_void_p), C.POINTER(Evidence), C.c_char_p,
+                                    C.c_uint64]),
+    "thb_model_session_release": (None, [C.c_void_p]),
+    "thb_model_execute": (C.c_int, [C.c_void_p, C.POINTER(AbiArg), C.c_uint64, C.c_void_p, C.c_uint64,
+                                    C.POINTER(Evidence), C.c_char_p, C.c_uint64]),
     "thb_gemm_bf16": (C.c_int, [C.c_int, C.POINTER(GemmDesc), C.c_void_p, C.c_char_p, C.c_uint64]),
     "thb_device_check_status": (C.c_int, [C.c_int, C.c_void_p, C.c_char_p, C.c_uint64]),
     "thb_mlp_create": (C.c_int, [C.c_int, C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64,
@@ -815,6 +825,85 @@ class Artifact:
     def release(self):
         if self.handle:
             lib().thb_artifact_release(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
+
+
+class ModelSession:
+    """A compiled model (thb_model_session): frozen parameters resident in
+    HBM, public inputs uploaded per call."""
+
+    def __init__(self, model: "Model", handle: C.c_void_p, evidence: dict):
+        self.model, self.handle, self.compile_evidence = model, handle, evidence
+        self._spec = _ArtifactSpec({"result": model.result, "parameters": model.public_inputs})
+
+    def execute(self, inputs, output_shape=None):
+        args, keep = _host_args(inputs)
+        shape = self._spec.infer_output_shape(inputs) if output_shape is None else list(output_shape)
+        out = np.empty([int(e) for e in shape], dtype=_NP[self._spec.output_dtype])
+        ev = Evidence()
+        fail = _failure()
+        status = lib().thb_model_execute(self.handle, args, len(inputs), out.ctypes.data if out.size else None,
+                                         out.size, C.byref(ev), fail, len(fail))
+        self.evidence = ev.as_dict()
+        _raise(status, fail)
+        return out if len(shape) else out.reshape(()).item()
+
+    def release(self):
+        if self.handle:
+            lib().thb_model_session_release(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
+
+
+class Model:
+    """A loaded `.thm` model bundle (thb_model). `manifest` is the inspect
+    JSON; `public_inputs` / `result` the public ABI of its GPU artifact."""
+
+    def __init__(self, handle: C.c_void_p):
+        import json
+        self.handle = handle
+        needed = C.c_uint64(0)
+        lib().thb_model_inspect(handle, None, 0, C.byref(needed))
+        buf = C.create_string_buffer(int(needed.value))
+        lib().thb_model_inspect(handle, buf, len(buf), C.byref(needed))
+        self.manifest = json.loads(buf.value.decode())
+        self.public_inputs = self.manifest["public_abi"]
+        self.result = self.manifest["result"]
+
+    @classmethod
+    def load(cls, source, identity=None) -> "Model":
+        handle = C.c_void_p()
+        fail = _failure()
+        ident = identity.encode() if identity is not None else None
+        if isinstance(source, (bytes, bytearray)):
+            data = bytes(source)
+            status = lib().thb_model_load(data, len(data), ident, C.byref(handle), fail, len(fail))
+        else:
+            status = lib().thb_model_load_file(os.fsencode(source), ident, C.byref(handle), fail, len(fail))
+        _raise(status, fail)
+        return cls(handle)
+
+    def compile(self, device: int = 0) -> ModelSession:
+        handle = C.c_void_p()
+        ev = Evidence()
+        fail = _failure()
+        _raise(lib().thb_model_compile(self.handle, device, C.byref(handle), C.byref(ev), fail, len(fail)), fail)
+        return ModelSession(self, handle, ev.as_dict())
+
+    def release(self):
+        if self.handle:
+            lib().thb_model_release(self.handle)
             self.handle = None
 
     def __del__(self):

@@ -458,7 +458,7 @@ std::string digest(const std::string& bytes) {
     return out.str();
 }
 
-Artifact load(const std::string& bytes) {
+Artifact load(const std::string& bytes, bool acceptCpu) {
     Reader r(bytes);
     for (char expected : kMagic)
         if (r.u8() != static_cast<std::uint8_t>(expected)) bad("ARTIFACT-MAGIC", "missing THIRAN16 header");
@@ -492,13 +492,16 @@ Artifact load(const std::string& bytes) {
     if (m.formatVersion != 0) bad("ARTIFACT-FORMAT-VERSION", "unsupported artifact format version");
     if (m.compilerAbiVersion != 1) bad("ARTIFACT-COMPILER-ABI", "unsupported compiler/artifact ABI");
     if (m.runtimeAbiVersion != 1) bad("ARTIFACT-RUNTIME-ABI", "unsupported native runtime ABI");
-    if (m.backend == kBackendCpu) bad("ARTIFACT-BACKEND", "CPU artifacts run on the reference's CPU runtime, not on this GPU engine");
-    if (m.backend != kBackendGpu) bad("ARTIFACT-BACKEND", "unsupported artifact backend");
-    const bool engine = m.payloadKind == kPayloadB200;
-    if (m.payloadKind != kPayloadPtx && !engine) bad("ARTIFACT-PAYLOAD-KIND", "payload kind/backend mismatch");
-    if (m.target != (engine ? kEngineTarget : kReferenceGpuTarget))
+    const bool cpu = m.backend == kBackendCpu;
+    if (cpu && !acceptCpu)
+        bad("ARTIFACT-BACKEND", "CPU artifacts run on the reference's CPU runtime, not on this GPU engine");
+    if (m.backend != kBackendGpu && !cpu) bad("ARTIFACT-BACKEND", "unsupported artifact backend");
+    const bool engine = m.payloadKind == kPayloadB200 && !cpu;
+    if (cpu ? m.payloadKind != kPayloadElf : (m.payloadKind != kPayloadPtx && !engine))
+        bad("ARTIFACT-PAYLOAD-KIND", "payload kind/backend mismatch");
+    if (!cpu && m.target != (engine ? kEngineTarget : kReferenceGpuTarget))
         bad("ARTIFACT-TARGET", "artifact target is incompatible with this runtime");
-    if (m.runtimeRequirement != (engine ? kEngineRuntime : kReferenceGpuRuntime))
+    if (m.runtimeRequirement != (cpu ? kReferenceCpuRuntime : engine ? kEngineRuntime : kReferenceGpuRuntime))
         bad("ARTIFACT-RUNTIME-REQUIREMENT", "artifact runtime requirement is unsupported");
     if (m.regionDigest != digest(regionBytes)) bad("ARTIFACT-REGION-INTEGRITY", "lowered-region size/digest mismatch");
     a.region = readRegion(regionBytes, engine);

@@ -27,6 +27,7 @@ constexpr std::uint8_t kPayloadElf = 1, kPayloadPtx = 2;          // PayloadKind
 constexpr std::uint8_t kPayloadB200 = 3;                          // engine addition
 constexpr const char* kReferenceGpuTarget = "ptx60-sm50-min-cc50";
 constexpr const char* kReferenceGpuRuntime = "native-runtime-abi=1;libcuda.so.1;driver-ptx-jit;min-cc=5.0";
+constexpr const char* kReferenceCpuRuntime = "native-runtime-abi=1;system-cxx-runtime";
 constexpr const char* kEngineTarget = "sm_100a";
 constexpr const char* kEngineRuntime = "thiran-b200-runtime-abi=1;libcudart;sm_100a";
 
@@ -64,8 +65,10 @@ struct Artifact {
 std::string digest(const std::string& bytes);
 
 // Parses and validates an artifact; throws Failure(Validation, "ARTIFACT-...")
-// with the reference's error ids.
-Artifact load(const std::string& bytes);
+// with the reference's error ids. CPU artifacts (ELF payload) are accepted
+// only with `acceptCpu` (a model bundle checks their signature; they never
+// execute here).
+Artifact load(const std::string& bytes, bool acceptCpu = false);
 
 // Builds a kind-3 artifact of `region` (device-free: NVRTC only).
 std::string build(const Region& region, PlanOptions options);

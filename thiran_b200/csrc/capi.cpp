@@ -6,8 +6,11 @@
 #include <memory>
 #include <thread>
 
+#include <array>
+
 #include "artifact.hpp"
 #include "gemm.hpp"
+#include "model.hpp"
 #include "mlp.hpp"
 #include "runtime.hpp"
 
@@ -388,6 +391,200 @@ int thb_artifact_compile(const thb_artifact* artifact, int device, thb_region** 
         *out = new thb_region{std::move(impl)};
         return THB_STATUS_OK;
     });
+}
+
+// ---- model bundles ----------------------------------------------------------------------
+
+struct thb_model {
+    thb::model::Bundle impl;
+};
+
+struct thb_model_session {
+    std::shared_ptr<CompiledRegion> region;
+    std::vector<std::int64_t> sources;                      // per artifact slot (model::slotSources)
+    std::vector<thb::model::StoredValue> parameters;        // host copies (scalars are passed by value)
+    std::vector<std::unique_ptr<DeviceBuffer>> resident;    // per parameter: its tensor in HBM
+    std::vector<std::unique_ptr<DeviceBuffer>> publicSlots; // per artifact slot: public upload buffer
+    std::vector<thb::artifact::Type> publicTypes;
+    std::uint64_t residentBytes = 0;
+};
+
+static int loadModel(const std::string& bytes, const char* identity, thb_model** out) {
+    const std::string expected = identity ? identity : "";
+    auto m = std::make_unique<thb_model>();
+    m->impl = thb::model::load(bytes, identity ? &expected : nullptr);
+    *out = m.release();
+    return THB_STATUS_OK;
+}
+
+int thb_model_load(const void* bytes, uint64_t size, const char* identity, thb_model** out, char* failure,
+                   uint64_t cap) {
+    return guarded(failure, cap, [&] {
+        if (!out || (!bytes && size)) fail(Category::Validation, "MODEL-IO", "null bundle bytes or result");
+        *out = nullptr;
+        return loadModel(std::string(static_cast<const char*>(bytes), static_cast<std::size_t>(size)), identity, out);
+    });
+}
+
+int thb_model_load_file(const char* path, const char* identity, thb_model** out, char* failure, uint64_t cap) {
+    return guarded(failure, cap, [&] {
+        if (!path || !out) fail(Category::Validation, "MODEL-IO", "null path or result");
+        *out = nullptr;
+        std::ifstream in(path, std::ios::binary | std::ios::ate);
+        if (!in) fail(Category::Validation, "MODEL-IO", std::string("cannot open ") + path);
+        const auto end = in.tellg();
+        if (end < 0 || static_cast<std::uint64_t>(end) > (2ull << 30))
+            fail(Category::Validation, "MODEL-IO", "file size exceeds V0 limit");
+        std::string bytes(static_cast<std::size_t>(end), '\0');
+        in.seekg(0);
+        if (!bytes.empty() && !in.read(bytes.data(), end)) fail(Category::Validation, "MODEL-IO", "short file read");
+        return loadModel(bytes, identity, out);
+    });
+}
+
+void thb_model_release(thb_model* model) { delete model; }
+
+int thb_model_inspect(const thb_model* model, char* buffer, uint64_t capacity, uint64_t* needed) {
+    if (!model) return THB_STATUS_ABI;
+    try {
+        const std::string text = thb::model::inspect(model->impl);
+        if (needed) *needed = text.size() + 1;
+        writeText(buffer, capacity, text);
+        return (capacity >= text.size() + 1 || !buffer) ? THB_STATUS_OK : THB_STATUS_ABI;
+    } catch (...) {
+        return THB_STATUS_UNKNOWN;
+    }
+}
+
+int thb_model_compile(const thb_model* model, int device, thb_model_session** out, thb_evidence* evidence,
+                      char* failure, uint64_t cap) {
+    thb_evidence ev{};
+    const int status = guarded(failure, cap, [&] {
+        if (!model || !out) fail(Category::Validation, "MODEL-IO", "null model or result");
+        *out = nullptr;
+        const auto& b = model->impl;
+        auto s = std::make_unique<thb_model_session>();
+        s->sources = thb::model::slotSources(b);  // MODEL-BACKEND-UNAVAILABLE without a GPU artifact
+        const auto& a = *b.gpu;
+        PlanOptions opts;
+        opts.enableReuse = a.manifest.enableReuse;
+        opts.enableFusion = a.manifest.enableFusion;
+        const std::string* cubin = a.engineCubin.empty() ? nullptr : &a.engineCubin;
+        s->region = std::make_shared<CompiledRegion>(a.region, opts, device, cubin);
+        s->publicTypes = b.publicInputs;
+        s->publicSlots.resize(s->sources.size());
+        // Frozen parameters go to HBM once; every later call reuses them.
+        for (const auto& p : b.parameters) {
+            s->parameters.push_back(p.value);
+            s->resident.push_back(std::make_unique<DeviceBuffer>());
+            if (p.value.kind != 2 || p.value.bytes.empty()) continue;
+            s->resident.back()->reserve(p.value.bytes.size(), device);
+            ++ev.allocation_count;
+            ev.allocation_bytes_requested += p.value.bytes.size();
+            cudaCheck(cudaMemcpy(s->resident.back()->ptr, p.value.bytes.data(), p.value.bytes.size(),
+                                 cudaMemcpyHostToDevice),
+                      "cudaMemcpy(parameter)");
+            ++ev.host_to_device_copies;
+            ev.host_to_device_bytes += p.value.bytes.size();
+            s->residentBytes += p.value.bytes.size();
+        }
+        *out = s.release();
+        return THB_STATUS_OK;
+    });
+    if (evidence) *evidence = ev;
+    return status;
+}
+
+void thb_model_session_release(thb_model_session* session) { delete session; }
+
+int thb_model_execute(thb_model_session* s, const thb_abi_arg* args, uint64_t argc, void* output,
+                      uint64_t outputCount, thb_evidence* evidence, char* failure, uint64_t cap) {
+    thb_evidence ev{};
+    const int status = guarded(failure, cap, [&] {
+        if (!s) fail(Category::Validation, "MODEL-IO", "null model session");
+        if (argc != s->publicTypes.size())
+            fail(Category::Validation, "MODEL-PUBLIC-INPUT-COUNT", "public inference input count mismatch");
+        if (argc && !args) fail(Category::Validation, "MODEL-PUBLIC-INPUT-COUNT", "argument array is null");
+        // validateRuntimeValue (src/model/v0/ModelBundle.cpp:86-110).
+        for (uint64_t i = 0; i < argc; ++i) {
+            const auto& t = s->publicTypes[i];
+            const thb_abi_arg& a = args[i];
+            const std::string where = "public input " + std::to_string(i) + ": ";
+            if (a.kind != t.kind) fail(Category::Validation, "MODEL-PUBLIC-INPUT-ABI", where + "kind mismatch");
+            if (a.dtype != t.dtype || a.rank != t.rank)
+                fail(Category::Validation, "MODEL-PUBLIC-INPUT-ABI", where + "dtype/rank mismatch");
+            for (std::size_t d = 0; d < t.extents.size(); ++d)
+                if (t.extents[d] && (!a.shape || a.shape[d] != *t.extents[d]))
+                    fail(Category::Validation, "MODEL-PUBLIC-INPUT-ABI", where + "shape mismatch");
+            if (a.reserved & 1u) fail(Category::Validation, "MODEL-PUBLIC-INPUT-ABI", where + "non-contiguous layout");
+        }
+        CompiledRegion& r = *s->region;
+        std::lock_guard<std::mutex> lock(r.mutex);
+        r.planEvidence(ev);
+        cudaCheck(cudaSetDevice(r.device()), "cudaSetDevice");
+        cudaStream_t stream = r.stream();
+        // Artifact-slot arguments: public tensors uploaded into their slot
+        // buffers, parameters from HBM, scalars by value.
+        std::vector<thb_abi_arg> slotArgs(s->sources.size());
+        std::vector<std::array<std::uint64_t, 2>> shapes(s->sources.size());
+        for (std::size_t k = 0; k < s->sources.size(); ++k) {
+            thb_abi_arg& d = slotArgs[k];
+            const std::int64_t src = s->sources[k];
+            if (src >= 0) {
+                d = args[src];
+                if (d.kind == THB_KIND_TENSOR) {
+                    const std::uint64_t bytes = d.count * (d.dtype == THB_DTYPE_I64 ? 8 : 4);
+                    if (!s->publicSlots[k]) s->publicSlots[k] = std::make_unique<DeviceBuffer>();
+                    if (s->publicSlots[k]->reserve(bytes, r.device())) {
+                        ++ev.allocation_count;
+                        ev.allocation_bytes_requested += bytes;
+                    }
+                    if (bytes) {
+                        if (!d.data) fail(Category::Validation, "MODEL-PUBLIC-INPUT-ABI", "tensor data pointer is null");
+                        cudaCheck(cudaMemcpyAsync(s->publicSlots[k]->ptr, d.data, bytes, cudaMemcpyHostToDevice, stream),
+                                  "cudaMemcpyAsync(public input)");
+                        ++ev.host_to_device_copies;
+                        ev.host_to_device_bytes += bytes;
+                        ++ev.input_storage_uploads;
+                    }
+                    d.data = s->publicSlots[k]->ptr;
+                }
+            } else {
+                const std::size_t p = static_cast<std::size_t>(-1 - src);
+                const auto& v = s->parameters[p];
+                d.kind = v.kind;
+                d.dtype = v.dtype;
+                d.rank = static_cast<std::uint32_t>(v.shape.size());
+                d.reserved = 0;
+                d.count = 1;
+                for (std::size_t a = 0; a < v.shape.size(); ++a) {
+                    shapes[k][a] = v.shape[a];
+                    d.count *= v.shape[a];
+                }
+                d.shape = shapes[k].data();
+                d.data = v.kind == 2 ? s->resident[p]->ptr : static_cast<const void*>(v.bytes.data());
+            }
+        }
+        auto inputs = bind(r, slotArgs.data(), slotArgs.size(), false, stream, ev, nullptr);
+        r.clearErrors(stream);
+        ++ev.submitted_operations;
+        Value out = r.run(inputs, stream, ev, nullptr,
+                          [&](const Value& o) { checkOutputCount(o, outputCount, true, output); });
+        downloadOutput(out, output, stream, ev);
+        std::vector<std::uint32_t> words(std::max<std::size_t>(1, r.errorWordCount()));
+        PinnedBuffer staged;
+        staged.reserve(words.size() * sizeof(std::uint32_t));
+        r.copyErrors(stream, static_cast<std::uint32_t*>(staged.ptr));
+        cudaCheck(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
+        ++ev.synchronizations;
+        ++ev.observations;
+        std::memcpy(words.data(), staged.ptr, words.size() * sizeof(std::uint32_t));
+        const std::string id = r.firstFailure(words.data());
+        if (!id.empty()) fail(Category::Semantic, id, id);
+        return THB_STATUS_OK;
+    });
+    if (evidence) *evidence = ev;
+    return status;
 }
 
 int thb_artifact_build(const thb_region_desc* desc, thb_plan_options options, void* buffer, uint64_t capacity,
