@@ -532,3 +532,351 @@ int orc_region_eval(const thb_region_desc* r, const thb_abi_arg* args, uint64_t 
     free(vals);
     return status;
 }
+
+/* ---- software renderer ------------------------------------------------------------
+ * Restatement of src/graphics/v0/Graphics.cpp. This file is compiled with
+ * -ffp-contract=off, so each f32 / f64 operation below rounds on its own like
+ * the reference's volatile helpers (:22-41). */
+
+static int gfx_finite(float v) { return isfinite(v); }
+
+static void gfx_set(float* m, const float* v) { memcpy(m, v, 16 * sizeof(float)); }
+
+void orc_gfx_identity(float* m) {
+    const float v[16] = {1, 0, 0, 0, 0, 1, 0, 0, 0, 0, 1, 0, 0, 0, 0, 1};
+    gfx_set(m, v);
+}
+
+void orc_gfx_translation(float x, float y, float z, float* m) {
+    const float v[16] = {1, 0, 0, x, 0, 1, 0, y, 0, 0, 1, z, 0, 0, 0, 1};
+    gfx_set(m, v);
+}
+
+void orc_gfx_scale(float x, float y, float z, float* m) {
+    const float v[16] = {x, 0, 0, 0, 0, y, 0, 0, 0, 0, z, 0, 0, 0, 0, 1};
+    gfx_set(m, v);
+}
+
+/* Graphics.cpp:448-473 (cosf / sinf of the host C library). */
+void orc_gfx_rotation_x(float r, float* m) {
+    const float c = cosf(r), s = sinf(r);
+    const float v[16] = {1, 0, 0, 0, 0, c, -s, 0, 0, s, c, 0, 0, 0, 0, 1};
+    gfx_set(m, v);
+}
+
+void orc_gfx_rotation_y(float r, float* m) {
+    const float c = cosf(r), s = sinf(r);
+    const float v[16] = {c, 0, s, 0, 0, 1, 0, 0, -s, 0, c, 0, 0, 0, 0, 1};
+    gfx_set(m, v);
+}
+
+void orc_gfx_rotation_z(float r, float* m) {
+    const float c = cosf(r), s = sinf(r);
+    const float v[16] = {c, -s, 0, 0, s, c, 0, 0, 0, 0, 1, 0, 0, 0, 0, 1};
+    gfx_set(m, v);
+}
+
+/* multiply (:475-485): out[r][c] accumulates a[r][k]*b[k][c] over k from 0.0f. */
+void orc_gfx_multiply(const float* a, const float* b, float* out) {
+    float r[16];
+    for (int row = 0; row < 4; ++row)
+        for (int col = 0; col < 4; ++col) {
+            float acc = 0.0f;
+            for (int k = 0; k < 4; ++k) {
+                const float p = a[row * 4 + k] * b[k * 4 + col];
+                acc = acc + p;
+            }
+            r[row * 4 + col] = acc;
+        }
+    gfx_set(out, r);
+}
+
+static float gfx_dot(const float* a, const float* b) {
+    float acc = 0.0f;
+    for (int k = 0; k < 3; ++k) {
+        const float p = a[k] * b[k];
+        acc = acc + p;
+    }
+    return acc;
+}
+
+static void gfx_cross(const float* a, const float* b, float* out) {
+    const float x1 = a[1] * b[2], x2 = a[2] * b[1];
+    const float y1 = a[2] * b[0], y2 = a[0] * b[2];
+    const float z1 = a[0] * b[1], z2 = a[1] * b[0];
+    out[0] = x1 + -x2;
+    out[1] = y1 + -y2;
+    out[2] = z1 + -z2;
+}
+
+static int gfx_normalize(const float* v, float* out) {
+    const float len2 = gfx_dot(v, v);
+    if (!gfx_finite(len2) || len2 <= 0.0f) return 0;
+    const float len = sqrtf(len2);
+    if (!gfx_finite(len) || len <= 1.1920928955078125e-07f) return 0;
+    for (int k = 0; k < 3; ++k) {
+        out[k] = v[k] / len;
+        if (!gfx_finite(out[k])) return 0;
+    }
+    return 1;
+}
+
+/* lookAt (:499-512). */
+const char* orc_gfx_look_at(const float* eye, const float* target, const float* up, float* m) {
+    for (int k = 0; k < 3; ++k)
+        if (!gfx_finite(eye[k]) || !gfx_finite(target[k]) || !gfx_finite(up[k])) return "TH019-CAMERA";
+    float dir[3] = {target[0] - eye[0], target[1] - eye[1], target[2] - eye[2]};
+    float forward[3], sideRaw[3], side[3], cameraUp[3];
+    if (!gfx_normalize(dir, forward)) return "TH019-CAMERA-DIRECTION";
+    gfx_cross(forward, up, sideRaw);
+    if (!gfx_normalize(sideRaw, side)) return "TH019-CAMERA-UP";
+    gfx_cross(side, forward, cameraUp);
+    const float v[16] = {side[0], side[1], side[2], -gfx_dot(side, eye),
+                         cameraUp[0], cameraUp[1], cameraUp[2], -gfx_dot(cameraUp, eye),
+                         -forward[0], -forward[1], -forward[2], gfx_dot(forward, eye),
+                         0, 0, 0, 1};
+    for (int k = 0; k < 16; ++k)
+        if (!gfx_finite(v[k])) return "TH019-NONFINITE-MATRIX";
+    gfx_set(m, v);
+    return 0;
+}
+
+/* perspective (:514-530). */
+const char* orc_gfx_perspective(float fovy, float aspect, float n, float f, float* m) {
+    if (!gfx_finite(fovy) || !gfx_finite(aspect) || !gfx_finite(n) || !gfx_finite(f)) return "TH019-PROJECTION";
+    const float pi = 3.14159265358979323846f;
+    if (fovy <= 0.0f || fovy >= pi || aspect <= 0.0f || n <= 0.0f || f <= n) return "TH019-PROJECTION";
+    const float focal = 1.0f / tanf(fovy * 0.5f);
+    const float depthScale = f / (n - f);
+    const float fn = f * n;
+    const float depthOffset = fn / (n - f);
+    const float v[16] = {focal / aspect, 0, 0, 0, 0, focal, 0, 0, 0, 0, depthScale, depthOffset, 0, 0, -1, 0};
+    for (int k = 0; k < 16; ++k)
+        if (!gfx_finite(v[k])) return "TH019-NONFINITE-MATRIX";
+    gfx_set(m, v);
+    return 0;
+}
+
+/* orthographic (:532-543). */
+const char* orc_gfx_orthographic(float l, float r, float b, float t, float n, float f, float* m) {
+    if (!gfx_finite(l) || !gfx_finite(r) || !gfx_finite(b) || !gfx_finite(t) || !gfx_finite(n) || !gfx_finite(f))
+        return "TH019-PROJECTION";
+    if (r <= l || t <= b || n < 0.0f || f <= n) return "TH019-PROJECTION";
+    const float v[16] = {2.0f / (r - l), 0, 0, -(r + l) / (r - l),
+                         0, 2.0f / (t - b), 0, -(t + b) / (t - b),
+                         0, 0, 1.0f / (n - f), n / (n - f),
+                         0, 0, 0, 1};
+    for (int k = 0; k < 16; ++k)
+        if (!gfx_finite(v[k])) return "TH019-NONFINITE-MATRIX";
+    gfx_set(m, v);
+    return 0;
+}
+
+typedef struct {
+    float p[4];
+    float c[4];
+} gfx_clip_vertex;
+
+/* distance to a clip plane (:102-113): Left, Right, Bottom, Top, Near, Far. */
+static float gfx_distance(const gfx_clip_vertex* v, int plane) {
+    const float* p = v->p;
+    switch (plane) {
+    case 0: return p[0] + p[3];
+    case 1: return p[3] + -p[0];
+    case 2: return p[1] + p[3];
+    case 3: return p[3] + -p[1];
+    case 4: return p[2];
+    default: return p[3] + -p[2];
+    }
+}
+
+static gfx_clip_vertex gfx_interpolate(const gfx_clip_vertex* a, const gfx_clip_vertex* b, float t) {
+    gfx_clip_vertex r;
+    for (int k = 0; k < 4; ++k) {
+        const float dp = b->p[k] + -a->p[k];
+        const float sp = t * dp;
+        r.p[k] = a->p[k] + sp;
+        const float dc = b->c[k] + -a->c[k];
+        const float sc = t * dc;
+        r.c[k] = a->c[k] + sc;
+    }
+    return r;
+}
+
+/* Sutherland-Hodgman against one plane (:126-149); returns the new count or
+ * -1 on TH019-CLIP-NUMERIC. `out` holds at most in + 1 vertices. */
+static int gfx_clip_plane(const gfx_clip_vertex* in, int n, int plane, gfx_clip_vertex* out) {
+    if (n == 0) return 0;
+    int m = 0;
+    gfx_clip_vertex prev = in[n - 1];
+    float prevDist = gfx_distance(&prev, plane);
+    int prevIn = prevDist >= 0.0f;
+    for (int i = 0; i < n; ++i) {
+        const float dist = gfx_distance(&in[i], plane);
+        const int curIn = dist >= 0.0f;
+        if (prevIn != curIn) {
+            const float den = prevDist + -dist;
+            if (den == 0.0f || !gfx_finite(den)) return -1;
+            const float amount = prevDist / den;
+            if (!gfx_finite(amount)) return -1;
+            out[m++] = gfx_interpolate(&prev, &in[i], amount);
+        }
+        if (curIn) out[m++] = in[i];
+        prev = in[i];
+        prevDist = dist;
+        prevIn = curIn;
+    }
+    return m;
+}
+
+typedef struct {
+    double x, y, depth, rw;
+    float c[4];
+} gfx_screen_vertex;
+
+static double gfx_edge(const gfx_screen_vertex* a, const gfx_screen_vertex* b, double x, double y) {
+    const double first = (b->x - a->x) * (y - a->y);
+    const double second = (b->y - a->y) * (x - a->x);
+    return first - second;
+}
+
+static int gfx_top_left(const gfx_screen_vertex* a, const gfx_screen_vertex* b) {
+    const double dx = b->x - a->x, dy = b->y - a->y;
+    return dy < 0.0 || (dy == 0.0 && dx > 0.0);
+}
+
+static int gfx_covered(double v, int inclusive) { return v > 0.0 || (v == 0.0 && inclusive); }
+
+/* prepareScreenTriangle (:348-372). */
+static int gfx_screen(const gfx_clip_vertex* t, uint64_t w, uint64_t h, gfx_screen_vertex* s) {
+    for (int i = 0; i < 3; ++i) {
+        const float cw = t[i].p[3];
+        if (!gfx_finite(cw) || cw <= 1.0e-7f) return 0;
+        const float x = t[i].p[0] / cw, y = t[i].p[1] / cw, z = t[i].p[2] / cw;
+        if (!gfx_finite(x) || !gfx_finite(y) || !gfx_finite(z)) return 0;
+        s[i].x = ((double)x * 0.5 + 0.5) * (double)w;
+        s[i].y = (0.5 - (double)y * 0.5) * (double)h;
+        s[i].depth = z;
+        s[i].rw = 1.0 / (double)cw;
+        memcpy(s[i].c, t[i].c, sizeof s[i].c);
+    }
+    const double area = gfx_edge(&s[0], &s[1], s[2].x, s[2].y);
+    if (!isfinite(area) || fabs(area) <= 1.0e-12) return 0;
+    if (area < 0.0) {
+        const gfx_screen_vertex tmp = s[1];
+        s[1] = s[2];
+        s[2] = tmp;
+    }
+    return 1;
+}
+
+static double gfx_min3(double a, double b, double c) { double m = a < b ? a : b; return m < c ? m : c; }
+static double gfx_max3(double a, double b, double c) { double m = a > b ? a : b; return m > c ? m : c; }
+
+/* rasterize (:251-320). */
+static void gfx_rasterize(const gfx_screen_vertex* v, uint64_t w, uint64_t h, float* color, float* depth,
+                          uint64_t* stats) {
+    if (w == 0 || h == 0) return;
+    const double area = gfx_edge(&v[0], &v[1], v[2].x, v[2].y);
+    int64_t x0 = (int64_t)ceil(gfx_min3(v[0].x, v[1].x, v[2].x) - 0.5);
+    int64_t x1 = (int64_t)floor(gfx_max3(v[0].x, v[1].x, v[2].x) - 0.5);
+    int64_t y0 = (int64_t)ceil(gfx_min3(v[0].y, v[1].y, v[2].y) - 0.5);
+    int64_t y1 = (int64_t)floor(gfx_max3(v[0].y, v[1].y, v[2].y) - 0.5);
+    if (x0 < 0) x0 = 0;
+    if (y0 < 0) y0 = 0;
+    if (x1 > (int64_t)w - 1) x1 = (int64_t)w - 1;
+    if (y1 > (int64_t)h - 1) y1 = (int64_t)h - 1;
+    if (x0 > x1 || y0 > y1) return;
+    const int in0 = gfx_top_left(&v[1], &v[2]), in1 = gfx_top_left(&v[2], &v[0]), in2 = gfx_top_left(&v[0], &v[1]);
+    for (int64_t y = y0; y <= y1; ++y)
+        for (int64_t x = x0; x <= x1; ++x) {
+            const double cx = (double)x + 0.5, cy = (double)y + 0.5;
+            const double e0 = gfx_edge(&v[1], &v[2], cx, cy);
+            const double e1 = gfx_edge(&v[2], &v[0], cx, cy);
+            const double e2 = gfx_edge(&v[0], &v[1], cx, cy);
+            if (!gfx_covered(e0, in0) || !gfx_covered(e1, in1) || !gfx_covered(e2, in2)) continue;
+            const double w0 = e0 / area, w1 = e1 / area, w2 = e2 / area;
+            double d = w0 * v[0].depth + w1 * v[1].depth + w2 * v[2].depth;
+            if (!isfinite(d) || d < -1.0e-6 || d > 1.0 + 1.0e-6) continue;
+            d = d < 0.0 ? 0.0 : (d > 1.0 ? 1.0 : d);
+            const double den = w0 * v[0].rw + w1 * v[1].rw + w2 * v[2].rw;
+            if (!isfinite(den) || den <= 0.0) continue;
+            float c[4];
+            int valid = 1;
+            for (int k = 0; k < 4; ++k) {
+                const double num = w0 * (double)v[0].c[k] * v[0].rw + w1 * (double)v[1].c[k] * v[1].rw +
+                                   w2 * (double)v[2].c[k] * v[2].rw;
+                const double value = num / den;
+                if (!isfinite(value)) { valid = 0; break; }
+                c[k] = (float)(value < 0.0 ? 0.0 : (value > 1.0 ? 1.0 : value));
+            }
+            if (!valid) continue;
+            ++stats[2];
+            const uint64_t pixel = (uint64_t)y * w + (uint64_t)x;
+            if (!((float)d < depth[pixel])) continue;
+            depth[pixel] = (float)d;
+            memcpy(&color[pixel * 4], c, sizeof c);
+            ++stats[3];
+        }
+}
+
+/* render (:574-596) with prepareRender (:374-421). */
+const char* orc_render(const float* positions, uint64_t vertices, const int64_t* indices, uint64_t triangles,
+                       const float* colors, const float* model, const float* view, const float* projection,
+                       uint64_t width, uint64_t height, const float* clear, float* color, float* depth,
+                       uint64_t* stats) {
+    for (uint64_t k = 0; k < vertices * 3; ++k)
+        if (!gfx_finite(positions[k])) return "TH019-NONFINITE-VERTEX";
+    for (uint64_t k = 0; k < vertices * 4; ++k)
+        if (!gfx_finite(colors[k]) || colors[k] < 0.0f || colors[k] > 1.0f) return "TH019-COLOR-RANGE";
+    for (uint64_t k = 0; k < triangles * 3; ++k)
+        if (indices[k] < 0 || (uint64_t)indices[k] >= vertices) return "TH019-INDEX";
+    for (int k = 0; k < 4; ++k)
+        if (!gfx_finite(clear[k]) || clear[k] < 0.0f || clear[k] > 1.0f) return "TH019-CLEAR-COLOR";
+    for (int k = 0; k < 16; ++k)
+        if (!gfx_finite(model[k]) || !gfx_finite(view[k]) || !gfx_finite(projection[k])) return "TH019-NONFINITE-MATRIX";
+    float mv[16], mvp[16];
+    orc_gfx_multiply(view, model, mv);
+    orc_gfx_multiply(projection, mv, mvp);
+    gfx_clip_vertex* clip = (gfx_clip_vertex*)malloc(sizeof(gfx_clip_vertex) * (vertices ? vertices : 1));
+    for (uint64_t v = 0; v < vertices; ++v) {
+        const float in[4] = {positions[v * 3], positions[v * 3 + 1], positions[v * 3 + 2], 1.0f};
+        for (int row = 0; row < 4; ++row) {
+            float acc = 0.0f;
+            for (int col = 0; col < 4; ++col) {
+                const float p = mvp[row * 4 + col] * in[col];
+                acc = acc + p;
+            }
+            if (!gfx_finite(acc)) { free(clip); return "TH019-NONFINITE-TRANSFORMED"; }
+            clip[v].p[row] = acc;
+        }
+        memcpy(clip[v].c, &colors[v * 4], 4 * sizeof(float));
+    }
+    const uint64_t pixels = width * height;
+    for (uint64_t p = 0; p < pixels; ++p) {
+        memcpy(&color[p * 4], clear, 4 * sizeof(float));
+        depth[p] = INFINITY;
+    }
+    stats[0] = triangles;
+    stats[1] = stats[2] = stats[3] = 0;
+    gfx_clip_vertex poly[2][16];
+    for (uint64_t t = 0; t < triangles; ++t) {
+        int n = 3;
+        for (int c = 0; c < 3; ++c) poly[0][c] = clip[indices[t * 3 + c]];
+        int cur = 0;
+        for (int plane = 0; plane < 6 && n >= 3; ++plane) {
+            n = gfx_clip_plane(poly[cur], n, plane, poly[cur ^ 1]);
+            if (n < 0) { free(clip); return "TH019-CLIP-NUMERIC"; }
+            cur ^= 1;
+        }
+        if (n < 3) continue;
+        for (int c = 1; c + 1 < n; ++c) {
+            ++stats[1];
+            const gfx_clip_vertex tri[3] = {poly[cur][0], poly[cur][c], poly[cur][c + 1]};
+            gfx_screen_vertex s[3];
+            if (gfx_screen(tri, width, height, s)) gfx_rasterize(s, width, height, color, depth, stats);
+        }
+    }
+    free(clip);
+    return 0;
+}

@@ -104,6 +104,29 @@ double orc_mlp_step_ex(const float* x, const float* t, float* w1, float* w2, uin
                        uint64_t o, float lr, float* dw1, float* dw2, float* hidden, float* y,
                        const orc_mlp_extras* extras);
 
+/* ---- software renderer (src/graphics/v0/Graphics.cpp) ----------------------
+ * Matrices are 16 f32, row-major, column-vector convention (P*V*M). Every f32
+ * product and sum is rounded separately, as the reference's volatile helpers
+ * do; the rasterizer works in f64 without contraction. Returns 0 or a
+ * TH019-* failure id (static string). */
+void orc_gfx_identity(float* m);
+void orc_gfx_rotation_x(float radians, float* m);
+void orc_gfx_rotation_y(float radians, float* m);
+void orc_gfx_rotation_z(float radians, float* m);
+void orc_gfx_translation(float x, float y, float z, float* m);
+void orc_gfx_scale(float x, float y, float z, float* m);
+void orc_gfx_multiply(const float* a, const float* b, float* out);
+const char* orc_gfx_look_at(const float* eye, const float* target, const float* up, float* m);
+const char* orc_gfx_perspective(float fovy, float aspect, float near_distance, float far_distance, float* m);
+const char* orc_gfx_orthographic(float left, float right, float bottom, float top, float near_distance,
+                                 float far_distance, float* m);
+/* render(): color [w*h][4] and depth [w*h] outputs; stats = input triangles,
+ * post-clip triangles, shaded pixels, depth passes. */
+const char* orc_render(const float* positions, uint64_t vertices, const int64_t* indices, uint64_t triangles,
+                       const float* colors, const float* model, const float* view, const float* projection,
+                       uint64_t width, uint64_t height, const float* clear, float* color, float* depth,
+                       uint64_t* stats);
+
 #ifdef __cplusplus
 }
 #endif

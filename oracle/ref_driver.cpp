@@ -22,6 +22,11 @@
 //       <public-count> inputs are public, the rest frozen parameters (ids 1..,
 //       names p1..) with the given values; one GPU artifact specialised to
 //       these shapes (specializeEntry, NativeArtifacts.cpp:891-922).
+//   ref_driver render <positions.bin> <indices.bin> <colors.bin> <model.bin>
+//                     <view.bin> <projection.bin> <width> <height> <out-prefix>
+//       graphics::render (src/graphics/v0/Graphics.cpp:574-596) with a zero
+//       clear colour; writes <prefix>color.bin / <prefix>depth.bin and prints
+//       the statistics, or the TH019-* failure id.
 //
 // Programs may call the extension operations `research_chain` (the
 // ((x*1.5+0.25)*x - x)*0.5 + x recipe) and `research_square_linear` (x*x + x).
@@ -30,6 +35,7 @@
 // little-endian elements; rank 0 is a scalar.
 #include "artifact/v0/NativeArtifacts.hpp"
 #include "autodiff/v0/Autodiff.hpp"
+#include "graphics/v0/Graphics.hpp"
 #include "model/v0/ModelBundle.hpp"
 #include "backend/v0/NativeCpu.hpp"
 #include "backend/v0/PhysicalPlan.hpp"
@@ -249,6 +255,34 @@ int main(int argc, char** argv) {
             return 64;
         }
         const std::string mode = argv[1];
+        if (mode == "render") {
+            if (argc < 11) throw std::runtime_error("render needs six tensors, width, height and a prefix");
+            auto tensor = [&](int k) {
+                const auto value = readValue(argv[k]);
+                const auto& t = std::get<s::RuntimeTensor>(value.data);
+                std::vector<std::uint64_t> shape(t.shape.begin(), t.shape.end());
+                return t.dtype == s::TypeKind::I64 ? storage::Tensor::materializeI64(shape, t.values)
+                                                   : storage::Tensor::materializeF32(shape, t.f32Values);
+            };
+            try {
+                const auto frame = graphics::render(tensor(2), tensor(3), tensor(4), tensor(5), tensor(6), tensor(7),
+                                                    std::stoull(argv[8]), std::stoull(argv[9]));
+                const std::string prefix = argv[10];
+                auto dump = [&](const storage::Tensor& t, const std::string& path) {
+                    const auto values = t.logicalF32Values();
+                    std::vector<std::int64_t> shape(t.descriptor().shape.begin(), t.descriptor().shape.end());
+                    writeValue(path, s::RuntimeValue{s::RuntimeTensor{s::TypeKind::F32, shape, {}, values}});
+                };
+                dump(frame.framebuffer.color(), prefix + "color.bin");
+                dump(frame.framebuffer.depth(), prefix + "depth.bin");
+                const auto& st = frame.statistics;
+                std::cout << "{\"status\":\"ok\",\"stats\":[" << st.inputTriangleCount << "," << st.postClipTriangleCount
+                          << "," << st.shadedPixelCount << "," << st.depthPassCount << "]}\n";
+            } catch (const std::exception& failure) {
+                std::cout << "{\"status\":\"error\",\"error_id\":\"" << failure.what() << "\"}\n";
+            }
+            return 0;
+        }
         e::ExtensionRegistry registry;
         if (auto r = registry.registerExtension(descriptor); !r.ok()) throw std::runtime_error(r.message);
         const s::Module module = compile(readText(argv[2]), registry);

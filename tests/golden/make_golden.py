@@ -316,7 +316,65 @@ def main():
         assert status == "ok"
         arrays[name], arrays[name + "_eval"] = x, value
 
+    # Software renderer scenes (graphics::render, src/graphics/v0/Graphics.cpp)
+    # rendered by the reference: random triangles under a perspective camera
+    # (clipping, overlap), equal-depth duplicates (first triangle wins), and
+    # an orthographic view cutting the near and far planes.
+    for name, scene in graphics_scenes().items():
+        with tempfile.TemporaryDirectory() as tmp:
+            paths = []
+            for key in ("positions", "indices", "colors", "model", "view", "projection"):
+                p = os.path.join(tmp, key + ".bin")
+                write_thb(p, scene[key])
+                paths.append(p)
+            res = subprocess.run([DRIVER, "render"] + paths + [str(scene["width"]), str(scene["height"]),
+                                                                os.path.join(tmp, "o_")],
+                                 check=True, capture_output=True, text=True)
+            status = json.loads(res.stdout.strip().splitlines()[-1])
+            assert status["status"] == "ok", status
+            for key, value in scene.items():
+                arrays[f"gfx_{name}_{key}"] = np.asarray(value)
+            arrays[f"gfx_{name}_color"] = read_thb(os.path.join(tmp, "o_color.bin"))
+            arrays[f"gfx_{name}_depth"] = read_thb(os.path.join(tmp, "o_depth.bin"))
+            arrays[f"gfx_{name}_stats"] = np.array(status["stats"], np.uint64)
+
     np.savez_compressed(os.path.join(HERE, "reference_outputs.npz"), **arrays)
+
+
+def graphics_scenes():
+    """Scene inputs; matrices come from the oracle's restated helpers (the
+    cube known answer pins them to the reference's)."""
+    sys.path.insert(0, os.path.dirname(HERE))
+    sys.path.insert(0, ROOT)
+    import oracle_lib as orc
+    g = orc.gfx
+    scenes = {}
+    rng = np.random.default_rng(17)
+    n = 240
+    scenes["random"] = dict(
+        positions=rng.uniform(-1.6, 1.6, (n * 3, 3)).astype(np.float32),
+        indices=np.arange(n * 3, dtype=np.int64).reshape(n, 3),
+        colors=rng.uniform(0, 1, (n * 3, 4)).astype(np.float32),
+        model=g.multiply(g.rotation_y(np.float32(0.3)), g.rotation_x(np.float32(-0.2))).reshape(4, 4),
+        view=g.look_at([0.5, 1.0, 3.0], [0, 0, 0], [0, 1, 0]).reshape(4, 4),
+        projection=g.perspective(np.float32(1.1), np.float32(160 / 120), np.float32(0.5), np.float32(20)).reshape(4, 4),
+        width=160, height=120)
+    tri = np.array([[-.8, -.6, .3], [.7, -.5, .3], [0, .8, .3]], np.float32)
+    scenes["ties"] = dict(
+        positions=np.concatenate([tri, tri, tri * 0.5]).astype(np.float32),
+        indices=np.array([[0, 1, 2], [3, 4, 5], [6, 7, 8]], np.int64),
+        colors=np.array([[1, 0, 0, 1]] * 3 + [[0, 1, 0, 1]] * 3 + [[0, 0, 1, 1]] * 3, np.float32),
+        model=g.identity().reshape(4, 4), view=g.identity().reshape(4, 4), projection=g.identity().reshape(4, 4),
+        width=64, height=48)
+    m = 120
+    scenes["ortho"] = dict(
+        positions=rng.uniform(-1.3, 1.3, (m * 3, 3)).astype(np.float32),
+        indices=rng.integers(0, m * 3, (m, 3), dtype=np.int64),
+        colors=rng.uniform(0, 1, (m * 3, 4)).astype(np.float32),
+        model=g.rotation_z(np.float32(0.4)).reshape(4, 4), view=g.identity().reshape(4, 4),
+        projection=g.orthographic(-1.2, 1.2, -1, 1, 0, 1).reshape(4, 4),
+        width=97, height=81)
+    return scenes
     with open(os.path.join(HERE, "reference_fixtures.json"), "w") as f:
         json.dump(fixtures, f, indent=1, sort_keys=True)
     print("wrote", len(arrays), "arrays and", len(fixtures), "fixtures")

@@ -42,6 +42,24 @@ class MlpExtras(C.Structure):
                 ("db2", C.c_void_p)]
 
 
+_m16 = np.ctypeslib.ndpointer(np.float32, shape=(16,), flags="C_CONTIGUOUS")
+for _name in ("orc_gfx_identity",):
+    getattr(_lib, _name).argtypes = [_m16]
+for _name in ("orc_gfx_rotation_x", "orc_gfx_rotation_y", "orc_gfx_rotation_z"):
+    getattr(_lib, _name).argtypes = [C.c_float, _m16]
+for _name in ("orc_gfx_translation", "orc_gfx_scale"):
+    getattr(_lib, _name).argtypes = [C.c_float, C.c_float, C.c_float, _m16]
+_lib.orc_gfx_multiply.argtypes = [_m16, _m16, _m16]
+_lib.orc_gfx_look_at.restype = C.c_char_p
+_lib.orc_gfx_look_at.argtypes = [_f32p, _f32p, _f32p, _m16]
+_lib.orc_gfx_perspective.restype = C.c_char_p
+_lib.orc_gfx_perspective.argtypes = [C.c_float, C.c_float, C.c_float, C.c_float, _m16]
+_lib.orc_gfx_orthographic.restype = C.c_char_p
+_lib.orc_gfx_orthographic.argtypes = [C.c_float] * 6 + [_m16]
+_lib.orc_render.restype = C.c_char_p
+_lib.orc_render.argtypes = [_f32p, C.c_uint64, np.ctypeslib.ndpointer(np.int64, flags="C_CONTIGUOUS"), C.c_uint64,
+                            _f32p, _m16, _m16, _m16, C.c_uint64, C.c_uint64, _f32p, _f32p, _f32p,
+                            np.ctypeslib.ndpointer(np.uint64, flags="C_CONTIGUOUS")]
 _lib.orc_mlp_step_ex.restype = C.c_double
 _lib.orc_mlp_step_ex.argtypes = [_f32p, _f32p, _f32p, _f32p, C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64,
                                  C.c_float, _f32p, _f32p, _f32p, _f32p, C.POINTER(MlpExtras)]
@@ -130,6 +148,57 @@ def mlp_step(x, t, w1, w2, lr):
     y = np.empty((b, o), np.float32)
     loss = _lib.orc_mlp_step(x, t, w1, w2, b, i, h, o, lr, dw1, dw2, hidden, y)
     return loss, dw1, dw2, hidden, y
+
+
+class gfx:
+    """Matrix helpers of the oracle's renderer (16 f32, row-major)."""
+
+    @staticmethod
+    def _m(fn, *args):
+        m = np.empty(16, np.float32)
+        err = fn(*args, m)
+        if err:
+            raise OracleFailure(2, err.decode())
+        return m
+
+    identity = staticmethod(lambda: gfx._m(_lib.orc_gfx_identity))
+    rotation_x = staticmethod(lambda r: gfx._m(_lib.orc_gfx_rotation_x, r))
+    rotation_y = staticmethod(lambda r: gfx._m(_lib.orc_gfx_rotation_y, r))
+    rotation_z = staticmethod(lambda r: gfx._m(_lib.orc_gfx_rotation_z, r))
+    translation = staticmethod(lambda x, y, z: gfx._m(_lib.orc_gfx_translation, x, y, z))
+    scale = staticmethod(lambda x, y, z: gfx._m(_lib.orc_gfx_scale, x, y, z))
+    multiply = staticmethod(lambda a, b: gfx._m(_lib.orc_gfx_multiply, a, b))
+    perspective = staticmethod(lambda fovy, aspect, n, f: gfx._m(_lib.orc_gfx_perspective, fovy, aspect, n, f))
+    orthographic = staticmethod(lambda *a: gfx._m(_lib.orc_gfx_orthographic, *a))
+
+    @staticmethod
+    def look_at(eye, target, up):
+        return gfx._m(_lib.orc_gfx_look_at, np.asarray(eye, np.float32), np.asarray(target, np.float32),
+                      np.asarray(up, np.float32))
+
+
+def render(positions, indices, colors, model, view, projection, width, height, clear=(0, 0, 0, 0)):
+    """orc_render: returns (color [w*h,4], depth [w*h], stats [4])."""
+    positions = np.ascontiguousarray(positions, np.float32).reshape(-1, 3)
+    colors = np.ascontiguousarray(colors, np.float32).reshape(-1, 4)
+    indices = np.ascontiguousarray(indices, np.int64).reshape(-1, 3)
+    color = np.empty((width * height, 4), np.float32)
+    depth = np.empty(width * height, np.float32)
+    stats = np.zeros(4, np.uint64)
+    err = _lib.orc_render(positions.reshape(-1), positions.shape[0], indices.reshape(-1), indices.shape[0],
+                          colors.reshape(-1), model, view, projection, width, height,
+                          np.asarray(clear, np.float32), color.reshape(-1), depth, stats)
+    if err:
+        raise OracleFailure(2, err.decode())
+    return color, depth, stats
+
+
+def fnv_floats(values):
+    """The reference's framebuffer digest (Graphics.cpp:188-200)."""
+    h = 14695981039346656037
+    for byte in np.ascontiguousarray(values, np.float32).tobytes():
+        h = ((h ^ byte) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+    return f"fnv1a64:{h:016x}"
 
 
 def sgd_update(p, g, lr, v=None, momentum=0.0):

@@ -223,3 +223,54 @@ def test_ad_linear_loss_backward_matches_reference(golden, name):
     args = [golden["ad_lin_x"], golden["ad_lin_w1"], golden["ad_lin_w2"], golden["ad_lin_t"], 1.0]
     out = orc.region_eval(regions.linear_loss_backward(name), args)
     assert out.view(np.uint32).tolist() == golden[f"ad_lin_{name}"].view(np.uint32).tolist()
+
+
+def cube_scene():
+    """The reference's TH-019 cube (tests/graphics/v0/GraphicsTests.cpp:358-376)."""
+    g = orc.gfx
+    positions = np.array([-1, -1, -1, 1, -1, -1, 1, 1, -1, -1, 1, -1, -1, -1, 1, 1, -1, 1, 1, 1, 1, -1, 1, 1],
+                         np.float32).reshape(8, 3)
+    indices = np.array([0, 2, 1, 0, 3, 2, 4, 5, 6, 4, 6, 7, 0, 1, 5, 0, 5, 4, 3, 7, 6, 3, 6, 2, 0, 4, 7, 0, 7, 3,
+                        1, 2, 6, 1, 6, 5], np.int64).reshape(12, 3)
+    colors = np.array([1, 0, 0, 1, 0, 1, 0, 1, 0, 0, 1, 1, 1, 1, 0, 1, 1, 0, 1, 1, 0, 1, 1, 1, 1, 1, 1, 1,
+                       .25, .5, .75, 1], np.float32).reshape(8, 4)
+    model = g.multiply(g.rotation_y(np.float32(.55)), g.rotation_x(np.float32(.25)))
+    view = g.look_at([3, 2, 4], [0, 0, 0], [0, 1, 0])
+    projection = g.perspective(np.float32(1.04719755119659774615), 1, np.float32(.1), 100)
+    return positions, indices, colors, model, view, projection
+
+
+def test_renderer_cube_known_answer():
+    """The reference's own cube digests and statistics (GraphicsTests.cpp:383-389)."""
+    color, depth, stats = orc.render(*cube_scene(), 96, 96)
+    assert stats.tolist() == [12, 12, 3150, 2218]
+    assert orc.fnv_floats(color) == "fnv1a64:0d0c47343db9df53"
+    assert orc.fnv_floats(depth) == "fnv1a64:4e244c6d47059a59"
+
+
+@pytest.mark.parametrize("scene", ["random", "ties", "ortho"])
+def test_renderer_matches_reference_scenes(golden, scene):
+    """Scenes rendered by the reference's graphics::render: bit-exact colour
+    and depth, equal statistics (clipping, overlap, equal-depth ties)."""
+    k = lambda key: golden[f"gfx_{scene}_{key}"]
+    color, depth, stats = orc.render(k("positions"), k("indices"), k("colors"), k("model").reshape(16),
+                                     k("view").reshape(16), k("projection").reshape(16), int(k("width")),
+                                     int(k("height")))
+    assert stats.tolist() == k("stats").tolist()
+    assert color.view(np.uint32).tolist() == k("color").view(np.uint32).tolist()
+    assert depth.view(np.uint32).tolist() == k("depth").view(np.uint32).tolist()
+
+
+def test_renderer_failure_ids():
+    g = orc.gfx
+    eye = g.identity()
+    tri = np.zeros((3, 3), np.float32)
+    with pytest.raises(orc.OracleFailure) as err:
+        orc.render(tri, np.array([[0, 1, 3]]), np.zeros((3, 4), np.float32), eye, eye, eye, 4, 4)
+    assert err.value.code == "TH019-INDEX"
+    with pytest.raises(orc.OracleFailure) as err:
+        orc.render(tri, np.array([[0, 1, 2]]), np.full((3, 4), 2, np.float32), eye, eye, eye, 4, 4)
+    assert err.value.code == "TH019-COLOR-RANGE"
+    with pytest.raises(orc.OracleFailure) as err:
+        g.perspective(np.float32(0), 1, np.float32(.1), 100)
+    assert err.value.code == "TH019-PROJECTION"
