@@ -366,6 +366,22 @@ int thb_artifact_inspect(const thb_artifact* artifact, char* buffer, uint64_t ca
  * (executeArtifact / submitArtifactGpu, NativeArtifacts.hpp:125-136). */
 int thb_artifact_compile(const thb_artifact* artifact, int device, thb_region** out, char* failure,
                          uint64_t failure_cap);
+/* ---- software renderer (src/graphics/v0/Graphics.cpp, GraphicsGpu.cpp) --
+ * renderGpu (include/graphics/v0/GraphicsGpu.hpp:76-86): positions [N][3] f32,
+ * indices [T][3] i64, colors [N][4] f32 in [0, 1]; model / view / projection
+ * 16 f32 row-major (column vectors, P*V*M); clear colour 4 f32 (NULL = 0).
+ * Writes color [width*height][4] and depth [width*height] (host buffers) and
+ * stats = {input triangles, post-clip triangles, shaded pixels, depth passes}
+ * (RenderStatistics). Validation, transform and clipping run on the host as
+ * the reference's shared prepareRender; rasterization runs on the GPU
+ * bit-exactly with the reference's CPU rasterizer (f64 edge functions,
+ * perspective-correct colour, strict-less depth test in submission order).
+ * Failures: status 2 with the reference's TH019-* id. */
+int thb_render(int device, const float* positions, uint64_t vertices, const int64_t* indices, uint64_t triangles,
+               const float* colors, const float* model, const float* view, const float* projection, uint64_t width,
+               uint64_t height, const float* clear, float* color, float* depth, uint64_t* stats,
+               thb_evidence* evidence, char* failure, uint64_t failure_cap);
+
 /* ---- `.thm` model bundles (src/model/v0/ModelBundle.cpp) ---------------
  * The reference's container ("THIRANMB", versions, FNV-1a 64 payload digest,
  * identity, entry, frozen parameters, public ABI, bindings, embedded

@@ -161,6 +161,9 @@ SIGNATURES = {
     "thb_artifact_compile": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_void_p), C.c_char_p, C.c_uint64]),
     "thb_artifact_build": (C.c_int, [C.POINTER(RegionDesc), PlanOptions, C.c_void_p, C.c_uint64,
                                      C.POINTER(C.c_uint64), C.c_char_p, C.c_uint64]),
+    "thb_render": (C.c_int, [C.c_int, C.c_void_p, C.c_uint64, C.c_void_p, C.c_uint64, C.c_void_p, C.c_void_p,
+                             C.c_void_p, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_void_p, C.c_void_p,
+                             C.c_void_p, C.POINTER(Evidence), C.c_char_p, C.c_uint64]),
     "thb_model_load": (C.c_int, [C.c_void_p, C.c_uint64, C.c_char_p, C.POINTER(C.c_void_p), C.c_char_p,
                                  C.c_uint64]),
     "thb_model_load_file": (C.c_int, [C.c_char_p, C.c_char_p, C.POINTER(C.c_void_p), C.c_char_p, C.c_uint64]),
@@ -911,6 +914,31 @@ class Model:
             self.release()
         except Exception:
             pass
+
+
+def render(positions, indices, colors, model, view, projection, width, height, clear=(0, 0, 0, 0), device=0):
+    """renderGpu (thb_render): returns (color [w*h, 4], depth [w*h], stats
+    [input triangles, post-clip triangles, shaded pixels, depth passes]) and
+    sets `render.evidence`."""
+    pos = np.ascontiguousarray(positions, np.float32).reshape(-1, 3)
+    col = np.ascontiguousarray(colors, np.float32).reshape(-1, 4)
+    idx = np.ascontiguousarray(indices, np.int64).reshape(-1, 3)
+    if pos.shape[0] != col.shape[0]:
+        raise GpuError(STATUS_SEMANTIC, "TH019-GEOMETRY-COUNT")
+    mats = [np.ascontiguousarray(m, np.float32).reshape(16) for m in (model, view, projection)]
+    clr = np.ascontiguousarray(clear, np.float32).reshape(4)
+    color = np.empty((width * height, 4), np.float32)
+    depth = np.empty(width * height, np.float32)
+    stats = np.zeros(4, np.uint64)
+    ev = Evidence()
+    fail = _failure()
+    ptr = lambda a: a.ctypes.data if a.size else None
+    status = lib().thb_render(device, ptr(pos), pos.shape[0], ptr(idx), idx.shape[0], ptr(col), mats[0].ctypes.data,
+                              mats[1].ctypes.data, mats[2].ctypes.data, width, height, clr.ctypes.data, ptr(color),
+                              ptr(depth), stats.ctypes.data, C.byref(ev), fail, len(fail))
+    render.evidence = ev.as_dict()
+    _raise(status, fail)
+    return color, depth, stats
 
 
 def build_artifact(spec: RegionSpec, reuse=True, fusion=True) -> bytes:

@@ -10,6 +10,7 @@
 
 #include "artifact.hpp"
 #include "gemm.hpp"
+#include "graphics.hpp"
 #include "model.hpp"
 #include "mlp.hpp"
 #include "runtime.hpp"
@@ -391,6 +392,77 @@ int thb_artifact_compile(const thb_artifact* artifact, int device, thb_region** 
         *out = new thb_region{std::move(impl)};
         return THB_STATUS_OK;
     });
+}
+
+// ---- renderer ---------------------------------------------------------------------------
+
+int thb_render(int device, const float* positions, uint64_t vertices, const int64_t* indices, uint64_t triangles,
+               const float* colors, const float* model, const float* view, const float* projection, uint64_t width,
+               uint64_t height, const float* clear, float* color, float* depth, uint64_t* stats, thb_evidence* evidence,
+               char* failure, uint64_t cap) {
+    thb_evidence ev{};
+    const int status = guarded(failure, cap, [&] {
+        namespace gfx = thb::graphics;
+        const float zero[4] = {0, 0, 0, 0};
+        // Preparation first: invalid geometry fails before any driver call.
+        const gfx::Prepared p = gfx::prepare(positions, vertices, indices, triangles, colors, model, view, projection,
+                                             width, height, clear ? clear : zero);
+        const std::uint64_t pixels = width * height;
+        if (pixels && (!color || !depth)) fail(Category::Validation, "TH019-FRAMEBUFFER-TENSOR", "null output buffer");
+        useDevice(device);
+        cudaStream_t stream = nullptr;
+        cudaCheck(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreateWithFlags");
+        struct StreamGuard {
+            cudaStream_t s;
+            ~StreamGuard() { cudaStreamDestroy(s); }
+        } guard{stream};
+        DeviceBuffer tri, offsets, lists, colorBuf, depthBuf, counters;
+        auto upload = [&](DeviceBuffer& b, const void* host, std::size_t bytes) {
+            if (!bytes) return;
+            b.reserve(bytes, device);
+            ++ev.allocation_count;
+            ev.allocation_bytes_requested += bytes;
+            cudaCheck(cudaMemcpyAsync(b.ptr, host, bytes, cudaMemcpyHostToDevice, stream), "cudaMemcpyAsync(render input)");
+            ++ev.host_to_device_copies;
+            ev.host_to_device_bytes += bytes;
+        };
+        upload(tri, p.triangles.data(), p.triangles.size() * sizeof(gfx::RasterTriangle));
+        upload(offsets, p.tileOffsets.data(), p.tileOffsets.size() * sizeof(std::uint32_t));
+        upload(lists, p.tileLists.data(), p.tileLists.size() * sizeof(std::uint32_t));
+        counters.reserve(2 * sizeof(unsigned long long), device);
+        cudaCheck(cudaMemsetAsync(counters.ptr, 0, 2 * sizeof(unsigned long long), stream), "cudaMemsetAsync");
+        if (pixels) {
+            colorBuf.reserve(pixels * 16, device);
+            depthBuf.reserve(pixels * 4, device);
+            ev.allocation_count += 2;
+            ev.allocation_bytes_requested += pixels * 20;
+            cudaCheck(gfx::rasterize(static_cast<const gfx::RasterTriangle*>(tri.ptr),
+                                     static_cast<const std::uint32_t*>(offsets.ptr),
+                                     static_cast<const std::uint32_t*>(lists.ptr), p.tilesX, p.tilesY,
+                                     static_cast<std::uint32_t>(width), static_cast<std::uint32_t>(height), p.clear,
+                                     static_cast<float*>(colorBuf.ptr), static_cast<float*>(depthBuf.ptr),
+                                     static_cast<unsigned long long*>(counters.ptr), stream),
+                      "raster launch");
+            ++ev.kernel_launches;
+            cudaCheck(cudaMemcpyAsync(color, colorBuf.ptr, pixels * 16, cudaMemcpyDeviceToHost, stream), "cudaMemcpyAsync(color)");
+            cudaCheck(cudaMemcpyAsync(depth, depthBuf.ptr, pixels * 4, cudaMemcpyDeviceToHost, stream), "cudaMemcpyAsync(depth)");
+            ev.device_to_host_copies += 2;
+            ev.device_to_host_bytes += pixels * 20;
+        }
+        unsigned long long counts[2] = {0, 0};
+        cudaCheck(cudaMemcpyAsync(counts, counters.ptr, sizeof counts, cudaMemcpyDeviceToHost, stream), "cudaMemcpyAsync(stats)");
+        cudaCheck(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
+        ++ev.synchronizations;
+        if (stats) {
+            stats[0] = p.inputTriangles;
+            stats[1] = p.postClipTriangles;
+            stats[2] = counts[0];
+            stats[3] = counts[1];
+        }
+        return THB_STATUS_OK;
+    });
+    if (evidence) *evidence = ev;
+    return status;
 }
 
 // ---- model bundles ----------------------------------------------------------------------
