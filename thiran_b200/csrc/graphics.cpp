@@ -7,8 +7,10 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <limits>
+#include <thread>
 
 #include "common.hpp"
 
@@ -49,7 +51,35 @@ ClipVertex lerp(const ClipVertex& a, const ClipVertex& b, float t) {
     return r;
 }
 
-// One Sutherland-Hodgman pass (Graphics.cpp:126-149).
+// Worker threads for `items` independent items (1 below 4096; at most
+// THB_HOST_THREADS when set, else the hardware threads, 64 at most).
+unsigned workerCount(std::uint64_t items) {
+    if (items < 4096) return 1;
+    unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    if (const char* env = std::getenv("THB_HOST_THREADS")) hw = std::max(1, std::atoi(env));
+    return static_cast<unsigned>(std::min<std::uint64_t>({hw, 64u, items / 2048}));
+}
+
+// Runs f(worker, begin, end) over `threads` contiguous chunks of [0, items).
+// f must not throw.
+template <class F>
+void parallelChunks(std::uint64_t items, unsigned threads, F&& f) {
+    if (threads <= 1) {
+        f(0u, 0ull, items);
+        return;
+    }
+    std::vector<std::thread> pool;
+    const std::uint64_t per = (items + threads - 1) / threads;
+    for (unsigned w = 0; w < threads; ++w) {
+        const std::uint64_t begin = std::min<std::uint64_t>(items, w * per);
+        const std::uint64_t end = std::min<std::uint64_t>(items, begin + per);
+        pool.emplace_back([&f, w, begin, end] { f(w, begin, end); });
+    }
+    for (auto& t : pool) t.join();
+}
+
+// One Sutherland-Hodgman pass (Graphics.cpp:126-149); -1 where the reference
+// fails with TH019-CLIP-NUMERIC.
 int clipPlane(const ClipVertex* in, int n, int plane, ClipVertex* out) {
     if (n == 0) return 0;
     int m = 0;
@@ -61,9 +91,9 @@ int clipPlane(const ClipVertex* in, int n, int plane, ClipVertex* out) {
         const bool inside = d >= 0.0f;
         if (prevInside != inside) {
             const float den = prevDistance + -d;
-            if (den == 0.0f || !finite(den)) bad("TH019-CLIP-NUMERIC");
+            if (den == 0.0f || !finite(den)) return -1;
             const float amount = prevDistance / den;
-            if (!finite(amount)) bad("TH019-CLIP-NUMERIC");
+            if (!finite(amount)) return -1;
             out[m++] = lerp(prev, in[i], amount);
         }
         if (inside) out[m++] = in[i];
@@ -184,64 +214,110 @@ Prepared prepare(const float* positions, std::uint64_t vertices, const std::int6
     multiply(projection, mv, mvp);
     for (int k = 0; k < 16; ++k)
         if (!finite(mv[k]) || !finite(mvp[k])) bad("TH019-NONFINITE-MATRIX");
+    // Transform, clip and bin in contiguous chunks on host threads; chunk
+    // results are joined in order, so the output equals a serial pass. The
+    // first failure of any chunk is the reference's failure too: every
+    // failure here has one id per step (NONFINITE-TRANSFORMED, CLIP-NUMERIC).
+    const unsigned threads = workerCount(std::max(vertices, triangles));
     std::vector<ClipVertex> clip(vertices);
-    for (std::uint64_t v = 0; v < vertices; ++v) {
-        const float in[4] = {positions[v * 3], positions[v * 3 + 1], positions[v * 3 + 2], 1.0f};
-        for (int row = 0; row < 4; ++row) {
-            float acc = 0.0f;
-            for (int col = 0; col < 4; ++col) {
-                const float p = mvp[row * 4 + col] * in[col];
-                acc = acc + p;
+    std::vector<char> transformFailed(threads, 0);
+    parallelChunks(vertices, threads, [&](unsigned w, std::uint64_t begin, std::uint64_t end) {
+        for (std::uint64_t v = begin; v < end; ++v) {
+            const float in[4] = {positions[v * 3], positions[v * 3 + 1], positions[v * 3 + 2], 1.0f};
+            for (int row = 0; row < 4; ++row) {
+                float acc = 0.0f;
+                for (int col = 0; col < 4; ++col) {
+                    const float p = mvp[row * 4 + col] * in[col];
+                    acc = acc + p;
+                }
+                if (!finite(acc)) transformFailed[w] = 1;
+                clip[v].p[row] = acc;
             }
-            if (!finite(acc)) bad("TH019-NONFINITE-TRANSFORMED");
-            clip[v].p[row] = acc;
+            std::memcpy(clip[v].c, colors + v * 4, sizeof clip[v].c);
         }
-        std::memcpy(clip[v].c, colors + v * 4, sizeof clip[v].c);
-    }
-    ClipVertex poly[2][16];
-    for (std::uint64_t t = 0; t < triangles; ++t) {
-        int n = 3;
-        for (int c = 0; c < 3; ++c) poly[0][c] = clip[static_cast<std::size_t>(indices[t * 3 + c])];
-        int cur = 0;
-        for (int plane = 0; plane < 6 && n >= 3; ++plane) {
-            n = clipPlane(poly[cur], n, plane, poly[cur ^ 1]);
-            cur ^= 1;
-        }
-        if (n < 3) continue;
-        for (int c = 1; c + 1 < n; ++c) {
-            ++out.postClipTriangles;
-            const ClipVertex tri[3] = {poly[cur][0], poly[cur][c], poly[cur][c + 1]};
-            ScreenVertex s[3];
-            RasterTriangle packed;
-            if (toScreen(tri, width, height, s) && pack(s, width, height, packed)) out.triangles.push_back(packed);
-        }
-    }
-    if (out.triangles.size() > std::numeric_limits<std::uint32_t>::max())
-        bad("TH019-FRAMEBUFFER-SIZE");
+    });
+    for (char f : transformFailed)
+        if (f) bad("TH019-NONFINITE-TRANSFORMED");
 
-    // Tiles of 16x16 pixels; each list keeps submission order.
+    struct Chunk {
+        std::vector<RasterTriangle> triangles;
+        std::uint64_t postClip = 0;
+        bool clipFailed = false;
+    };
+    std::vector<Chunk> chunks(threads);
+    parallelChunks(triangles, threads, [&](unsigned w, std::uint64_t begin, std::uint64_t end) {
+        Chunk& chunk = chunks[w];
+        ClipVertex poly[2][16];
+        for (std::uint64_t t = begin; t < end && !chunk.clipFailed; ++t) {
+            int n = 3;
+            for (int c = 0; c < 3; ++c) poly[0][c] = clip[static_cast<std::size_t>(indices[t * 3 + c])];
+            int cur = 0;
+            for (int plane = 0; plane < 6 && n >= 3; ++plane) {
+                n = clipPlane(poly[cur], n, plane, poly[cur ^ 1]);
+                if (n < 0) {
+                    chunk.clipFailed = true;
+                    break;
+                }
+                cur ^= 1;
+            }
+            if (n < 3) continue;
+            for (int c = 1; c + 1 < n; ++c) {
+                ++chunk.postClip;
+                const ClipVertex tri[3] = {poly[cur][0], poly[cur][c], poly[cur][c + 1]};
+                ScreenVertex s[3];
+                RasterTriangle packed;
+                if (toScreen(tri, width, height, s) && pack(s, width, height, packed)) chunk.triangles.push_back(packed);
+            }
+        }
+    });
+    std::uint64_t total = 0;
+    for (const auto& c : chunks) {
+        if (c.clipFailed) bad("TH019-CLIP-NUMERIC");
+        out.postClipTriangles += c.postClip;
+        total += c.triangles.size();
+    }
+    if (total > std::numeric_limits<std::uint32_t>::max()) bad("TH019-FRAMEBUFFER-SIZE");
+    out.triangles.reserve(total);
+    for (auto& c : chunks) {
+        out.triangles.insert(out.triangles.end(), c.triangles.begin(), c.triangles.end());
+        std::vector<RasterTriangle>().swap(c.triangles);
+    }
+
+    // Tiles of 16x16 pixels; each list keeps submission order: per-chunk
+    // counts, offsets = tile-major then chunk-major prefix sums, parallel fill.
     out.tilesX = static_cast<std::uint32_t>((width + kTile - 1) / kTile);
     out.tilesY = static_cast<std::uint32_t>((height + kTile - 1) / kTile);
     const std::uint64_t tiles = static_cast<std::uint64_t>(out.tilesX) * out.tilesY;
     if (tiles >= std::numeric_limits<std::uint32_t>::max()) bad("TH019-FRAMEBUFFER-SIZE");
+    const std::uint64_t count = out.triangles.size();
+    const unsigned binThreads = tiles * workerCount(count) > (64ull << 20) ? 1 : workerCount(count);
+    std::vector<std::uint64_t> counts(binThreads * tiles, 0);
+    auto forTiles = [&](const RasterTriangle& t, auto&& f) {
+        for (std::int32_t ty = t.y0 / kTile; ty <= t.y1 / kTile; ++ty)
+            for (std::int32_t tx = t.x0 / kTile; tx <= t.x1 / kTile; ++tx) f(static_cast<std::uint64_t>(ty) * out.tilesX + tx);
+    };
+    parallelChunks(count, binThreads, [&](unsigned w, std::uint64_t begin, std::uint64_t end) {
+        std::uint64_t* c = counts.data() + w * tiles;
+        for (std::uint64_t i = begin; i < end; ++i) forTiles(out.triangles[i], [&](std::uint64_t k) { ++c[k]; });
+    });
     out.tileOffsets.assign(tiles + 1, 0);
+    std::vector<std::uint64_t> starts(binThreads * tiles);
     std::uint64_t entries = 0;
-    for (const auto& t : out.triangles)
-        for (std::int32_t ty = t.y0 / kTile; ty <= t.y1 / kTile; ++ty)
-            for (std::int32_t tx = t.x0 / kTile; tx <= t.x1 / kTile; ++tx) {
-                ++out.tileOffsets[static_cast<std::uint64_t>(ty) * out.tilesX + tx + 1];
-                ++entries;
-            }
-    if (entries >= std::numeric_limits<std::uint32_t>::max()) bad("TH019-FRAMEBUFFER-SIZE");
-    for (std::uint64_t k = 0; k < tiles; ++k) out.tileOffsets[k + 1] += out.tileOffsets[k];
-    out.tileLists.resize(entries);
-    std::vector<std::uint32_t> cursor(out.tileOffsets.begin(), out.tileOffsets.end() - 1);
-    for (std::uint32_t i = 0; i < out.triangles.size(); ++i) {
-        const auto& t = out.triangles[i];
-        for (std::int32_t ty = t.y0 / kTile; ty <= t.y1 / kTile; ++ty)
-            for (std::int32_t tx = t.x0 / kTile; tx <= t.x1 / kTile; ++tx)
-                out.tileLists[cursor[static_cast<std::uint64_t>(ty) * out.tilesX + tx]++] = i;
+    for (std::uint64_t k = 0; k < tiles; ++k) {
+        out.tileOffsets[k] = static_cast<std::uint32_t>(std::min<std::uint64_t>(entries, ~0u));
+        for (unsigned w = 0; w < binThreads; ++w) {
+            starts[w * tiles + k] = entries;
+            entries += counts[w * tiles + k];
+        }
     }
+    if (entries >= std::numeric_limits<std::uint32_t>::max()) bad("TH019-FRAMEBUFFER-SIZE");
+    out.tileOffsets[tiles] = static_cast<std::uint32_t>(entries);
+    out.tileLists.resize(entries);
+    parallelChunks(count, binThreads, [&](unsigned w, std::uint64_t begin, std::uint64_t end) {
+        std::uint64_t* cursor = starts.data() + w * tiles;
+        for (std::uint64_t i = begin; i < end; ++i)
+            forTiles(out.triangles[i], [&](std::uint64_t k) { out.tileLists[cursor[k]++] = static_cast<std::uint32_t>(i); });
+    });
     return out;
 }
 
