@@ -223,8 +223,8 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
     elif world > 1:
         collective = "NCCL all-reduce of dW1, dW2 and the bias gradients"
 
-    def step():
-        session.forward_backward(x, t, s)
+    def step(xx=x, tt=t):
+        session.forward_backward(xx, tt, s)
         if fused:
             with torch.cuda.stream(stream):
                 fused.after_backward()
@@ -260,20 +260,48 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
     value = workload.flops_per_step() * args.steps / (total_ms / 1e3) / 1e12
     achieved = (flops_rank / 5) * gemm_launches / (gemm_ms / 1e3) / 1e12
 
-    # End to end: X, T from pinned host memory every step, loss read back.
+    # End to end: X, T from pinned host memory every step, loss read back
+    # every step. A training loop's input pipeline: step i+1's batch crosses
+    # PCIe on a copy stream into the second of two device buffers while
+    # step i computes; the host reads step i's loss during step i+1.
     hx = x.cpu().pin_memory()
     ht = t.cpu().pin_memory()
-    host_loss = torch.zeros(2, dtype=torch.float64).pin_memory()
+    host_loss = [torch.zeros(2, dtype=torch.float64).pin_memory() for _ in range(2)]
     e2e_steps = args.e2e_steps or max(3, min(args.steps, 10))
+    copy_stream = torch.cuda.Stream()
+    xs, ts = [x, torch.empty_like(x)], [t, torch.empty_like(t)]
+    ready = [torch.cuda.Event() for _ in range(2)]
+    consumed = [torch.cuda.Event() for _ in range(2)]
+    loss_read = [torch.cuda.Event() for _ in range(2)]
+    used = [False, False]
+
+    def prefetch(i):
+        j = i % 2
+        if used[j]:
+            copy_stream.wait_event(consumed[j])
+        with torch.cuda.stream(copy_stream):
+            xs[j].copy_(hx, non_blocking=True)
+            ts[j].copy_(ht, non_blocking=True)
+            ready[j].record(copy_stream)
+
+    torch.cuda.synchronize()
     barrier()
     t0 = time.perf_counter()
+    prefetch(0)
     with torch.cuda.stream(stream):
-        for _ in range(e2e_steps):
-            x.copy_(hx, non_blocking=True)
-            t.copy_(ht, non_blocking=True)
-            step()
-            host_loss.copy_(loss, non_blocking=True)
-            stream.synchronize()
+        for i in range(e2e_steps):
+            j = i % 2
+            if i + 1 < e2e_steps:
+                prefetch(i + 1)
+            stream.wait_event(ready[j])
+            step(xs[j], ts[j])
+            consumed[j].record(stream)
+            used[j] = True
+            host_loss[j].copy_(loss, non_blocking=True)
+            loss_read[j].record(stream)
+            if i > 0:
+                loss_read[1 - j].synchronize()
+        stream.synchronize()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     e2e_value = workload.flops_per_step() * e2e_steps / e2e_s / 1e12
 
@@ -313,12 +341,15 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
             "config": dict(workload.config(world), **({"gradient_reduction": collective} if collective else {})),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": None,
-                         "kernel": "tcgen05 GEMM (128x256 tiles, TMEM accumulators)",
+                         "kernel": "tcgen05 GEMM (256x256 tiles on CTA pairs, cta_group::2, TMEM accumulators; "
+                                   "dW GEMMs with the fused all-reduce: 128x256 tiles on single CTAs)",
                          "algorithmic_flops_per_launch": flops_rank / 5,
                          "avg_launch_ms": gemm_ms / max(1, gemm_launches), "peak_source": peak_kind},
             "cpu_baseline": cpu_baseline,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": (x.numel() + t.numel()) * 4,
-                    "d2h_bytes_per_step": 16, "steps": e2e_steps, "api": "thb_mlp_* (inputs from pinned host)"},
+                    "d2h_bytes_per_step": 16, "steps": e2e_steps,
+                    "api": "thb_mlp_* (inputs from pinned host, next batch copied during the current step; "
+                           "loss read back every step)"},
             "gpu_launches": args.steps * 10,
             "clocks": clocks,
             "loss": float(loss[0].item()) / (workload.batch * d_out) if world == 1 else None,

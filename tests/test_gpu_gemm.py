@@ -42,7 +42,10 @@ def run_gemm(torch, a32, b32, a_major, b_major, epilogue=thb.EPI_F32, aux32=None
 
 @pytest.mark.parametrize("a_major", [thb.MAJOR_K, thb.MAJOR_MN])
 @pytest.mark.parametrize("b_major", [thb.MAJOR_K, thb.MAJOR_MN])
-@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 512, 640), (384, 768, 1024), (200, 296, 136)])
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 512, 640), (384, 768, 1024), (200, 296, 136),
+                                   # CTA-pair tiles (256 rows): second block partly / wholly past M,
+                                   # more tiles than pairs; single CTAs: more tiles than SMs
+                                   (136, 512, 128), (296, 256, 64), (4096, 2048, 256), (128, 40960, 192)])
 def test_gemm_majors_and_shapes(device, a_major, b_major, m, n, k):
     torch = pytest.importorskip("torch")
     rng = np.random.default_rng(m * 131 + n * 7 + k)

@@ -102,7 +102,7 @@ def test_mlp_training_trajectory_matches_oracle(device):
 
 
 @pytest.mark.parametrize("batch,d_in,hidden,d_out,momentum", [(256, 256, 512, 256, 0.0), (256, 256, 512, 256, 0.9),
-                                                              (200, 136, 520, 136, 0.5)])
+                                                              (200, 136, 520, 136, 0.5), (384, 256, 512, 256, 0.9)])
 def test_mlp_biases_and_momentum_match_oracle(device, batch, d_in, hidden, d_out, momentum):
     """The examples/mlp.th structure (broadcast biases, their gradients the
     column sums of dH and dY) with SGD or SGD with momentum (Training.cpp:

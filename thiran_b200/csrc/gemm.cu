@@ -14,9 +14,14 @@
 //   warps 6..9  (fused all-reduce only) reducers: sum the tiles this rank
 //               owns over all ranks and write the totals to every rank
 // Two TMEM accumulators (2 x 256 columns) let the epilogue of tile i overlap
-// the MMAs of tile i+1. Every wait (mbarrier, tile queue, other ranks'
-// signal words) is bounded: on expiry the CTA raises bit 4 of the status
-// word, drains its copies and MMAs, frees TMEM and returns.
+// the MMAs of tile i+1. Past one 128-row block the same roles run in CTA
+// pairs (clusters of two, tcgen05 cta_group::2) on 256x256 tiles: each CTA
+// stages half of A and half of B, the even CTA issues M=256 MMAs over both,
+// and each CTA's epilogue drains its own 128 TMEM lanes (the fused
+// all-reduce keeps single CTAs: its signal words are per 128-row tile).
+// Every wait (mbarrier, tile queue, other ranks' signal words) is bounded:
+// on expiry the CTA raises bit 4 of the status word, drains its copies and
+// MMAs, frees TMEM and returns.
 //
 // The reference's only matmul is its Evaluator's sequential f32 triple loop
 // (src/semantic/v0/Evaluator.cpp:125-154); reverse-mode rules dA = dZ B^T,
@@ -27,6 +32,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdint>
+#include <cstdlib>
 #include <mutex>
 
 #include "gemm.hpp"
@@ -39,9 +45,21 @@ constexpr int kThreads = 192;
 // The fused all-reduce adds 4 reducer warps (warps 6..9).
 constexpr int threadsFor(int epilogue) { return epilogue == kEpiAllReduceF32 ? kThreads + 128 : kThreads; }
 constexpr uint32_t kABytes = kBM * kBK * 2;  // 16 KB
-constexpr uint32_t kBBytes = kBN * kBK * 2;  // 32 KB
-constexpr uint32_t kStageBytes = kABytes + kBBytes;
-constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024;  // + alignment slack
+
+// Stage geometry. PAIR = a cluster of two CTAs on one 256x256 tile with
+// tcgen05.mma.cta_group::2 (M = 256): each CTA stages its 128 rows of A and
+// its 128 columns of B, so a stage is 32 KB and six fit where four single-CTA
+// stages (48 KB) did. Operand bytes moved from L2 per FLOP drop by a third.
+template <bool PAIR>
+struct Geometry {
+    static constexpr int stages = PAIR ? 6 : kStages;
+    static constexpr uint32_t bRows = PAIR ? kBN / 2 : kBN;  // B rows (N) staged per CTA
+    static constexpr uint32_t bBytes = bRows * kBK * 2;
+    static constexpr uint32_t stageBytes = kABytes + bBytes;
+    static constexpr uint32_t tileM = PAIR ? 2 * kBM : kBM;
+    static constexpr uint32_t smemBytes = stages * stageBytes + 1024;
+};
+static_assert(Geometry<true>::smemBytes <= 232448 && Geometry<false>::smemBytes <= 232448, "shared memory");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kWaitStatus = 16u;
 constexpr uint64_t kSpinLimit = 1ull << 24;
@@ -93,14 +111,15 @@ __device__ __forceinline__ uint64_t ummaDesc(uint32_t addr, uint32_t lbo, uint32
     return d;
 }
 
-// Instruction descriptor: bf16 x bf16 -> f32, dense, M=128, N=256.
-template <bool A_MN, bool B_MN>
+// Instruction descriptor: bf16 x bf16 -> f32, dense, N=256, M=128 (one CTA)
+// or M=256 (a CTA pair).
+template <bool A_MN, bool B_MN, bool PAIR>
 __device__ __forceinline__ constexpr uint32_t instrDesc() {
     return (1u << 4)                          // D format f32
            | (1u << 7)                        // A bf16
            | (1u << 10)                       // B bf16
            | (static_cast<uint32_t>(A_MN) << 15) | (static_cast<uint32_t>(B_MN) << 16) |
-           (static_cast<uint32_t>(kBN >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
+           (static_cast<uint32_t>(kBN >> 3) << 17) | (static_cast<uint32_t>(Geometry<PAIR>::tileM >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
@@ -113,6 +132,58 @@ __device__ __forceinline__ void mma(uint32_t tmem, uint64_t a, uint64_t b, uint3
 
 __device__ __forceinline__ void mmaCommit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem(bar))
+                 : "memory");
+}
+
+// ---- CTA pairs (cta_group::2) ----
+__device__ __forceinline__ uint32_t clusterRank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Shared-memory address of the same object in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t pairAddress(const void* p, uint32_t rank) {
+    uint32_t a;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem(p)), "r"(rank));
+    return a;
+}
+
+// All threads of both CTAs.
+__device__ __forceinline__ void clusterSync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbarArriveCluster(uint32_t clusterAddress) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(clusterAddress) : "memory");
+}
+
+// A load into this CTA's shared memory whose completion is counted on an
+// mbarrier of either CTA of the pair (.cta_group::2). No multicast: each CTA
+// loads only its own half of the operands.
+__device__ __forceinline__ void tmaLoad2dPair(void* dst, const CUtensorMap* map, int32_t x, int32_t y,
+                                              uint32_t barClusterAddress) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(barClusterAddress)
+        : "memory");
+}
+
+__device__ __forceinline__ void mmaPair(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrives on the barrier at this offset in both CTAs once the pair's MMAs
+// issued so far have completed.
+__device__ __forceinline__ void mmaCommitPair(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                     smem(bar)),
+                 "h"(static_cast<uint16_t>(3))
                  : "memory");
 }
 
@@ -387,11 +458,16 @@ __device__ __forceinline__ bool reduceRows(const Params& p, uint32_t tile, uint3
     return true;
 }
 
-template <bool A_MN, bool B_MN, int EPI>
+// PAIR: launched as clusters of two CTAs. Rank 0 (the leader) issues the
+// MMAs of the 256-row tile for both; each CTA stages its own halves, its
+// epilogue reads its own 128 TMEM lanes (rows), and both epilogues release an
+// accumulator on the leader's tmemEmpty barrier.
+template <bool A_MN, bool B_MN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(threadsFor(EPI), 1)
     gemmKernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, const Params p) {
+    using G = Geometry<PAIR>;
     extern __shared__ uint8_t dynamicSmem[];
-    __shared__ __align__(8) uint64_t full[kStages], empty[kStages], tmemFull[2], tmemEmpty[2], mmaDone;
+    __shared__ __align__(8) uint64_t full[G::stages], empty[G::stages], tmemFull[2], tmemEmpty[2], mmaDone;
     __shared__ uint32_t tmemSlot;
     __shared__ volatile int abortFlag;
     __shared__ TileQueue queues[4];  // kEpiAllReduceF32: one per TMEM quadrant
@@ -399,99 +475,153 @@ __global__ void __launch_bounds__(threadsFor(EPI), 1)
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dynamicSmem) + 1023) & ~uintptr_t(1023));
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const uint32_t tiles = p.mTiles * p.nTiles;
+    const uint32_t rank = PAIR ? clusterRank() : 0u;
+    // Tile schedule: pairs (clusters) or single CTAs take tiles g, g + n, ...
+    const uint32_t first = PAIR ? blockIdx.x / 2 : blockIdx.x;
+    const uint32_t step = PAIR ? gridDim.x / 2 : gridDim.x;
 
     if (threadIdx.x == 0) {
         abortFlag = 0;
         for (auto& q : queues) q.head = q.tail = 0;
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < G::stages; ++s) {
             mbarInit(&full[s], 1);
             mbarInit(&empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
             mbarInit(&tmemFull[a], 1);
-            mbarInit(&tmemEmpty[a], 128);
+            mbarInit(&tmemEmpty[a], PAIR ? 256 : 128);
         }
         mbarInit(&mmaDone, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem(&tmemSlot)),
-                     "r"(kTmemCols)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        if constexpr (PAIR) {
+            // Collective over the pair: the same columns in both CTAs.
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem(&tmemSlot)),
+                         "r"(kTmemCols)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem(&tmemSlot)),
+                         "r"(kTmemCols)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        }
     }
     fenceBefore();
     __syncthreads();
+    // The peer's barriers are initialised before any remote arrival or load.
+    if constexpr (PAIR) clusterSync();
     fenceAfter();
     const uint32_t tmemBase = tmemSlot;
 
     if (warp == 0 && lane == 0) {
         // ---- TMA producer ----
         uint32_t stage = 0, phase = 0;
-        uint32_t issuedParity[kStages];
+        uint32_t issuedParity[G::stages];
         uint32_t issued = 0;  // bitmask of stages with a load issued
-        for (uint32_t tile = blockIdx.x; tile < tiles && !abortFlag; tile += gridDim.x) {
+        for (uint32_t tile = first; tile < tiles && !abortFlag; tile += step) {
             uint32_t mb, nb;
             tileCoords(tile, p, mb, nb);
+            // This CTA's rows of A and columns of B.
+            const int32_t row0 = static_cast<int32_t>(mb * G::tileM + rank * kBM);
+            const int32_t col0 = static_cast<int32_t>(nb * kBN + rank * G::bRows);
             for (uint32_t kb = 0; kb < p.kBlocks; ++kb) {
                 if (!mbarWait(&empty[stage], phase ^ 1u, &abortFlag)) { abortFlag = 1; break; }
-                uint8_t* a = base + stage * kStageBytes;
+                uint8_t* a = base + stage * G::stageBytes;
                 uint8_t* b = a + kABytes;
-                mbarExpect(&full[stage], kStageBytes);
                 const int32_t k0 = static_cast<int32_t>(kb * kBK);
-                if constexpr (A_MN) {
-                    tmaLoad2d(a, &mapA, static_cast<int32_t>(mb * kBM), k0, &full[stage]);
-                    tmaLoad2d(a + kABytes / 2, &mapA, static_cast<int32_t>(mb * kBM + 64), k0, &full[stage]);
-                } else {
-                    tmaLoad2d(a, &mapA, k0, static_cast<int32_t>(mb * kBM), &full[stage]);
-                }
-                if constexpr (B_MN) {
+                if constexpr (PAIR) {
+                    // Both CTAs' loads complete on the leader's barrier, which
+                    // expects the bytes of the whole pair.
+                    if (rank == 0) mbarExpect(&full[stage], 2 * G::stageBytes);
+                    const uint32_t bar = pairAddress(&full[stage], 0);
+                    if constexpr (A_MN) {
+                        tmaLoad2dPair(a, &mapA, row0, k0, bar);
+                        tmaLoad2dPair(a + kABytes / 2, &mapA, row0 + 64, k0, bar);
+                    } else {
+                        tmaLoad2dPair(a, &mapA, k0, row0, bar);
+                    }
+                    if constexpr (B_MN) {
 #pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        tmaLoad2d(b + j * (kBBytes / 4), &mapB, static_cast<int32_t>(nb * kBN + 64 * j), k0, &full[stage]);
+                        for (int j = 0; j < static_cast<int>(G::bRows / 64); ++j)
+                            tmaLoad2dPair(b + j * (G::bBytes / (G::bRows / 64)), &mapB, col0 + 64 * j, k0, bar);
+                    } else {
+                        tmaLoad2dPair(b, &mapB, k0, col0, bar);
+                    }
                 } else {
-                    tmaLoad2d(b, &mapB, k0, static_cast<int32_t>(nb * kBN), &full[stage]);
+                    mbarExpect(&full[stage], G::stageBytes);
+                    if constexpr (A_MN) {
+                        tmaLoad2d(a, &mapA, row0, k0, &full[stage]);
+                        tmaLoad2d(a + kABytes / 2, &mapA, row0 + 64, k0, &full[stage]);
+                    } else {
+                        tmaLoad2d(a, &mapA, k0, row0, &full[stage]);
+                    }
+                    if constexpr (B_MN) {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            tmaLoad2d(b + j * (G::bBytes / 4), &mapB, col0 + 64 * j, k0, &full[stage]);
+                    } else {
+                        tmaLoad2d(b, &mapB, k0, col0, &full[stage]);
+                    }
                 }
                 issuedParity[stage] = phase;
                 issued |= 1u << stage;
-                if (++stage == kStages) { stage = 0; phase ^= 1u; }
+                if (++stage == G::stages) { stage = 0; phase ^= 1u; }
             }
         }
         if (abortFlag) {
-            // Let loads already issued land before the CTA can exit.
-            for (int s = 0; s < kStages; ++s)
-                if (issued & (1u << s)) (void)mbarWait(&full[s], issuedParity[s]);
+            // Let loads already issued land before the CTA can exit. A pair
+            // counts them on the leader's barriers, which only the leader can
+            // wait on; the peer gives its loads a fixed 200 us instead.
+            if (!PAIR || rank == 0) {
+                for (int s = 0; s < G::stages; ++s)
+                    if (issued & (1u << s)) (void)mbarWait(&full[s], issuedParity[s]);
+            } else {
+                for (int k = 0; k < 2000; ++k) __nanosleep(100);
+            }
         }
     } else if (warp == 1 && lane == 0) {
         // ---- MMA issuer ----
-        constexpr uint32_t idesc = instrDesc<A_MN, B_MN>();
-        uint32_t stage = 0, phase = 0, acc = 0, accPhase = 0;
-        for (uint32_t tile = blockIdx.x; tile < tiles && !abortFlag; tile += gridDim.x) {
-            if (!mbarWait(&tmemEmpty[acc], accPhase ^ 1u, &abortFlag)) { abortFlag = 1; break; }
-            fenceAfter();
-            const uint32_t d = tmemBase + acc * kBN;
-            bool ok = true;
-            for (uint32_t kb = 0; kb < p.kBlocks; ++kb) {
-                if (!mbarWait(&full[stage], phase, &abortFlag)) { abortFlag = 1; ok = false; break; }
+        // (PAIR: the leader only; its MMAs read both CTAs' stages and write
+        // both CTAs' TMEM, and its commits arrive in both CTAs.)
+        if (!PAIR || rank == 0) {
+            constexpr uint32_t idesc = instrDesc<A_MN, B_MN, PAIR>();
+            constexpr uint32_t bAtom = G::bBytes / (G::bRows / 64);  // MN-major B: 64-column atoms
+            auto commit = [](uint64_t* bar) {
+                if constexpr (PAIR) mmaCommitPair(bar);
+                else mmaCommit(bar);
+            };
+            uint32_t stage = 0, phase = 0, acc = 0, accPhase = 0;
+            for (uint32_t tile = first; tile < tiles && !abortFlag; tile += step) {
+                if (!mbarWait(&tmemEmpty[acc], accPhase ^ 1u, &abortFlag)) { abortFlag = 1; break; }
                 fenceAfter();
-                const uint32_t a = smem(base + stage * kStageBytes);
-                const uint32_t b = a + kABytes;
+                const uint32_t d = tmemBase + acc * kBN;
+                bool ok = true;
+                for (uint32_t kb = 0; kb < p.kBlocks; ++kb) {
+                    if (!mbarWait(&full[stage], phase, &abortFlag)) { abortFlag = 1; ok = false; break; }
+                    fenceAfter();
+                    const uint32_t a = smem(base + stage * G::stageBytes);
+                    const uint32_t b = a + kABytes;
 #pragma unroll
-                for (uint32_t ks = 0; ks < kBK / 16; ++ks) {
-                    const uint64_t da = A_MN ? ummaDesc(a + ks * 2048u, kABytes / 2, 1024u) : ummaDesc(a + ks * 32u, 16u, 1024u);
-                    const uint64_t db = B_MN ? ummaDesc(b + ks * 2048u, kBBytes / 4, 1024u) : ummaDesc(b + ks * 32u, 16u, 1024u);
-                    mma(d, da, db, idesc, (kb | ks) != 0 ? 1u : 0u);
+                    for (uint32_t ks = 0; ks < kBK / 16; ++ks) {
+                        const uint64_t da =
+                            A_MN ? ummaDesc(a + ks * 2048u, kABytes / 2, 1024u) : ummaDesc(a + ks * 32u, 16u, 1024u);
+                        const uint64_t db = B_MN ? ummaDesc(b + ks * 2048u, bAtom, 1024u) : ummaDesc(b + ks * 32u, 16u, 1024u);
+                        if constexpr (PAIR) mmaPair(d, da, db, idesc, (kb | ks) != 0 ? 1u : 0u);
+                        else mma(d, da, db, idesc, (kb | ks) != 0 ? 1u : 0u);
+                    }
+                    commit(&empty[stage]);
+                    if (++stage == G::stages) { stage = 0; phase ^= 1u; }
                 }
-                mmaCommit(&empty[stage]);
-                if (++stage == kStages) { stage = 0; phase ^= 1u; }
+                if (!ok) break;
+                commit(&tmemFull[acc]);
+                if (++acc == 2) { acc = 0; accPhase ^= 1u; }
             }
-            if (!ok) break;
-            mmaCommit(&tmemFull[acc]);
-            if (++acc == 2) { acc = 0; accPhase ^= 1u; }
+            // All MMAs issued by this thread complete before TMEM is released.
+            commit(&mmaDone);
+            if (!mbarWait(&mmaDone, 0)) abortFlag = 1;
         }
-        // All MMAs issued by this thread complete before TMEM is released.
-        mmaCommit(&mmaDone);
-        if (!mbarWait(&mmaDone, 0)) abortFlag = 1;
     } else if (warp >= 2 && warp < 6) {
         // ---- epilogue ----
         const uint32_t quadrant = warp % 4;  // TMEM lanes 32*quadrant .. +31
@@ -499,15 +629,22 @@ __global__ void __launch_bounds__(threadsFor(EPI), 1)
         uint32_t acc = 0, accPhase = 0;
         TileQueue& queue = queues[quadrant];
         (void)queue;
-        for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+        // This CTA's 128-row block (its TMEM holds those rows of the tile).
+        const uint32_t blocksPerTile = G::tileM / kBM;
+        const uint32_t releaseAddress = PAIR ? pairAddress(&tmemEmpty[0], 0) : 0u;
+        for (uint32_t tile = first; tile < tiles; tile += step) {
             uint32_t mb, nb;
             tileCoords(tile, p, mb, nb);
             if (!mbarWait(&tmemFull[acc], accPhase, &abortFlag)) abortFlag = 1;
             if (abortFlag) break;
             fenceAfter();
-            const uint64_t grow = static_cast<uint64_t>(mb) * kBM + row;
+            const uint32_t rowBlock = mb * blocksPerTile + rank;
+            const uint64_t grow = static_cast<uint64_t>(rowBlock) * kBM + row;
+            // A pair's second row block can lie wholly past M (no rows, and
+            // no column-sum rows either).
+            const uint32_t chunks = static_cast<uint64_t>(rowBlock) * kBM < p.m ? kBN / 32 : 0u;
 #pragma unroll 1
-            for (uint32_t chunk = 0; chunk < kBN / 32; ++chunk) {
+            for (uint32_t chunk = 0; chunk < chunks; ++chunk) {
                 uint32_t r[32];
                 tmemLoad32(tmemBase + ((quadrant * 32u) << 16) + acc * kBN + chunk * 32u, r);
                 const uint64_t col0 = static_cast<uint64_t>(nb) * kBN + chunk * 32u;
@@ -570,7 +707,8 @@ __global__ void __launch_bounds__(threadsFor(EPI), 1)
 #pragma unroll
                         for (int j = 0; j < 32; ++j) s[j] = rowValid ? v[j] : 0.0f;
                         const float total = columnSum32(s, lane);
-                        if (col0 + lane < p.n) p.colSums[(static_cast<uint64_t>(mb) * 4 + quadrant) * p.n + col0 + lane] = total;
+                        if (col0 + lane < p.n)
+                            p.colSums[(static_cast<uint64_t>(rowBlock) * 4 + quadrant) * p.n + col0 + lane] = total;
                         if (!rowValid) continue;
                     }
                 }
@@ -607,7 +745,10 @@ __global__ void __launch_bounds__(threadsFor(EPI), 1)
                 }
             }
             fenceBefore();
-            mbarArrive(&tmemEmpty[acc]);
+            // The accumulator is free once both CTAs of a pair have read it;
+            // the leader's barrier counts all 256 epilogue threads.
+            if (PAIR && rank != 0) mbarArriveCluster(releaseAddress + acc * static_cast<uint32_t>(sizeof(uint64_t)));
+            else mbarArrive(&tmemEmpty[acc]);
             if (++acc == 2) { acc = 0; accPhase ^= 1u; }
             if constexpr (EPI == kEpiAllReduceF32) {
                 // Announce this tile; owned tiles go to this quadrant's reducer warp.
@@ -633,9 +774,15 @@ __global__ void __launch_bounds__(threadsFor(EPI), 1)
     }
     __syncthreads();
     if (threadIdx.x == 0 && abortFlag) atomicOr(p.status, kWaitStatus);
+    // A pair stays resident until both CTAs are done: the leader's MMAs read
+    // the peer's shared memory and the peer arrives on the leader's barriers.
+    if constexpr (PAIR) clusterSync();
     if (warp == 1) {
         fenceAfter();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmemBase), "r"(kTmemCols) : "memory");
+        if constexpr (PAIR)
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmemBase), "r"(kTmemCols) : "memory");
+        else
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmemBase), "r"(kTmemCols) : "memory");
     }
 }
 
@@ -667,25 +814,73 @@ bool makeMap(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, 
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool A_MN, bool B_MN, int EPI>
-cudaError_t launchTyped(const CUtensorMap& a, const CUtensorMap& b, const Params& p, int smCount, cudaStream_t stream) {
-    auto kernel = gemmKernel<A_MN, B_MN, EPI>;
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+// p.grid CTAs; a pair kernel is launched as clusters of two (p.grid even).
+template <bool A_MN, bool B_MN, int EPI, bool PAIR>
+cudaError_t launchTyped(const CUtensorMap& a, const CUtensorMap& b, const Params& p, cudaStream_t stream) {
+    auto kernel = gemmKernel<A_MN, B_MN, EPI, PAIR>;
+    constexpr uint32_t smemBytes = Geometry<PAIR>::smemBytes;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smemBytes);
     if (e != cudaSuccess) return e;
-    kernel<<<p.grid, threadsFor(EPI), kSmemBytes, stream>>>(a, b, p);
-    return cudaGetLastError();
+    if constexpr (!PAIR) {
+        kernel<<<p.grid, threadsFor(EPI), smemBytes, stream>>>(a, b, p);
+        return cudaGetLastError();
+    } else {
+        cudaLaunchConfig_t config{};
+        config.gridDim = dim3(p.grid);
+        config.blockDim = dim3(threadsFor(EPI));
+        config.dynamicSmemBytes = smemBytes;
+        config.stream = stream;
+        cudaLaunchAttribute attribute{};
+        attribute.id = cudaLaunchAttributeClusterDimension;
+        attribute.val.clusterDim.x = 2;
+        attribute.val.clusterDim.y = 1;
+        attribute.val.clusterDim.z = 1;
+        config.attrs = &attribute;
+        config.numAttrs = 1;
+        // Persistent pairs: no more clusters than can be resident at once
+        // (SMs left over by the GPC layout cannot host a pair).
+        static int resident = -1;
+        if (resident < 0) {
+            int clusters = 0;
+            resident = cudaOccupancyMaxActiveClusters(&clusters, kernel, &config) == cudaSuccess ? clusters : 0;
+            (void)cudaGetLastError();
+        }
+        if (resident > 0 && p.grid > 2u * static_cast<uint32_t>(resident)) config.gridDim = dim3(2u * resident);
+        return cudaLaunchKernelEx(&config, kernel, a, b, p);
+    }
 }
 
 template <bool A_MN, bool B_MN>
-cudaError_t launchEpi(int epi, const CUtensorMap& a, const CUtensorMap& b, const Params& p, int sm, cudaStream_t s) {
+cudaError_t launchEpi(int epi, bool pair, const CUtensorMap& a, const CUtensorMap& b, const Params& p, cudaStream_t s) {
+    if (pair) {
+        switch (epi) {
+        case kEpiF32: return launchTyped<A_MN, B_MN, kEpiF32, true>(a, b, p, s);
+        case kEpiBf16: return launchTyped<A_MN, B_MN, kEpiBf16, true>(a, b, p, s);
+        case kEpiReluBf16: return launchTyped<A_MN, B_MN, kEpiReluBf16, true>(a, b, p, s);
+        case kEpiMaskBf16: return launchTyped<A_MN, B_MN, kEpiMaskBf16, true>(a, b, p, s);
+        }
+        return cudaErrorInvalidValue;
+    }
     switch (epi) {
-    case kEpiF32: return launchTyped<A_MN, B_MN, kEpiF32>(a, b, p, sm, s);
-    case kEpiBf16: return launchTyped<A_MN, B_MN, kEpiBf16>(a, b, p, sm, s);
-    case kEpiReluBf16: return launchTyped<A_MN, B_MN, kEpiReluBf16>(a, b, p, sm, s);
-    case kEpiMaskBf16: return launchTyped<A_MN, B_MN, kEpiMaskBf16>(a, b, p, sm, s);
-    case kEpiAllReduceF32: return launchTyped<A_MN, B_MN, kEpiAllReduceF32>(a, b, p, sm, s);
+    case kEpiF32: return launchTyped<A_MN, B_MN, kEpiF32, false>(a, b, p, s);
+    case kEpiBf16: return launchTyped<A_MN, B_MN, kEpiBf16, false>(a, b, p, s);
+    case kEpiReluBf16: return launchTyped<A_MN, B_MN, kEpiReluBf16, false>(a, b, p, s);
+    case kEpiMaskBf16: return launchTyped<A_MN, B_MN, kEpiMaskBf16, false>(a, b, p, s);
+    case kEpiAllReduceF32: return launchTyped<A_MN, B_MN, kEpiAllReduceF32, false>(a, b, p, s);
     }
     return cudaErrorInvalidValue;
+}
+
+// CTA pairs for every epilogue but the cross-GPU all-reduce (whose signal
+// words are per 128-row tile), once M spans two row blocks and there are at
+// least as many pair tiles as pairs of SMs would want work. THB_GEMM_PAIR=0
+// keeps single CTAs.
+bool usePairs(const Problem& q) {
+    static const bool enabled = [] {
+        const char* e = std::getenv("THB_GEMM_PAIR");
+        return !(e && e[0] == '0');
+    }();
+    return enabled && q.epilogue != kEpiAllReduceF32 && q.m > static_cast<uint64_t>(kBM);
 }
 
 } // namespace
@@ -724,15 +919,18 @@ std::uint64_t tileCount(std::uint64_t m, std::uint64_t n) { return ((m + kBM - 1
 std::uint64_t colSumRows(std::uint64_t m) { return 4 * ((m + kBM - 1) / kBM); }
 
 cudaError_t run(const Problem& q, int smCount, uint32_t* status, cudaStream_t stream) {
+    const bool pair = usePairs(q) && smCount >= 2;
+    const uint32_t tileM = pair ? Geometry<true>::tileM : Geometry<false>::tileM;
+    const uint32_t bRows = pair ? Geometry<true>::bRows : Geometry<false>::bRows;
     CUtensorMap a, b;
     const bool okA = q.aMajorMN ? makeMap(&a, q.a, q.m, q.k, q.lda, 64) : makeMap(&a, q.a, q.k, q.m, q.lda, kBM);
-    const bool okB = q.bMajorMN ? makeMap(&b, q.b, q.n, q.k, q.ldb, 64) : makeMap(&b, q.b, q.k, q.n, q.ldb, kBN);
+    const bool okB = q.bMajorMN ? makeMap(&b, q.b, q.n, q.k, q.ldb, 64) : makeMap(&b, q.b, q.k, q.n, q.ldb, bRows);
     if (!okA || !okB) return cudaErrorInvalidValue;
     Params p{};
     p.m = static_cast<uint32_t>(q.m);
     p.n = static_cast<uint32_t>(q.n);
     p.k = static_cast<uint32_t>(q.k);
-    p.mTiles = static_cast<uint32_t>((q.m + kBM - 1) / kBM);
+    p.mTiles = static_cast<uint32_t>((q.m + tileM - 1) / tileM);
     p.nTiles = static_cast<uint32_t>((q.n + kBN - 1) / kBN);
     p.kBlocks = static_cast<uint32_t>((q.k + kBK - 1) / kBK);
     p.c = q.c;
@@ -742,7 +940,8 @@ cudaError_t run(const Problem& q, int smCount, uint32_t* status, cudaStream_t st
     p.c2 = q.c2;
     p.status = status;
     const uint32_t tiles = p.mTiles * p.nTiles;
-    p.grid = tiles < static_cast<uint32_t>(smCount) ? tiles : static_cast<uint32_t>(smCount);
+    const uint32_t slots = pair ? static_cast<uint32_t>(smCount) / 2 : static_cast<uint32_t>(smCount);
+    p.grid = (tiles < slots ? tiles : slots) * (pair ? 2u : 1u);
     p.cMc = static_cast<float*>(q.reduce.cMulticast);
     for (int r = 0; r < kMaxRanks; ++r) {
         p.cPeers[r] = static_cast<float*>(q.reduce.cPeers[r]);
@@ -754,11 +953,11 @@ cudaError_t run(const Problem& q, int smCount, uint32_t* status, cudaStream_t st
     p.bias = q.bias;
     p.colSums = q.colSums;
     if (q.aMajorMN) {
-        if (q.bMajorMN) return launchEpi<true, true>(q.epilogue, a, b, p, smCount, stream);
-        return launchEpi<true, false>(q.epilogue, a, b, p, smCount, stream);
+        if (q.bMajorMN) return launchEpi<true, true>(q.epilogue, pair, a, b, p, stream);
+        return launchEpi<true, false>(q.epilogue, pair, a, b, p, stream);
     }
-    if (q.bMajorMN) return launchEpi<false, true>(q.epilogue, a, b, p, smCount, stream);
-    return launchEpi<false, false>(q.epilogue, a, b, p, smCount, stream);
+    if (q.bMajorMN) return launchEpi<false, true>(q.epilogue, pair, a, b, p, stream);
+    return launchEpi<false, false>(q.epilogue, pair, a, b, p, stream);
 }
 
 } // namespace thb::gemm
