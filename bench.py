@@ -224,6 +224,9 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
         collective = "NCCL all-reduce of dW1, dW2 and the bias gradients"
 
     def step(xx=x, tt=t):
+        if world == 1:  # thb_mlp_step: the weight updates run in the dW GEMMs' read-out
+            session.step(xx, tt, lr, s)
+            return
         session.forward_backward(xx, tt, s)
         if fused:
             with torch.cuda.stream(stream):
@@ -338,7 +341,9 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (torch.Generator on device, seeded)",
-            "config": dict(workload.config(world), **({"gradient_reduction": collective} if collective else {})),
+            "config": dict(workload.config(world), **({"gradient_reduction": collective} if collective else {}),
+                           optimizer=("SGD applied in the dW GEMMs' read-out (thb_mlp_step), biases by a separate "
+                                      "pass" if world == 1 else "SGD pass after the gradient all-reduce")),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": None,
                          "kernel": "tcgen05 GEMM (256x256 tiles on CTA pairs, cta_group::2, TMEM accumulators; "

@@ -504,7 +504,12 @@ int thb_mlp_set_biases(thb_mlp* session, const float* b1, const float* b2, void*
  * reference's OPT05 / OPT06 bounds; otherwise status 2 with that id), and
  * zeroes every velocity (the reference initialises them ZeroLike). */
 int thb_mlp_set_momentum(thb_mlp* session, float momentum, void* stream, char* failure, uint64_t failure_cap);
-/* One full single-device step: forward_backward then apply_sgd. */
+/* One full single-device training step (training::trainingStep,
+ * src/training/v0/Training.cpp:382-432): forward, loss, backward and the
+ * optimizer update. The weight updates run inside the weight-gradient GEMMs'
+ * read-out, bit-identical to forward_backward + apply_sgd, so THB_MLP_DW1 /
+ * DW2 are not written by this call (the bias gradients are). A session with
+ * a bound gradient all-reduce is refused (GPU-MLP-ARGUMENT). */
 int thb_mlp_step(thb_mlp* session, const float* x, const float* t, float lr, void* stream, char* failure,
                  uint64_t failure_cap);
 /* Device pointer and element count of a session buffer (THB_MLP_*); Y, dW,

@@ -45,7 +45,8 @@ def test_mlp_step_matches_oracle(device, batch, d_in, hidden, d_out):
     L = s.bind(thb.MLP_LOSS_SUM, torch.zeros(2, dtype=torch.float64, device="cuda"))
     stream = torch.cuda.current_stream().cuda_stream
     s.set_weights(cuda(w1), cuda(w2), stream)
-    s.step(X, T, lr, stream)
+    s.forward_backward(X, T, stream)
+    s.apply_sgd(lr, stream)
     thb.check_device_status(0, stream)
     torch.cuda.synchronize()
 
@@ -181,3 +182,47 @@ def test_mlp_rejects_bad_extents(device):
     with pytest.raises(thb.GpuError) as err:
         thb.MlpSession(100, 256, 512, 128)  # batch not a multiple of 8
     assert err.value.code == "GPU-MLP-ARGUMENT"
+
+
+@pytest.mark.parametrize("batch,d_in,hidden,d_out,momentum,biases", [(256, 256, 512, 256, 0.0, False),
+                                                                     (384, 256, 512, 256, 0.9, True),
+                                                                     (200, 136, 520, 136, 0.5, True)])
+def test_mlp_fused_update_step_is_bit_identical(device, batch, d_in, hidden, d_out, momentum, biases):
+    """thb_mlp_step applies the weight updates inside the dW GEMMs' read-out;
+    three steps must give the same parameter bits (and the same loss) as
+    forward_backward followed by the standalone SGD pass. The last shape
+    leaves partial tiles, where the read-out takes its scalar path."""
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(17)
+    x = torch.from_numpy(rng.standard_normal((batch, d_in)).astype(np.float32)).cuda()
+    t = torch.from_numpy(rng.standard_normal((batch, d_out)).astype(np.float32)).cuda()
+    w1 = torch.from_numpy(xavier(rng, d_in, hidden)).cuda()
+    w2 = torch.from_numpy(xavier(rng, hidden, d_out)).cuda()
+    b1 = torch.from_numpy((rng.standard_normal(hidden) * 0.1).astype(np.float32)).cuda()
+    b2 = torch.from_numpy((rng.standard_normal(d_out) * 0.1).astype(np.float32)).cuda()
+    runs = []
+    for fused in (False, True):
+        s = thb.MlpSession(batch, d_in, hidden, d_out)
+        params = {"w1": s.bind(thb.MLP_W1, torch.empty_like(w1)), "w2": s.bind(thb.MLP_W2, torch.empty_like(w2))}
+        loss = s.bind(thb.MLP_LOSS_SUM, torch.zeros(2, dtype=torch.float64, device="cuda"))
+        s.set_weights(w1, w2)
+        if biases:
+            s.set_biases(b1, b2)
+            params["b1"] = s.bind(thb.MLP_B1, b1.clone())
+            params["b2"] = s.bind(thb.MLP_B2, b2.clone())
+        s.set_momentum(momentum)
+        losses = []
+        for _ in range(3):
+            if fused:
+                s.step(x, t, 0.05)
+            else:
+                s.forward_backward(x, t)
+                s.apply_sgd(0.05)
+            losses.append(loss[0].item())
+        thb.check_device_status(0)
+        runs.append(({k: v.cpu() for k, v in params.items()}, losses))
+        s.release()
+    (plain, plain_losses), (fused_p, fused_losses) = runs
+    assert plain_losses == fused_losses
+    for k in plain:
+        assert torch.equal(plain[k].view(torch.int32), fused_p[k].view(torch.int32)), k

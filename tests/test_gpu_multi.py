@@ -113,7 +113,8 @@ def single_gpu_reference():
     dbias = bind_bias_gradients(s)
     X, T = torch.from_numpy(x).cuda(), torch.from_numpy(t).cuda()
     for _ in range(3):
-        s.step(X, T, LR)
+        s.forward_backward(X, T)
+        s.apply_sgd(LR)
     torch.cuda.synchronize()
     return dict(dw1=dw1.cpu().numpy(), dw2=dw2.cpu().numpy(), dbias=dbias.cpu().numpy(),
                 **{k: v.cpu().numpy() for k, v in params.items()})

@@ -237,6 +237,8 @@ class MlpSession:
         self._call("thb_mlp_set_momentum", C.c_float(momentum), C.c_void_p(stream))
 
     def step(self, x, t, lr, stream=0):
+        """One single-device training step; the weight updates run in the dW
+        GEMMs' read-out, so the DW1 / DW2 buffers are not written."""
         self._call("thb_mlp_step", x.data_ptr(), t.data_ptr(), C.c_float(lr), C.c_void_p(stream))
 
     def enable_timing(self, enabled=True):

@@ -994,9 +994,22 @@ int thb_mlp_apply_sgd(thb_mlp* s, float lr, void* stream, char* failure, uint64_
 }
 
 int thb_mlp_step(thb_mlp* s, const float* x, const float* t, float lr, void* stream, char* failure, uint64_t cap) {
-    const int status = thb_mlp_forward_backward(s, x, t, stream, failure, cap);
-    if (status != THB_STATUS_OK) return status;
-    return thb_mlp_apply_sgd(s, lr, stream, failure, cap);
+    return guarded(failure, cap, [&] {
+        if (!s || !x || !t) fail(Category::Validation, "GPU-MLP-ARGUMENT", "null session or data");
+        if ((reinterpret_cast<std::uintptr_t>(x) | reinterpret_cast<std::uintptr_t>(t)) % 16)
+            fail(Category::Validation, "GPU-MLP-ARGUMENT", "x and t must be 16-byte aligned");
+        if (s->b.dw1Reduce.cPeers[0] || s->b.dw2Reduce.cPeers[0])
+            fail(Category::Validation, "GPU-MLP-ARGUMENT",
+                 "thb_mlp_step is the single-device step; a session with a bound gradient all-reduce runs "
+                 "thb_mlp_forward_backward, a barrier, then thb_mlp_apply_sgd");
+        useDevice(s->device);
+        const auto st = static_cast<cudaStream_t>(stream);
+        // The weight updates run in the dW GEMM epilogues; the biases follow.
+        cudaCheck(mlp::forwardBackward(s->b, x, t, s->smCount, deviceStatus(s->device), st, &s->timer, &lr),
+                  "MLP step");
+        cudaCheck(mlp::applySgd(s->b, lr, s->smCount, st, false), "MLP bias update");
+        return THB_STATUS_OK;
+    });
 }
 
 int thb_mlp_buffer(thb_mlp* s, uint32_t which, void** pointer, uint64_t* elements) {

@@ -36,6 +36,7 @@
 #include <mutex>
 
 #include "gemm.hpp"
+#include "sgd.cuh"
 
 namespace thb::gemm {
 namespace {
@@ -219,6 +220,10 @@ struct Params {
     uint32_t rank, world, target;
     const float* bias;              // [n] or null
     float* colSums;                 // [mTiles * 4][n] or null (kEpiMaskBf16)
+    // kEpiSgdF32
+    float* velocity;                // [m][ldc] or null
+    __nv_bfloat16* copy;            // [m][ldc] or null
+    float lr, mu;
 };
 
 // Lane j ends with the sum over the warp's 32 lanes of s[j] (a butterfly
@@ -712,7 +717,49 @@ __global__ void __launch_bounds__(threadsFor(EPI), 1)
                         if (!rowValid) continue;
                     }
                 }
-                if constexpr (EPI == kEpiF32 || EPI == kEpiAllReduceF32) {
+                if constexpr (EPI == kEpiSgdF32) {
+                    // v[] is the gradient; C holds the parameters.
+                    float* dst = static_cast<float*>(p.c) + grow * p.ldc + col0;
+                    float* vel = p.velocity ? p.velocity + grow * p.ldc + col0 : nullptr;
+                    __nv_bfloat16* cp = p.copy ? p.copy + grow * p.ldc + col0 : nullptr;
+                    const uintptr_t bits = reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(vel) |
+                                           reinterpret_cast<uintptr_t>(cp);
+                    if (full32 && bits % 16 == 0) {
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            float4 w = *reinterpret_cast<const float4*>(dst + 4 * q);
+                            if (vel) {
+                                float4 m = *reinterpret_cast<const float4*>(vel + 4 * q);
+                                w.x = sgdStep(w.x, v[4 * q], &m.x, p.lr, p.mu);
+                                w.y = sgdStep(w.y, v[4 * q + 1], &m.y, p.lr, p.mu);
+                                w.z = sgdStep(w.z, v[4 * q + 2], &m.z, p.lr, p.mu);
+                                w.w = sgdStep(w.w, v[4 * q + 3], &m.w, p.lr, p.mu);
+                                *reinterpret_cast<float4*>(vel + 4 * q) = m;
+                            } else {
+                                w.x = sgdStep(w.x, v[4 * q], nullptr, p.lr, p.mu);
+                                w.y = sgdStep(w.y, v[4 * q + 1], nullptr, p.lr, p.mu);
+                                w.z = sgdStep(w.z, v[4 * q + 2], nullptr, p.lr, p.mu);
+                                w.w = sgdStep(w.w, v[4 * q + 3], nullptr, p.lr, p.mu);
+                            }
+                            *reinterpret_cast<float4*>(dst + 4 * q) = w;
+                            if (cp) {
+                                const __nv_bfloat162 lo = __floats2bfloat162_rn(w.x, w.y);
+                                const __nv_bfloat162 hi = __floats2bfloat162_rn(w.z, w.w);
+                                uint2 packed;
+                                packed.x = *reinterpret_cast<const uint32_t*>(&lo);
+                                packed.y = *reinterpret_cast<const uint32_t*>(&hi);
+                                *reinterpret_cast<uint2*>(cp + 4 * q) = packed;
+                            }
+                        }
+                    } else {
+                        for (int j = 0; j < 32; ++j) {
+                            if (col0 + j >= p.n) break;
+                            const float w = sgdStep(dst[j], v[j], vel ? vel + j : nullptr, p.lr, p.mu);
+                            dst[j] = w;
+                            if (cp) cp[j] = __float2bfloat16_rn(w);
+                        }
+                    }
+                } else if constexpr (EPI == kEpiF32 || EPI == kEpiAllReduceF32) {
                     float* dst = static_cast<float*>(p.c) + grow * p.ldc + col0;
                     if (full32 && reinterpret_cast<uintptr_t>(dst) % 16 == 0) {
 #pragma unroll
@@ -858,6 +905,7 @@ cudaError_t launchEpi(int epi, bool pair, const CUtensorMap& a, const CUtensorMa
         case kEpiBf16: return launchTyped<A_MN, B_MN, kEpiBf16, true>(a, b, p, s);
         case kEpiReluBf16: return launchTyped<A_MN, B_MN, kEpiReluBf16, true>(a, b, p, s);
         case kEpiMaskBf16: return launchTyped<A_MN, B_MN, kEpiMaskBf16, true>(a, b, p, s);
+        case kEpiSgdF32: return launchTyped<A_MN, B_MN, kEpiSgdF32, true>(a, b, p, s);
         }
         return cudaErrorInvalidValue;
     }
@@ -866,6 +914,7 @@ cudaError_t launchEpi(int epi, bool pair, const CUtensorMap& a, const CUtensorMa
     case kEpiBf16: return launchTyped<A_MN, B_MN, kEpiBf16, false>(a, b, p, s);
     case kEpiReluBf16: return launchTyped<A_MN, B_MN, kEpiReluBf16, false>(a, b, p, s);
     case kEpiMaskBf16: return launchTyped<A_MN, B_MN, kEpiMaskBf16, false>(a, b, p, s);
+    case kEpiSgdF32: return launchTyped<A_MN, B_MN, kEpiSgdF32, false>(a, b, p, s);
     case kEpiAllReduceF32: return launchTyped<A_MN, B_MN, kEpiAllReduceF32, false>(a, b, p, s);
     }
     return cudaErrorInvalidValue;
@@ -894,7 +943,12 @@ const char* validate(const Problem& q) {
     if (q.lda < (q.aMajorMN ? q.m : q.k) || q.ldb < (q.bMajorMN ? q.n : q.k)) return "leading dimension too small";
     if (q.ldc < q.n) return "ldc smaller than N";
     if (q.epilogue == kEpiMaskBf16 && (!q.aux || q.ldAux < q.n)) return "mask epilogue needs an auxiliary bf16 matrix";
-    if (q.epilogue < kEpiF32 || q.epilogue > kEpiAllReduceF32) return "unknown epilogue";
+    if (q.epilogue < kEpiF32 || q.epilogue > kEpiSgdF32) return "unknown epilogue";
+    if (q.epilogue == kEpiSgdF32) {
+        const Update& u = q.update;
+        if (!(u.momentum >= 0.0f && u.momentum < 1.0f)) return "the fused update needs momentum in [0, 1)";
+        if (u.momentum > 0.0f && !u.velocity) return "momentum needs the velocity buffer";
+    }
     if (q.bias && (q.epilogue == kEpiMaskBf16 || q.epilogue == kEpiAllReduceF32))
         return "a bias applies to the f32, bf16 and ReLU epilogues only";
     if (q.colSums && q.epilogue != kEpiMaskBf16) return "column sums are produced by the mask epilogue only";
@@ -952,6 +1006,10 @@ cudaError_t run(const Problem& q, int smCount, uint32_t* status, cudaStream_t st
     p.target = q.reduce.target;
     p.bias = q.bias;
     p.colSums = q.colSums;
+    p.velocity = q.update.momentum > 0.0f ? q.update.velocity : nullptr;
+    p.copy = static_cast<__nv_bfloat16*>(q.update.copy);
+    p.lr = q.update.lr;
+    p.mu = q.update.momentum;
     if (q.aMajorMN) {
         if (q.bMajorMN) return launchEpi<true, true>(q.epilogue, pair, a, b, p, stream);
         return launchEpi<true, false>(q.epilogue, pair, a, b, p, stream);

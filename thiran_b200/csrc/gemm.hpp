@@ -14,6 +14,21 @@ enum : int {
     kEpiReluBf16 = 2,  // C (bf16) = max(acc, 0)            (forward ReLU)
     kEpiMaskBf16 = 3,  // C (bf16) = aux > 0 ? acc : 0       (ReLU backward mask, aux bf16 [M][N])
     kEpiAllReduceF32 = 4,  // C (f32) = sum over ranks of acc, on every rank (see AllReduce)
+    kEpiSgdF32 = 5,        // C (f32 parameters) updated in place with gradient acc (see Update)
+};
+
+// The optimizer step fused into the read-out of a weight-gradient GEMM
+// (kEpiSgdF32): C holds the f32 parameters, g = acc, and per element
+// d = g (or d = v*mu + g, v = d when `velocity` is given), C = C - d*lr, each
+// operation rounded to f32 as the standalone SGD pass does
+// (src/training/v0/Training.cpp:366-372); `copy` (bf16, optional) receives
+// the updated parameters. The gradient itself is never stored. velocity and
+// copy share C's leading dimension.
+struct Update {
+    float* velocity = nullptr;
+    void* copy = nullptr;
+    float lr = 0.0f;
+    float momentum = 0.0f;
 };
 
 // Cross-GPU all-reduce fused into the epilogue (kEpiAllReduceF32). Every rank
@@ -62,6 +77,7 @@ struct Problem {
     // colSums[(mTile * 4 + q) * N + j] = sum over rows 32q..32q+31 of the
     // M tile of C[row][j], rows past M counting 0. Fixed summation order.
     float* colSums = nullptr;
+    Update update;              // kEpiSgdF32
 };
 
 // Rows of partial sums `colSums` receives for an M x N problem.

@@ -24,6 +24,7 @@
 
 #include "gemm.hpp"
 #include "mlp.hpp"
+#include "sgd.cuh"
 
 namespace thb::mlp {
 namespace {
@@ -114,15 +115,8 @@ __global__ void __launch_bounds__(kThreads) sumPartialsKernel(const double* __re
     }
 }
 
-// One parameter update (Training.cpp:366-372): d = g, or with momentum
-// d = v*mu + g and v = d; p = p - d*lr. Each operation rounds to f32.
 __device__ __forceinline__ float updateOne(float p, float g, float* v, float lr, float mu) {
-    float d = g;
-    if (v) {
-        d = __fadd_rn(__fmul_rn(*v, mu), g);
-        *v = d;
-    }
-    return __fsub_rn(p, __fmul_rn(d, lr));
+    return sgdStep(p, g, v, lr, mu);
 }
 
 // p = update(p, g, v); pb = bf16(p) when pb is given. Vectorised by 4.
@@ -220,9 +214,30 @@ cudaError_t sgdUpdate(float* p, const float* g, float* v, void* pb, std::uint64_
 }
 
 cudaError_t forwardBackward(const Buffers& b, const float* x, const float* t, int smCount, std::uint32_t* status,
-                            cudaStream_t s, GemmTimer* timer) {
+                            cudaStream_t s, GemmTimer* timer, const float* fusedLr) {
     GemmTimer none;
     GemmTimer& tm = timer ? *timer : none;
+    if (fusedLr && (b.dw1Reduce.cPeers[0] || b.dw2Reduce.cPeers[0])) return cudaErrorInvalidValue;
+    // Weight-gradient GEMM epilogue: store dW, all-reduce it, or apply the
+    // optimizer step to the parameters in place.
+    const bool momentum = b.momentum > 0.0f;
+    auto weightGradient = [&](gemm::Problem& q, float* dw, float* w, float* vw, void* wb, const gemm::AllReduce& r) {
+        if (fusedLr) {
+            q.c = w;
+            q.epilogue = gemm::kEpiSgdF32;
+            q.update.velocity = momentum ? vw : nullptr;
+            q.update.copy = wb;
+            q.update.lr = *fusedLr;
+            q.update.momentum = b.momentum;
+        } else if (r.cPeers[0]) {
+            q.c = dw;
+            q.epilogue = gemm::kEpiAllReduceF32;
+            q.reduce = r;
+        } else {
+            q.c = dw;
+            q.epilogue = gemm::kEpiF32;
+        }
+    };
     auto runGemm = [&](const gemm::Problem& q) {
         tm.begin(s);
         const cudaError_t r = gemm::run(q, smCount, status, s);
@@ -268,26 +283,32 @@ cudaError_t forwardBackward(const Buffers& b, const float* x, const float* t, in
     q.m = b.hidden; q.n = b.out; q.k = b.batch;
     q.a = b.h; q.aMajorMN = true; q.lda = b.hidden;
     q.b = b.dy; q.bMajorMN = true; q.ldb = b.out;
-    q.c = b.dw2; q.ldc = b.out; q.epilogue = gemm::kEpiF32;
-    if (b.dw2Reduce.cPeers[0]) { q.epilogue = gemm::kEpiAllReduceF32; q.reduce = b.dw2Reduce; }
+    q.ldc = b.out;
+    // (W2's bf16 copy may be rewritten here: the dH GEMM above has read it.)
+    weightGradient(q, b.dw2, b.w2, b.vw2, b.w2b, b.dw2Reduce);
     if ((e = runGemm(q)) != cudaSuccess) return e;
     // dW1 = Xb^T dH: A = Xb stored [B][in] (MN-major), B = dH stored [B][hidden] (MN-major).
     q = {};
     q.m = b.in; q.n = b.hidden; q.k = b.batch;
     q.a = b.xb; q.aMajorMN = true; q.lda = b.in;
     q.b = b.dh; q.bMajorMN = true; q.ldb = b.hidden;
-    q.c = b.dw1; q.ldc = b.hidden; q.epilogue = gemm::kEpiF32;
-    if (b.dw1Reduce.cPeers[0]) { q.epilogue = gemm::kEpiAllReduceF32; q.reduce = b.dw1Reduce; }
+    q.ldc = b.hidden;
+    weightGradient(q, b.dw1, b.w1, b.vw1, b.w1b, b.dw1Reduce);
     return runGemm(q);
 }
 
-cudaError_t applySgd(const Buffers& b, float lr, int smCount, cudaStream_t s) {
+cudaError_t applySgd(const Buffers& b, float lr, int smCount, cudaStream_t s, bool weights) {
     const float mu = b.momentum;
     const bool m = mu > 0.0f;
-    cudaError_t e = sgdUpdate(b.w1, b.dw1, m ? b.vw1 : nullptr, b.w1b, b.in * b.hidden, lr, mu, smCount, s);
-    if (e != cudaSuccess) return e;
-    if ((e = sgdUpdate(b.w2, b.dw2, m ? b.vw2 : nullptr, b.w2b, b.hidden * b.out, lr, mu, smCount, s)) != cudaSuccess)
-        return e;
+    cudaError_t e = cudaSuccess;
+    if (weights) {
+        if ((e = sgdUpdate(b.w1, b.dw1, m ? b.vw1 : nullptr, b.w1b, b.in * b.hidden, lr, mu, smCount, s)) !=
+            cudaSuccess)
+            return e;
+        if ((e = sgdUpdate(b.w2, b.dw2, m ? b.vw2 : nullptr, b.w2b, b.hidden * b.out, lr, mu, smCount, s)) !=
+            cudaSuccess)
+            return e;
+    }
     if (!b.b1) return cudaSuccess;
     if ((e = sgdUpdate(b.b1, b.db1, m ? b.vb1 : nullptr, nullptr, b.hidden, lr, mu, smCount, s)) != cudaSuccess) return e;
     return sgdUpdate(b.b2, b.db2, m ? b.vb2 : nullptr, nullptr, b.out, lr, mu, smCount, s);

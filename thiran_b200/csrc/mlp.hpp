@@ -73,10 +73,15 @@ cudaError_t castToBf16(const float* x, void* y, std::uint64_t n, int smCount, cu
 // the bf16 copy pb when given.
 cudaError_t sgdUpdate(float* p, const float* g, float* v, void* pb, std::uint64_t n, float lr, float momentum,
                       int smCount, cudaStream_t s);
-// Forward, loss and backward: fills h, y, dy, dh, dw1, dw2 and lossSum.
+// Forward, loss and backward: fills h, y, dy, dh, dw1, dw2, the bias
+// gradients and lossSum. With `fusedLr` (single device, no all-reduce bound)
+// the weight updates run in the dW GEMM epilogues instead (kEpiSgdF32): W1,
+// W2, their velocities and bf16 copies are updated and dw1, dw2 are not
+// written; applySgd(..., weights = false) then updates the biases.
 cudaError_t forwardBackward(const Buffers&, const float* x, const float* t, int smCount, std::uint32_t* status,
-                            cudaStream_t s, GemmTimer* timer = nullptr);
-// W -= lr * dW for both layers, refreshing the bf16 copies.
-cudaError_t applySgd(const Buffers&, float lr, int smCount, cudaStream_t s);
+                            cudaStream_t s, GemmTimer* timer = nullptr, const float* fusedLr = nullptr);
+// p -= lr * g for every parameter (the weights only when `weights`),
+// refreshing the bf16 copies.
+cudaError_t applySgd(const Buffers&, float lr, int smCount, cudaStream_t s, bool weights = true);
 
 } // namespace thb::mlp
