@@ -30,7 +30,20 @@ struct GroupKernel {
     std::string vectorName, scalarName;
     void* vectorKernel = nullptr;   // cudaKernel_t
     void* scalarKernel = nullptr;
+    unsigned vectorResident = 4;    // resident CTAs per SM at kBlock threads
+    unsigned scalarResident = 4;
+    // Bulk-copy pipelined entry (groups with tensor inputs; null when the
+    // module lacks it): extra arguments (stages, tile elements), dynamic
+    // shared memory (stages * arity + 2) * tile * element size.
+    std::string bulkName;
+    void* bulkKernel = nullptr;
+    std::uint32_t bulkSmemAllowed = 0;  // dynamic shared memory the entry is configured for
+    std::uint32_t bulkResident = 1;     // resident CTAs per SM at bulkResidentSmem
+    std::uint32_t bulkResidentSmem = 0;
 };
+
+// Most ring stages of the bulk entry.
+constexpr unsigned kBulkMaxStages = 8;
 
 struct Module;  // compiled NVRTC library (opaque)
 

@@ -54,31 +54,45 @@ __device__ __forceinline__ T warpSum(T v) {
 }
 
 // D = Y - T; G = D * scale; dY = bf16(G). Block (x, y) covers columns
-// 256x .. 256x+255 of the rows of chunk y (one column per thread, so a warp
-// reads 128 contiguous bytes per row): partial[block] = sum D^2 (f64) and,
-// when colSums is given, colSums[y][col] = sum over the chunk's rows of G
-// (f32, row order).
+// 1024x .. 1024x+1023 of the rows of chunk y, four adjacent columns per
+// thread (16-byte loads; a warp reads 512 contiguous bytes of Y and of T per
+// row; cols is a multiple of 4 and rows are 16-byte aligned):
+// partial[block] = sum D^2 (f64) and, when colSums is given,
+// colSums[y][col] = sum over the chunk's rows of G (f32, row order).
 __global__ void __launch_bounds__(kThreads) lossGradKernel(const float* __restrict__ y, const float* __restrict__ t,
                                                            __nv_bfloat16* __restrict__ dy, double* __restrict__ partials,
                                                            float* __restrict__ colSums, std::uint64_t rows,
                                                            std::uint64_t cols, std::uint64_t rowsPerChunk, float scale) {
     __shared__ double red[kThreads / 32];
     double acc = 0.0;
-    float colAcc = 0.0f;
-    const std::uint64_t col = static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
+    const std::uint64_t col = (static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x) * 4;
     const std::uint64_t r0 = static_cast<std::uint64_t>(blockIdx.y) * rowsPerChunk;
     const std::uint64_t r1 = r0 + rowsPerChunk < rows ? r0 + rowsPerChunk : rows;
     if (col < cols) {
+        float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll 4
         for (std::uint64_t r = r0; r < r1; ++r) {
             const std::uint64_t i = r * cols + col;
-            const float d = __fsub_rn(__ldcs(y + i), __ldcs(t + i));
-            acc += static_cast<double>(d) * static_cast<double>(d);
-            const float g = __fmul_rn(d, scale);
-            dy[i] = __float2bfloat16_rn(g);
-            colAcc = __fadd_rn(colAcc, g);
+            const float4 yv = __ldcs(reinterpret_cast<const float4*>(y + i));
+            const float4 tv = __ldcs(reinterpret_cast<const float4*>(t + i));
+            const float d[4] = {__fsub_rn(yv.x, tv.x), __fsub_rn(yv.y, tv.y), __fsub_rn(yv.z, tv.z),
+                                __fsub_rn(yv.w, tv.w)};
+            float g[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                acc += static_cast<double>(d[j]) * static_cast<double>(d[j]);
+                g[j] = __fmul_rn(d[j], scale);
+                c[j] = __fadd_rn(c[j], g[j]);
+            }
+            const __nv_bfloat162 lo = __floats2bfloat162_rn(g[0], g[1]), hi = __floats2bfloat162_rn(g[2], g[3]);
+            uint2 packed;
+            packed.x = *reinterpret_cast<const std::uint32_t*>(&lo);
+            packed.y = *reinterpret_cast<const std::uint32_t*>(&hi);
+            __stcs(reinterpret_cast<uint2*>(dy + i), packed);
         }
-        if (colSums) colSums[static_cast<std::uint64_t>(blockIdx.y) * cols + col] = colAcc;
+        if (colSums)
+            *reinterpret_cast<float4*>(colSums + static_cast<std::uint64_t>(blockIdx.y) * cols + col) =
+                make_float4(c[0], c[1], c[2], c[3]);
     }
     acc = warpSum(acc);
     if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = acc;
@@ -165,15 +179,18 @@ unsigned gridFor(std::uint64_t work, int smCount) {
 
 } // namespace
 
+// Columns per loss block (four per thread).
+constexpr std::uint64_t kLossCols = kThreads * 4;
+
 unsigned lossRowChunks(std::uint64_t rows, std::uint64_t cols, int smCount) {
-    const std::uint64_t colBlocks = (cols + kThreads - 1) / kThreads;
-    std::uint64_t chunks = (static_cast<std::uint64_t>(smCount) * 4 + colBlocks - 1) / colBlocks;
+    const std::uint64_t colBlocks = (cols + kLossCols - 1) / kLossCols;
+    std::uint64_t chunks = (static_cast<std::uint64_t>(smCount) * 8 + colBlocks - 1) / colBlocks;
     if (chunks > rows) chunks = rows;
     return static_cast<unsigned>(chunks < 1 ? 1 : chunks);
 }
 
 unsigned lossPartialCount(std::uint64_t rows, std::uint64_t cols, int smCount) {
-    return static_cast<unsigned>((cols + kThreads - 1) / kThreads) * lossRowChunks(rows, cols, smCount);
+    return static_cast<unsigned>((cols + kLossCols - 1) / kLossCols) * lossRowChunks(rows, cols, smCount);
 }
 
 cudaError_t castToBf16(const float* x, void* y, std::uint64_t n, int smCount, cudaStream_t s) {
@@ -187,7 +204,7 @@ cudaError_t lossAndGradient(const float* y, const float* t, void* dy, double* pa
                             float* colSums, float* db, std::uint64_t rows, std::uint64_t cols, float scale, int smCount,
                             cudaStream_t s) {
     const unsigned chunks = lossRowChunks(rows, cols, smCount);
-    const unsigned colBlocks = static_cast<unsigned>((cols + kThreads - 1) / kThreads);
+    const unsigned colBlocks = static_cast<unsigned>((cols + kLossCols - 1) / kLossCols);
     const std::uint64_t rowsPerChunk = (rows + chunks - 1) / chunks;
     lossGradKernel<<<dim3(colBlocks, chunks), kThreads, 0, s>>>(y, t, static_cast<__nv_bfloat16*>(dy), partials,
                                                                 db ? colSums : nullptr, rows, cols, rowsPerChunk, scale);

@@ -2,7 +2,10 @@
 #include "runtime.hpp"
 
 #include <algorithm>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
+#include <utility>
 
 #include "gemm.hpp"
 #include "kernels.hpp"
@@ -21,6 +24,42 @@ std::map<int, DeviceInfo> deviceInfos;
 
 std::mutex unobservedMutex;
 std::vector<std::string> unobservedErrors;
+
+struct BulkShape {
+    std::uint32_t stages = 0;
+    std::uint32_t tileBytes = 0;
+};
+
+// Ring geometry of a group's bulk-copy entry for `arity` tensor inputs: two
+// stages of 32 KiB tiles per input while (2 * arity + 2) tiles fit in
+// 200 KiB of shared memory, smaller tiles (multiples of 4 KiB) past that.
+// On B200 two stages of 32 KiB ran the 8192^2 i64 region at ~238 us per
+// launch whatever the placement of its three arrays, where the 128-bit
+// vector kernel took ~270-290 us; 16 KiB tiles (2-4 stages) took ~325 us and
+// 8 KiB tiles ~515 us (the per-tile barriers dominate).
+// THB_BULK=off keeps the vector kernel; THB_BULK=<stages>,<KiB> sets the
+// shape.
+bool bulkShape(std::size_t arity, BulkShape& s) {
+    static const std::pair<int, int> choice = [] {
+        const char* e = std::getenv("THB_BULK");
+        if (!e || !*e) return std::pair<int, int>{0, 0};
+        int stages = 0, kib = 0;
+        if (std::sscanf(e, "%d,%d", &stages, &kib) == 2 && stages > 0 && kib > 0) return std::pair<int, int>{stages, kib};
+        return std::pair<int, int>{-1, 0};
+    }();
+    if (choice.first < 0 || arity == 0) return false;
+    if (choice.first > 0) {
+        s.stages = static_cast<std::uint32_t>(choice.first);
+        s.tileBytes = static_cast<std::uint32_t>(choice.second) * 1024u;
+    } else {
+        constexpr std::uint64_t kBudget = 200u * 1024u, kTile = 32768, kStep = 4096;
+        s.stages = 2;
+        const std::uint64_t tiles = 2 * arity + 2;
+        s.tileBytes = static_cast<std::uint32_t>(std::min<std::uint64_t>(kTile, kBudget / tiles / kStep * kStep));
+        if (s.tileBytes < kStep) return false;
+    }
+    return s.stages >= 1 && s.stages <= kBulkMaxStages && s.tileBytes >= 256 && s.tileBytes % 16 == 0;
+}
 
 } // namespace
 
@@ -92,6 +131,7 @@ const DeviceInfo& useDevice(int ordinal) {
         info.smCount = prop.multiProcessorCount;
         info.major = prop.major;
         info.minor = prop.minor;
+        info.maxSmemOptin = static_cast<int>(prop.sharedMemPerBlockOptin);
         found = deviceInfos.emplace(ordinal, info).first;
     }
     return found->second;
@@ -265,8 +305,8 @@ void* CompiledRegion::slotPointer(std::uint32_t value, std::size_t bytes, thb_ev
 void CompiledRegion::launchElementwise(const FusionGroup& group, const std::vector<const Value*>& operands,
                                        const std::vector<const Value*>& scalars, Value& out, cudaStream_t stream,
                                        thb_evidence& ev) {
-    const GroupKernel* kernel = nullptr;
-    for (const auto& k : kernels_)
+    GroupKernel* kernel = nullptr;
+    for (auto& k : kernels_)
         if (k.group == group.id) kernel = &k;
     if (!kernel) fail(Category::Unsupported, "GPU-INVALID-PLAN", "fusion group has no generated kernel");
     const std::uint64_t n = out.count();
@@ -276,9 +316,11 @@ void CompiledRegion::launchElementwise(const FusionGroup& group, const std::vect
     const unsigned lanes = group.dtype == DType::F32 ? 4 : 2;
     const std::uint64_t work = aligned ? std::max<std::uint64_t>(1, n / lanes) : n;
     const std::uint64_t perBlock = static_cast<std::uint64_t>(kBlock) * (aligned ? kUnroll : 1);
-    // Eight CTAs per SM: about two resident waves of the streaming kernel,
-    // which measured faster than one occupancy-sized persistent wave.
-    const std::uint64_t cap = static_cast<std::uint64_t>(info_->smCount) * 8;
+    // One full resident wave (SMs x resident CTAs per SM) of the grid-stride
+    // kernel: measured 1-2 % faster than two waves on the 8192^2 i64 region
+    // (interleaved medians, 12 rounds of 20 back-to-back launches).
+    const std::uint64_t cap =
+        static_cast<std::uint64_t>(info_->smCount) * (aligned ? kernel->vectorResident : kernel->scalarResident);
     const unsigned blocks = static_cast<unsigned>(std::max<std::uint64_t>(1, std::min(cap, (work + perBlock - 1) / perBlock)));
     std::vector<void*> args;
     void* outPtr = out.data;
@@ -300,6 +342,44 @@ void CompiledRegion::launchElementwise(const FusionGroup& group, const std::vect
     }
     args.push_back(&count);
     args.push_back(&errorWord);
+    // Large aligned groups stream through the bulk-copy pipeline: at least
+    // one whole tile per SM, in one resident wave of persistent CTAs.
+    BulkShape shape;
+    const std::uint64_t elementBytes = group.dtype == DType::F32 ? 4 : 8;
+    if (aligned && kernel->bulkKernel && bulkShape(kernel->arity, shape)) {
+        std::uint32_t tile = static_cast<std::uint32_t>(shape.tileBytes / elementBytes);
+        std::uint32_t stages = shape.stages;
+        const std::uint64_t smem = (static_cast<std::uint64_t>(stages) * kernel->arity + 2) * shape.tileBytes;
+        const std::uint64_t tiles = n / tile;
+        if (tiles >= static_cast<std::uint64_t>(info_->smCount) && smem <= static_cast<std::uint64_t>(info_->maxSmemOptin)) {
+            if (kernel->bulkSmemAllowed < smem) {
+                check(cudaFuncSetAttribute(kernel->bulkKernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem)),
+                      "cudaFuncSetAttribute(bulk)");
+                kernel->bulkSmemAllowed = static_cast<std::uint32_t>(smem);
+            }
+            if (kernel->bulkResidentSmem != smem) {
+                int resident = 0;
+                if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kernel->bulkKernel, kBlock, smem) !=
+                        cudaSuccess ||
+                    resident < 1) {
+                    (void)cudaGetLastError();
+                    resident = 1;
+                }
+                kernel->bulkResident = static_cast<std::uint32_t>(resident);
+                kernel->bulkResidentSmem = static_cast<std::uint32_t>(smem);
+            }
+            const unsigned bulkBlocks = static_cast<unsigned>(
+                std::min<std::uint64_t>(tiles, static_cast<std::uint64_t>(info_->smCount) * kernel->bulkResident));
+            args.push_back(&stages);
+            args.push_back(&tile);
+            check(cudaLaunchKernel(kernel->bulkKernel, dim3(bulkBlocks), dim3(kBlock), args.data(), smem, stream),
+                  "cudaLaunchKernel(fusion-group, bulk)");
+            ++ev.kernel_launches;
+            ++ev.stream_submissions;
+            return;
+        }
+    }
     const void* fn = aligned ? kernel->vectorKernel : kernel->scalarKernel;
     check(cudaLaunchKernel(fn, dim3(blocks), dim3(kBlock), args.data(), 0, stream), "cudaLaunchKernel(fusion-group)");
     ++ev.kernel_launches;

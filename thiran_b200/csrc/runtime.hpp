@@ -52,6 +52,7 @@ struct DeviceInfo {
     int ordinal = 0;
     int smCount = 148;
     int major = 0, minor = 0;
+    int maxSmemOptin = 232448;  // dynamic shared memory a block may opt into
 };
 
 // Selects `ordinal` as the current device after validating it; throws
