@@ -693,7 +693,8 @@ def main():
             "config": workload.config(world),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": getattr(workload, "kernel", "generated fused elementwise group (NVRTC, sm_100a)"),
+                         "kernel": getattr(workload, "kernel", "generated fused elementwise group (NVRTC, sm_100a), "
+                                                               "bulk-copy entry: cp.async.bulk tile ring + mbarriers"),
                          "algorithmic_bytes_per_launch": bytes_per_step_rank,
                          "avg_launch_ms": launch_ms, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
             "cpu_baseline": cpu_baseline,
