@@ -43,7 +43,9 @@ def test_softmax_extreme_values(device):
     np.testing.assert_array_equal(out == 0, orc.softmax_rows(x) == 0)
 
 
-@pytest.mark.parametrize("rows,cols", [(1, 1), (17, 4096), (300, 333), (64, 8192)])
+@pytest.mark.parametrize("rows,cols", [(1, 1), (17, 4096), (300, 333), (64, 8192),
+                                       # warp-per-row kernel: partial last packet column, short rows
+                                       (257, 1028), (1000, 64), (5, 2048)])
 def test_row_max_and_sum(device, rows, cols):
     x = np.random.default_rng(cols).standard_normal((rows, cols)).astype(np.float32)
     b = thb.RegionBuilder("rm")
