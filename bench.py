@@ -119,7 +119,7 @@ class Softmax(Workload):
     dtype = "f32"
     rows, cols = 65536, 4096
     ncu_name = "softmax_65536x4096"
-    kernel = "rowStaged softmax (rows staged by cp.async.bulk, mbarrier pipeline)"
+    kernel = "rowWarp softmax (one warp per row, row in registers, warp-shuffle max and sum)"
 
     def build(self, torch, rank, world):
         from thiran_b200 import regions
