@@ -13,11 +13,30 @@ pytestmark = pytest.mark.gpu
 
 
 def test_cube_known_answer(device):
-    color, depth, stats = thb.render(*cube_scene(), 96, 96, device=device)
+    scene = cube_scene()
+    color, depth, stats = thb.render(*scene, 96, 96, device=device)
     assert stats.tolist() == [12, 12, 3150, 2218]
     assert orc.fnv_floats(color) == "fnv1a64:0d0c47343db9df53"
     assert orc.fnv_floats(depth) == "fnv1a64:4e244c6d47059a59"
-    assert thb.render.evidence["kernel_launches"] == 1
+    # The raw geometry crosses PCIe (positions, colours, indices); transform,
+    # clipping, setup and binning run as kernels before the raster kernel.
+    positions, indices, colors = scene[0], scene[1], scene[2]
+    ev = thb.render.evidence
+    assert ev["host_to_device_bytes"] == positions.size * 4 + colors.size * 4 + indices.size * 8
+    assert ev["kernel_launches"] > 1
+
+
+def test_transform_failure_on_the_device(device):
+    """A vertex whose transformed coordinate overflows f32 fails with the
+    reference's TH019-NONFINITE-TRANSFORMED (found by the transform kernel)."""
+    g = orc.gfx
+    positions = np.array([[3e38, 0, 0], [0, 1, 0], [1, 0, 0]], np.float32)
+    scale = np.diag(np.array([10, 10, 10, 1], np.float32)).astype(np.float32)
+    eye = g.identity()
+    with pytest.raises(thb.GpuError) as err:
+        thb.render(positions, np.array([[0, 1, 2]]), np.full((3, 4), 0.5, np.float32), scale, eye, eye, 8, 8,
+                   device=device)
+    assert err.value.code == "TH019-NONFINITE-TRANSFORMED"
 
 
 @pytest.mark.parametrize("scene", ["random", "ties", "ortho"])

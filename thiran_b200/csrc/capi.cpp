@@ -404,9 +404,21 @@ int thb_render(int device, const float* positions, uint64_t vertices, const int6
     const int status = guarded(failure, cap, [&] {
         namespace gfx = thb::graphics;
         const float zero[4] = {0, 0, 0, 0};
-        // Preparation first: invalid geometry fails before any driver call.
-        const gfx::Prepared p = gfx::prepare(positions, vertices, indices, triangles, colors, model, view, projection,
-                                             width, height, clear ? clear : zero);
+        // The transform, clipping, setup and binning run on the GPU unless
+        // THB_RENDER_PREP=host (the same pipeline on host threads).
+        static const bool hostPrep = [] {
+            const char* e = std::getenv("THB_RENDER_PREP");
+            return e && std::strcmp(e, "host") == 0;
+        }();
+        // Validation first: invalid geometry fails before any driver call.
+        gfx::Prepared p;
+        gfx::Scene scene;
+        if (hostPrep)
+            p = gfx::prepare(positions, vertices, indices, triangles, colors, model, view, projection, width, height,
+                             clear ? clear : zero);
+        else
+            scene = gfx::validate(positions, vertices, indices, triangles, colors, model, view, projection, width,
+                                  height, clear ? clear : zero);
         const std::uint64_t pixels = width * height;
         if (pixels && (!color || !depth)) fail(Category::Validation, "TH019-FRAMEBUFFER-TENSOR", "null output buffer");
         useDevice(device);
@@ -426,9 +438,28 @@ int thb_render(int device, const float* positions, uint64_t vertices, const int6
             ++ev.host_to_device_copies;
             ev.host_to_device_bytes += bytes;
         };
-        upload(tri, p.triangles.data(), p.triangles.size() * sizeof(gfx::RasterTriangle));
-        upload(offsets, p.tileOffsets.data(), p.tileOffsets.size() * sizeof(std::uint32_t));
-        upload(lists, p.tileLists.data(), p.tileLists.size() * sizeof(std::uint32_t));
+        std::uint64_t postClip = 0;
+        if (hostPrep) {
+            upload(tri, p.triangles.data(), p.triangles.size() * sizeof(gfx::RasterTriangle));
+            upload(offsets, p.tileOffsets.data(), p.tileOffsets.size() * sizeof(std::uint32_t));
+            upload(lists, p.tileLists.data(), p.tileLists.size() * sizeof(std::uint32_t));
+            postClip = p.postClipTriangles;
+        } else {
+            DeviceBuffer devPositions, devColors, devIndices;
+            upload(devPositions, positions, vertices * 3 * sizeof(float));
+            upload(devColors, colors, vertices * 4 * sizeof(float));
+            upload(devIndices, indices, triangles * 3 * sizeof(std::int64_t));
+            const gfx::DevicePrepared d = gfx::prepareOnDevice(
+                scene, static_cast<const float*>(devPositions.ptr), static_cast<const float*>(devColors.ptr),
+                static_cast<const std::int64_t*>(devIndices.ptr), device, stream, tri, offsets, lists);
+            if (d.failure) fail(Category::Semantic, d.failure, d.failure);
+            ev.kernel_launches += d.launches;
+            ev.synchronizations += 3;
+            postClip = d.postClipTriangles;
+            p.tilesX = scene.tilesX;
+            p.tilesY = scene.tilesY;
+            std::memcpy(p.clear, scene.clear, sizeof p.clear);
+        }
         counters.reserve(2 * sizeof(unsigned long long), device);
         cudaCheck(cudaMemsetAsync(counters.ptr, 0, 2 * sizeof(unsigned long long), stream), "cudaMemsetAsync");
         if (pixels) {
@@ -454,8 +485,8 @@ int thb_render(int device, const float* positions, uint64_t vertices, const int6
         cudaCheck(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
         ++ev.synchronizations;
         if (stats) {
-            stats[0] = p.inputTriangles;
-            stats[1] = p.postClipTriangles;
+            stats[0] = triangles;
+            stats[1] = postClip;
             stats[2] = counts[0];
             stats[3] = counts[1];
         }

@@ -183,18 +183,32 @@ void multiply(const float* a, const float* b, float* out) {
 
 } // namespace
 
-Prepared prepare(const float* positions, std::uint64_t vertices, const std::int64_t* indices, std::uint64_t triangles,
-                 const float* colors, const float* model, const float* view, const float* projection,
-                 std::uint64_t width, std::uint64_t height, const float* clear) {
+Scene validate(const float* positions, std::uint64_t vertices, const std::int64_t* indices, std::uint64_t triangles,
+               const float* colors, const float* model, const float* view, const float* projection,
+               std::uint64_t width, std::uint64_t height, const float* clear) {
     // validateGeometry (Graphics.cpp:322-342), validateFramebuffer (:210-226).
+    // Each check scans its whole array on host threads; the checks keep the
+    // reference's order, so the first failing check gives the id.
     if ((vertices && (!positions || !colors)) || (triangles && !indices) || !model || !view || !projection || !clear)
         fail(Category::Validation, "TH019-GEOMETRY-SHAPE", "null geometry, matrix or clear colour");
-    for (std::uint64_t k = 0; k < vertices * 3; ++k)
-        if (!finite(positions[k])) bad("TH019-NONFINITE-VERTEX");
-    for (std::uint64_t k = 0; k < vertices * 4; ++k)
-        if (!finite(colors[k]) || colors[k] < 0.0f || colors[k] > 1.0f) bad("TH019-COLOR-RANGE");
-    for (std::uint64_t k = 0; k < triangles * 3; ++k)
-        if (indices[k] < 0 || static_cast<std::uint64_t>(indices[k]) >= vertices) bad("TH019-INDEX");
+    auto anyOf = [](std::uint64_t n, auto&& failing) {
+        const unsigned threads = workerCount(n);
+        std::vector<char> found(std::max(1u, threads), 0);
+        parallelChunks(n, threads, [&](unsigned w, std::uint64_t begin, std::uint64_t end) {
+            for (std::uint64_t k = begin; k < end; ++k)
+                if (failing(k)) {
+                    found[w] = 1;
+                    return;
+                }
+        });
+        return std::find(found.begin(), found.end(), 1) != found.end();
+    };
+    if (anyOf(vertices * 3, [&](std::uint64_t k) { return !finite(positions[k]); })) bad("TH019-NONFINITE-VERTEX");
+    if (anyOf(vertices * 4, [&](std::uint64_t k) { return !finite(colors[k]) || colors[k] < 0.0f || colors[k] > 1.0f; }))
+        bad("TH019-COLOR-RANGE");
+    if (anyOf(triangles * 3,
+              [&](std::uint64_t k) { return indices[k] < 0 || static_cast<std::uint64_t>(indices[k]) >= vertices; }))
+        bad("TH019-INDEX");
     for (int k = 0; k < 4; ++k)
         if (!finite(clear[k]) || clear[k] < 0.0f || clear[k] > 1.0f) bad("TH019-CLEAR-COLOR");
     const auto limit = static_cast<std::uint64_t>(std::numeric_limits<std::int32_t>::max());
@@ -204,16 +218,35 @@ Prepared prepare(const float* positions, std::uint64_t vertices, const std::int6
     for (int k = 0; k < 16; ++k)
         if (!finite(model[k]) || !finite(view[k]) || !finite(projection[k])) bad("TH019-NONFINITE-MATRIX");
 
+    Scene scene;
+    scene.width = width;
+    scene.height = height;
+    scene.vertices = vertices;
+    scene.triangles = triangles;
+    std::memcpy(scene.clear, clear, sizeof scene.clear);
+    float mv[16];
+    multiply(view, model, mv);
+    multiply(projection, mv, scene.mvp);
+    for (int k = 0; k < 16; ++k)
+        if (!finite(mv[k]) || !finite(scene.mvp[k])) bad("TH019-NONFINITE-MATRIX");
+    // (Tile counts of 2^32 and more fail with TH019-FRAMEBUFFER-SIZE after
+    // clipping, where the triangle count is checked too.)
+    scene.tilesX = static_cast<std::uint32_t>(std::min<std::uint64_t>((width + kTile - 1) / kTile, ~0u));
+    scene.tilesY = static_cast<std::uint32_t>(std::min<std::uint64_t>((height + kTile - 1) / kTile, ~0u));
+    return scene;
+}
+
+Prepared prepare(const float* positions, std::uint64_t vertices, const std::int64_t* indices, std::uint64_t triangles,
+                 const float* colors, const float* model, const float* view, const float* projection,
+                 std::uint64_t width, std::uint64_t height, const float* clear) {
+    const Scene scene = validate(positions, vertices, indices, triangles, colors, model, view, projection, width,
+                                 height, clear);
     Prepared out;
     out.width = width;
     out.height = height;
-    std::memcpy(out.clear, clear, sizeof out.clear);
+    std::memcpy(out.clear, scene.clear, sizeof out.clear);
     out.inputTriangles = triangles;
-    float mv[16], mvp[16];
-    multiply(view, model, mv);
-    multiply(projection, mv, mvp);
-    for (int k = 0; k < 16; ++k)
-        if (!finite(mv[k]) || !finite(mvp[k])) bad("TH019-NONFINITE-MATRIX");
+    const float* mvp = scene.mvp;
     // Transform, clip and bin in contiguous chunks on host threads; chunk
     // results are joined in order, so the output equals a serial pass. The
     // first failure of any chunk is the reference's failure too: every
@@ -285,8 +318,8 @@ Prepared prepare(const float* positions, std::uint64_t vertices, const std::int6
 
     // Tiles of 16x16 pixels; each list keeps submission order: per-chunk
     // counts, offsets = tile-major then chunk-major prefix sums, parallel fill.
-    out.tilesX = static_cast<std::uint32_t>((width + kTile - 1) / kTile);
-    out.tilesY = static_cast<std::uint32_t>((height + kTile - 1) / kTile);
+    out.tilesX = scene.tilesX;
+    out.tilesY = scene.tilesY;
     const std::uint64_t tiles = static_cast<std::uint64_t>(out.tilesX) * out.tilesY;
     if (tiles >= std::numeric_limits<std::uint32_t>::max()) bad("TH019-FRAMEBUFFER-SIZE");
     const std::uint64_t count = out.triangles.size();

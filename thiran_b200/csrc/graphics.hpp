@@ -1,12 +1,14 @@
 // GPU renderer of the reference's software rasterizer
 // (src/graphics/v0/Graphics.cpp, GPU backend src/graphics/v0/GraphicsGpu.cpp).
 //
-// Split as in the reference: validation, the f32 vertex transform and
-// homogeneous clipping run on the host (its prepareRender, shared by its CPU
-// and GPU backends, Graphics.cpp:374-421), so the post-clip triangles are the
-// same bits as on the CPU. The rasterizer runs on the GPU: screen triangles
-// are binned into 16x16-pixel tiles in submission order, and one thread per
-// pixel walks its tile's list in that order with the reference's f64
+// Validation runs on the host before any driver call, as the reference's
+// prepareRender does (Graphics.cpp:374-421). The f32 vertex transform,
+// homogeneous clipping, screen setup and binning of screen triangles into
+// 16x16-pixel tiles (submission order within each tile) run on the GPU
+// (prep.cu) with every operation rounded on its own, so the post-clip
+// triangles are the same bits as the reference's CPU path; prepare() is the
+// same pipeline on host threads. The rasterizer runs on the GPU: one thread
+// per pixel walks its tile's list in order with the reference's f64
 // edge / barycentric / perspective-correct arithmetic and strict-less depth
 // test, so colour, depth and both pixel counters equal the sequential CPU
 // result. (The reference's GPU kernel walks every triangle for every pixel.)
@@ -17,6 +19,10 @@
 #include <cstdint>
 #include <string>
 #include <vector>
+
+namespace thb {
+struct DeviceBuffer;
+}
 
 namespace thb::graphics {
 
@@ -48,6 +54,36 @@ struct Prepared {
 Prepared prepare(const float* positions, std::uint64_t vertices, const std::int64_t* indices,
                  std::uint64_t triangles, const float* colors, const float* model, const float* view,
                  const float* projection, std::uint64_t width, std::uint64_t height, const float* clear);
+
+// The checks of prepare() that precede the transform (the reference's
+// validateGeometry / validateFramebuffer and the matrix checks, same ids in
+// the same order) and the model-view-projection product P * (V * M).
+struct Scene {
+    std::uint64_t width = 0, height = 0, vertices = 0, triangles = 0;
+    float clear[4] = {0, 0, 0, 0};
+    float mvp[16] = {};
+    std::uint32_t tilesX = 0, tilesY = 0;
+};
+Scene validate(const float* positions, std::uint64_t vertices, const std::int64_t* indices, std::uint64_t triangles,
+               const float* colors, const float* model, const float* view, const float* projection,
+               std::uint64_t width, std::uint64_t height, const float* clear);
+
+// Transform, clipping, screen setup and binning of a validated scene on the
+// GPU (prep.cu): the same triangles, tile offsets and lists as prepare(),
+// bit for bit. positions [vertices][3], colors [vertices][4] and indices
+// [triangles][3] are device memory. The three outputs are device buffers
+// the raster kernel reads. Synchronises `stream` twice (to size the
+// triangle array and the tile lists).
+struct DevicePrepared {
+    std::uint64_t postClipTriangles = 0;
+    std::uint64_t count = 0;  // screen triangles after setup
+    const char* failure = nullptr;  // TH019 id found on the device, or null
+    std::uint64_t launches = 0;     // kernels launched
+};
+DevicePrepared prepareOnDevice(const Scene& scene, const float* positions, const float* colors,
+                               const std::int64_t* indices, int device, cudaStream_t stream,
+                               thb::DeviceBuffer& triangles, thb::DeviceBuffer& tileOffsets,
+                               thb::DeviceBuffer& tileLists);
 
 // Rasterizes on `stream`: color [pixels][4], depth [pixels] (device), stats
 // (device, 2 x u64: shaded pixels, depth passes; accumulated into).
