@@ -185,7 +185,12 @@ bool pinnedHost(const void* p) {
 bool executePipelined(CompiledRegion& r, const std::vector<Value>& host, void* output, std::uint64_t outputCount,
                       cudaStream_t stream, thb_evidence& ev, std::uint32_t* stagedErrors) {
     constexpr std::size_t kMinBytes = 64ull << 20;
-    constexpr std::size_t kChunkBytes = 48ull << 20;
+    // Bytes (inputs + output) per chunk; THB_CHUNK_MB overrides 48 MiB.
+    static const std::size_t kChunkBytes = [] {
+        const char* e = std::getenv("THB_CHUNK_MB");
+        const long mb = e ? std::atol(e) : 0;
+        return static_cast<std::size_t>(mb > 0 ? mb : 48) << 20;
+    }();
     if (!r.rowLocal() || host.empty() || !output) return false;
     const Node& outNode = r.region().at(r.region().output);
     const std::uint64_t rows = host[0].shape[0];
