@@ -209,7 +209,7 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
         from thiran_b200.distributed import FusedGradientAllReduce
         mode = {"fused": None, "fused-peer": "peer", "fused-switch": "switch"}[args.dp_collective]
         with torch.cuda.stream(stream):
-            fused = FusedGradientAllReduce(session, dist, mode=mode)
+            fused = FusedGradientAllReduce(session, dist, mode=mode, update=args.dp_update == "fused")
         if not fused.available:
             fused = None
     from thiran_b200.distributed import bind_bias_gradients
@@ -219,6 +219,8 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
         collective = ("dW all-reduce fused into the dW GEMMs: per-tile announce, owner rank sums "
                       + ("with NVLink peer loads and stores" if fused.mode == "peer"
                          else "in NVSwitch (multimem.ld_reduce + multimem.st)")
+                      + ("; optimizer step applied by each tile's owner in the reduction, new W and bf16 W "
+                         "written to every rank" if fused.update else "; separate optimizer pass")
                       + "; bias gradients (80 KiB) by NCCL all-reduce")
     elif world > 1:
         collective = "NCCL all-reduce of dW1, dW2 and the bias gradients"
@@ -227,7 +229,10 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
         if world == 1:  # thb_mlp_step: the weight updates run in the dW GEMMs' read-out
             session.step(xx, tt, lr, s)
             return
-        session.forward_backward(xx, tt, s)
+        if fused and fused.update:
+            session.forward_backward_update(xx, tt, lr, s)
+        else:
+            session.forward_backward(xx, tt, s)
         if fused:
             with torch.cuda.stream(stream):
                 fused.after_backward()
@@ -343,7 +348,10 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
             "data": "synthetic (torch.Generator on device, seeded)",
             "config": dict(workload.config(world), **({"gradient_reduction": collective} if collective else {}),
                            optimizer=("SGD applied in the dW GEMMs' read-out (thb_mlp_step), biases by a separate "
-                                      "pass" if world == 1 else "SGD pass after the gradient all-reduce")),
+                                      "pass" if world == 1 else
+                                      "SGD applied by each tile's owner inside the fused all-reduce, biases by a "
+                                      "separate pass" if fused and fused.update else
+                                      "SGD pass after the gradient all-reduce")),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": None,
                          "kernel": "tcgen05 GEMM (256x256 tiles on CTA pairs, cta_group::2, TMEM accumulators; "
@@ -562,6 +570,9 @@ def main():
     p.add_argument("--dp-collective", default="fused", choices=["fused", "fused-peer", "fused-switch", "nccl"],
                    help="MLP data-parallel gradient reduction: fused into the dW GEMMs (peer loads/stores at "
                         "2 ranks, in-switch from 3; or forced), or NCCL all-reduce after the backward pass")
+    p.add_argument("--dp-update", default="pass", choices=["fused", "pass"],
+                   help="with a fused all-reduce: run the separate update pass on every rank (default; measured "
+                        "faster at 2 ranks), or apply the optimizer step in the reduction (each tile's owner)")
     p.add_argument("--shrink", type=int, default=1,
                    help="divide the leading extent (small cases for profiler captures; not a bench line)")
     args = p.parse_args()

@@ -543,6 +543,31 @@ int thb_mlp_bind_reduction(thb_mlp* session, uint32_t which, void* const* peers,
 /* Signal words thb_mlp_bind_reduction needs for `which` (0 for an unknown
  * buffer or session). */
 uint64_t thb_mlp_reduction_flag_words(thb_mlp* session, uint32_t which);
+/* Lets the all-reduce of layer `which` (THB_MLP_W1 or THB_MLP_W2; bind its
+ * reduction first) apply the optimizer step (applyOptimizer,
+ * src/training/v0/Training.cpp:343-381):
+ * - `param_peers[k]` is rank k's f32 parameter buffer as mapped on this GPU;
+ * - `copy_peers[k]` is rank k's bf16 copy of it (16-byte aligned);
+ * - param_peers[rank] and copy_peers[rank] become the session's buffers.
+ *   Copy the weights in afterwards with thb_mlp_set_weights.
+ * - With a multicast reduction, `param_multicast` and `copy_multicast` are
+ *   their NVLS multicast addresses; otherwise both are NULL.
+ * - NULL `param_peers` removes the binding.
+ * Rebinding the reduction removes it too. */
+int thb_mlp_bind_update(thb_mlp* session, uint32_t which, float* const* param_peers, void* param_multicast,
+                        void* const* copy_peers, void* copy_multicast);
+/* thb_mlp_forward_backward with the weight updates done inside the
+ * all-reduce (both layers bound with thb_mlp_bind_update, else status 1 with
+ * GPU-MLP-ARGUMENT):
+ * - The owner rank of each gradient tile applies SGD / momentum to the
+ *   summed tile.
+ * - It writes the new parameters and their bf16 copy to every rank.
+ * - Results are bit-identical to forward_backward + apply_sgd in peer mode.
+ * - dW is not written back to the ranks.
+ * - Velocities of a tile live on its owner only.
+ * After the ranks synchronise, thb_mlp_apply_sgd updates only the biases. */
+int thb_mlp_forward_backward_update(thb_mlp* session, const float* x, const float* t, float lr, void* stream,
+                                    char* failure, uint64_t failure_cap);
 /* CUDA-event timing of the session's GEMM launches, recorded on the stream
  * they are launched on (up to 512 launches between reads). */
 int thb_mlp_enable_timing(thb_mlp* session, int enabled);

@@ -142,3 +142,87 @@ def test_data_parallel_mlp_matches_full_batch(tmp_path, mode, world):
         assert rel(got[k], ref[k]) <= 1e-2, k
     for k in ("w1", "w2", "b1", "b2"):
         assert rel(got[k], ref[k]) <= 1e-4, k
+
+
+def _update_rank(rank, world, port, mode, out_path):
+    """Two data-parallel runs over the same process group: the all-reduce
+    fused into the dW GEMMs followed by the separate update pass, and the
+    update applied by each tile's owner inside the all-reduce."""
+    import datetime
+    import sys
+    import torch.distributed as dist
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    import thiran_b200 as thb
+    from thiran_b200.distributed import FusedGradientAllReduce
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    x, t, w1, w2, b1, b2 = problem()
+    batch = x.shape[0]
+    local = batch // world
+    xs = torch.from_numpy(x[rank * local:(rank + 1) * local].copy()).cuda()
+    ts = torch.from_numpy(t[rank * local:(rank + 1) * local].copy()).cuda()
+    results = {}
+    for fused in (False, True):
+        s, params = session(thb, local, batch, rank, w1, w2, b1, b2)
+        mc = FusedGradientAllReduce(s, dist, mode=mode, update=fused)
+        if not mc.available:
+            dist.destroy_process_group()
+            if rank == 0:
+                open(out_path, "w").write("unavailable")
+            return
+        for _ in range(3):
+            if fused:
+                s.forward_backward_update(xs, ts, LR)
+            else:
+                s.forward_backward(xs, ts)
+            mc.after_backward()
+            s.apply_sgd(LR)
+        thb.check_device_status(rank)
+        torch.cuda.synchronize()
+        weights = [mc.param_handles[0][1][0][0], mc.param_handles[1][1][0][0]] if fused else [params["w1"], params["w2"]]
+        copies = [mc.param_handles[0][1][1][0], mc.param_handles[1][1][1][0]] if fused else None
+        tag = "fused" if fused else "plain"
+        results[f"{tag}_w1"] = weights[0].cpu().numpy()
+        results[f"{tag}_w2"] = weights[1].cpu().numpy()
+        results[f"{tag}_b1"] = params["b1"].cpu().numpy()
+        results[f"{tag}_b2"] = params["b2"].cpu().numpy()
+        if copies is not None:
+            # Every rank holds the same parameters and bf16 copies.
+            for k, (w, c) in enumerate(zip(weights, copies)):
+                gathered = [torch.empty_like(w) for _ in range(world)]
+                dist.all_gather(gathered, w)
+                results[f"ranks_equal_w{k + 1}"] = np.array(all(torch.equal(g, w) for g in gathered))
+                results[f"copy_matches_w{k + 1}"] = np.array(torch.equal(c, w.to(torch.bfloat16)))
+        dist.barrier()
+        s.release()
+    if rank == 0:
+        np.savez(out_path, **results)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("mode", ["peer", "switch"])
+def test_update_fused_into_the_all_reduce(tmp_path, mode, world):
+    """The owner-applied update gives the same parameter bits as the separate
+    update pass after the fused all-reduce, on every rank, with bf16 copies
+    that match, and follows the single-process full-batch step."""
+    if gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    out = str(tmp_path / f"update_{mode}{world}.npz")
+    mp.start_processes(_update_rank, args=(world, free_port(), mode, out), nprocs=world, join=True,
+                       start_method="spawn")
+    if os.path.exists(out) and open(out, "rb").read(11) == b"unavailable":
+        pytest.skip("no NVLink multicast on this system")
+    got = dict(np.load(out))
+    for k in ("w1", "w2", "b1", "b2"):
+        assert np.array_equal(got[f"fused_{k}"].view(np.uint32), got[f"plain_{k}"].view(np.uint32)), k
+    for k in ("1", "2"):
+        assert bool(got[f"ranks_equal_w{k}"]) and bool(got[f"copy_matches_w{k}"]), k
+    ref = single_gpu_reference()
+    for k in ("w1", "w2", "b1", "b2"):
+        assert rel(got[f"fused_{k}"], ref[k]) <= 1e-4, k

@@ -190,6 +190,10 @@ SIGNATURES = {
     "thb_mlp_bind_reduction": (C.c_int, [C.c_void_p, C.c_uint32, C.POINTER(C.c_void_p), C.c_void_p,
                                          C.POINTER(C.c_void_p), C.c_uint32, C.c_uint32]),
     "thb_mlp_reduction_flag_words": (C.c_uint64, [C.c_void_p, C.c_uint32]),
+    "thb_mlp_bind_update": (C.c_int, [C.c_void_p, C.c_uint32, C.POINTER(C.c_void_p), C.c_void_p,
+                                      C.POINTER(C.c_void_p), C.c_void_p]),
+    "thb_mlp_forward_backward_update": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_void_p,
+                                                  C.c_char_p, C.c_uint64]),
     "thb_mlp_enable_timing": (C.c_int, [C.c_void_p, C.c_int]),
     "thb_mlp_read_timing": (C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
     "thb_sum_all_f32_noalloc": (C.c_int, [C.c_int, C.c_void_p, C.c_uint64, C.c_void_p, C.c_void_p, C.c_void_p,
@@ -220,6 +224,10 @@ class MlpSession:
 
     def set_weights(self, w1, w2, stream=0):
         self._call("thb_mlp_set_weights", w1.data_ptr(), w2.data_ptr(), C.c_void_p(stream))
+
+    def set_weight_pointers(self, w1_ptr, w2_ptr, stream=0):
+        """set_weights from raw device pointers (f32 [in][hidden], [hidden][out])."""
+        self._call("thb_mlp_set_weights", C.c_void_p(w1_ptr), C.c_void_p(w2_ptr), C.c_void_p(stream))
 
     def forward_backward(self, x, t, stream=0):
         self._call("thb_mlp_forward_backward", x.data_ptr(), t.data_ptr(), C.c_void_p(stream))
@@ -269,6 +277,25 @@ class MlpSession:
     def reduction_flag_words(self, which):
         """Number of u32 signal words bind_reduction needs for `which`."""
         return int(lib().thb_mlp_reduction_flag_words(self.handle, which))
+
+    def bind_update(self, which, param_ptrs, copy_ptrs, param_multicast=None, copy_multicast=None):
+        """Lets the all-reduce of layer `which` (MLP_W1 / MLP_W2, reduction
+        bound first) apply the optimizer step (thb_mlp_bind_update):
+        `param_ptrs[k]` / `copy_ptrs[k]` are rank k's f32 parameters and their
+        bf16 copy as mapped on this GPU. Copy the weights in afterwards with
+        set_weights."""
+        params = copies = None
+        if param_ptrs is not None:
+            params = (C.c_void_p * len(param_ptrs))(*param_ptrs)
+            copies = (C.c_void_p * len(copy_ptrs))(*copy_ptrs)
+        if lib().thb_mlp_bind_update(self.handle, which, params, C.c_void_p(param_multicast), copies,
+                                     C.c_void_p(copy_multicast)) != STATUS_OK:
+            raise GpuError(STATUS_ABI, "GPU-MLP-ARGUMENT: cannot bind the fused update")
+
+    def forward_backward_update(self, x, t, lr, stream=0):
+        """forward_backward with the weight updates applied in the
+        all-reduce; apply_sgd afterwards updates only the biases."""
+        self._call("thb_mlp_forward_backward_update", x.data_ptr(), t.data_ptr(), C.c_float(lr), C.c_void_p(stream))
 
     def bind(self, which, tensor):
         """Makes the session use `tensor`'s device memory for buffer `which`."""

@@ -29,6 +29,7 @@ struct thb_mlp {
     thb::mlp::Buffers b;
     thb::mlp::GemmTimer timer;
     std::uint32_t reduceEpoch = 0;  // forward/backward passes since the all-reduce was bound
+    bool weightsUpdated = false;    // the last pass applied the weight updates in its all-reduce
     std::vector<std::unique_ptr<thb::DeviceBuffer>> owned;
     ~thb_mlp() {
         for (auto& e : timer.events)
@@ -1003,28 +1004,51 @@ int thb_mlp_set_weights(thb_mlp* s, const float* w1, const float* w2, void* stre
     });
 }
 
-int thb_mlp_forward_backward(thb_mlp* s, const float* x, const float* t, void* stream, char* failure, uint64_t cap) {
+namespace {
+
+// Forward, loss and backward; with `lr`, the weight updates run in the
+// all-reduce of the weight-gradient GEMMs (thb_mlp_forward_backward_update).
+int forwardBackwardCall(thb_mlp* s, const float* x, const float* t, const float* lr, void* stream, char* failure,
+                        uint64_t cap) {
     return guarded(failure, cap, [&] {
         if (!s || !x || !t) fail(Category::Validation, "GPU-MLP-ARGUMENT", "null session or data");
         if ((reinterpret_cast<std::uintptr_t>(x) | reinterpret_cast<std::uintptr_t>(t)) % 16)
             fail(Category::Validation, "GPU-MLP-ARGUMENT", "x and t must be 16-byte aligned");
+        if (lr && !(s->b.dw1Reduce.update.paramPeers[0] && s->b.dw2Reduce.update.paramPeers[0]))
+            fail(Category::Validation, "GPU-MLP-ARGUMENT",
+                 "the fused update needs thb_mlp_bind_reduction and thb_mlp_bind_update for both layers");
         useDevice(s->device);
         // Each step's announcements raise every signal word by `world`.
         ++s->reduceEpoch;
         s->b.dw1Reduce.target = s->b.dw1Reduce.world * s->reduceEpoch;
         s->b.dw2Reduce.target = s->b.dw2Reduce.world * s->reduceEpoch;
         cudaCheck(mlp::forwardBackward(s->b, x, t, s->smCount, deviceStatus(s->device), static_cast<cudaStream_t>(stream),
-                                       &s->timer),
+                                       &s->timer, lr),
                   "MLP forward/backward");
+        s->weightsUpdated = lr != nullptr;
         return THB_STATUS_OK;
     });
+}
+
+} // namespace
+
+int thb_mlp_forward_backward(thb_mlp* s, const float* x, const float* t, void* stream, char* failure, uint64_t cap) {
+    return forwardBackwardCall(s, x, t, nullptr, stream, failure, cap);
+}
+
+int thb_mlp_forward_backward_update(thb_mlp* s, const float* x, const float* t, float lr, void* stream, char* failure,
+                                    uint64_t cap) {
+    return forwardBackwardCall(s, x, t, &lr, stream, failure, cap);
 }
 
 int thb_mlp_apply_sgd(thb_mlp* s, float lr, void* stream, char* failure, uint64_t cap) {
     return guarded(failure, cap, [&] {
         if (!s) fail(Category::Validation, "GPU-MLP-ARGUMENT", "null session");
         useDevice(s->device);
-        cudaCheck(mlp::applySgd(s->b, lr, s->smCount, static_cast<cudaStream_t>(stream)), "MLP SGD");
+        // After a fused-update pass only the biases are left.
+        cudaCheck(mlp::applySgd(s->b, lr, s->smCount, static_cast<cudaStream_t>(stream), !s->weightsUpdated),
+                  "MLP SGD");
+        s->weightsUpdated = false;
         return THB_STATUS_OK;
     });
 }
@@ -1177,6 +1201,32 @@ int thb_mlp_bind_reduction(thb_mlp* s, uint32_t which, void* const* peers, void*
     }
     (which == THB_MLP_DW1 ? s->b.dw1Reduce : s->b.dw2Reduce) = r;
     s->reduceEpoch = 0;  // fresh (zeroed) signal words
+    return THB_STATUS_OK;
+}
+
+int thb_mlp_bind_update(thb_mlp* s, uint32_t which, float* const* paramPeers, void* paramMulticast,
+                        void* const* copyPeers, void* copyMulticast) {
+    if (!s || (which != THB_MLP_W1 && which != THB_MLP_W2)) return THB_STATUS_ABI;
+    auto& r = which == THB_MLP_W1 ? s->b.dw1Reduce : s->b.dw2Reduce;
+    thb::gemm::ReduceUpdate u;
+    if (paramPeers) {
+        if (!r.cPeers[0] || !copyPeers) return THB_STATUS_ABI;
+        if (!r.cMulticast != !paramMulticast || !paramMulticast != !copyMulticast) return THB_STATUS_ABI;
+        if (reinterpret_cast<std::uintptr_t>(paramMulticast) % 16 || reinterpret_cast<std::uintptr_t>(copyMulticast) % 16)
+            return THB_STATUS_ABI;
+        for (uint32_t k = 0; k < r.world; ++k) {
+            if (!paramPeers[k] || !copyPeers[k] || reinterpret_cast<std::uintptr_t>(paramPeers[k]) % 16 ||
+                reinterpret_cast<std::uintptr_t>(copyPeers[k]) % 16)
+                return THB_STATUS_ABI;
+            u.paramPeers[k] = paramPeers[k];
+            u.copyPeers[k] = copyPeers[k];
+        }
+        u.paramMulticast = static_cast<float*>(paramMulticast);
+        u.copyMulticast = copyMulticast;
+        (which == THB_MLP_W1 ? s->b.w1 : s->b.w2) = paramPeers[r.rank];
+        (which == THB_MLP_W1 ? s->b.w1b : s->b.w2b) = copyPeers[r.rank];
+    }
+    r.update = u;
     return THB_STATUS_OK;
 }
 

@@ -220,10 +220,17 @@ struct Params {
     uint32_t rank, world, target;
     const float* bias;              // [n] or null
     float* colSums;                 // [mTiles * 4][n] or null (kEpiMaskBf16)
-    // kEpiSgdF32
+    // kEpiSgdF32, and kEpiAllReduceF32 with the fused update
     float* velocity;                // [m][ldc] or null
-    __nv_bfloat16* copy;            // [m][ldc] or null
+    __nv_bfloat16* copy;            // [m][ldc] or null (kEpiSgdF32)
     float lr, mu;
+    // kEpiAllReduceF32 with the fused update: parameters and their bf16
+    // copies on every rank (peer pointers; multicast in switch mode)
+    uint32_t fusedUpdate;
+    float* pPeers[kMaxRanks];
+    __nv_bfloat16* pbPeers[kMaxRanks];
+    float* pMc;
+    __nv_bfloat16* pbMc;
 };
 
 // Lane j ends with the sum over the warp's 32 lanes of s[j] (a butterfly
@@ -363,10 +370,59 @@ __device__ __forceinline__ bool awaitRows(const Params& p, uint32_t tile, uint32
     return ok != 0;
 }
 
+// The fused update of 4 parameters at element offset `at` (16-byte aligned)
+// from their summed gradients g: reads this rank's parameters (and
+// velocities), then writes the new parameters and their bf16 copy to every
+// rank, through the switch (multimem.st) or by peer stores.
+__device__ __forceinline__ void updateVector(const Params& p, uint64_t at, const float4& g, bool multicast) {
+    float4 w = __ldcg(reinterpret_cast<const float4*>(p.pPeers[p.rank] + at));
+    if (p.velocity) {
+        float4 m = *reinterpret_cast<const float4*>(p.velocity + at);
+        w.x = sgdStep(w.x, g.x, &m.x, p.lr, p.mu);
+        w.y = sgdStep(w.y, g.y, &m.y, p.lr, p.mu);
+        w.z = sgdStep(w.z, g.z, &m.z, p.lr, p.mu);
+        w.w = sgdStep(w.w, g.w, &m.w, p.lr, p.mu);
+        *reinterpret_cast<float4*>(p.velocity + at) = m;
+    } else {
+        w.x = sgdStep(w.x, g.x, nullptr, p.lr, p.mu);
+        w.y = sgdStep(w.y, g.y, nullptr, p.lr, p.mu);
+        w.z = sgdStep(w.z, g.z, nullptr, p.lr, p.mu);
+        w.w = sgdStep(w.w, g.w, nullptr, p.lr, p.mu);
+    }
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(w.x, w.y), hi = __floats2bfloat162_rn(w.z, w.w);
+    const uint32_t loBits = *reinterpret_cast<const uint32_t*>(&lo), hiBits = *reinterpret_cast<const uint32_t*>(&hi);
+    if (multicast) {
+        asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p.pMc + at), "f"(w.x),
+                     "f"(w.y), "f"(w.z), "f"(w.w)
+                     : "memory");
+        asm volatile("multimem.st.relaxed.sys.global.v2.bf16x2 [%0], {%1, %2};" ::"l"(p.pbMc + at), "r"(loBits),
+                     "r"(hiBits)
+                     : "memory");
+    } else {
+        for (uint32_t k = 0; k < p.world; ++k) {
+            __stcg(reinterpret_cast<float4*>(p.pPeers[k] + at), w);
+            __stcg(reinterpret_cast<uint2*>(p.pbPeers[k] + at), make_uint2(loBits, hiBits));
+        }
+    }
+}
+
+// The same for one parameter (ragged tile edges), always by peer stores.
+__device__ __forceinline__ void updateScalar(const Params& p, uint64_t at, float g) {
+    const float w = sgdStep(__ldcg(p.pPeers[p.rank] + at), g, p.velocity ? p.velocity + at : nullptr, p.lr, p.mu);
+    const __nv_bfloat16 b = __float2bfloat16_rn(w);
+    for (uint32_t k = 0; k < p.world; ++k) {
+        __stcg(p.pPeers[k] + at, w);
+        p.pbPeers[k][at] = b;
+    }
+}
+
 // Switch mode, full-width rows: the switch sums 16-byte vectors over all
-// ranks (multimem.ld_reduce) and writes the totals to all (multimem.st).
-// Lane takes vectors lane and lane + 32 of 8 rows per round: 16 in flight.
-__device__ __forceinline__ void switchReduceRows(float* base, uint64_t ldc, uint32_t rows, uint32_t lane) {
+// ranks (multimem.ld_reduce) and writes the totals to all (multimem.st), or
+// the owner applies the fused update. Lane takes vectors lane and lane + 32
+// of 8 rows per round: 16 in flight.
+__device__ __forceinline__ void switchReduceRows(const Params& p, uint64_t offset, uint32_t rows, uint32_t lane) {
+    float* base = p.cMc + offset;
+    const uint64_t ldc = p.ldc;
     for (uint32_t r0 = 0; r0 < rows; r0 += 8) {
         float4 v[16];
 #pragma unroll
@@ -384,10 +440,14 @@ __device__ __forceinline__ void switchReduceRows(float* base, uint64_t ldc, uint
         for (uint32_t i = 0; i < 16; ++i) {
             const uint32_t r = r0 + i / 2;
             if (r < rows) {
-                float* dst = base + r * ldc + 4u * (lane + 32u * (i % 2));
-                asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "f"(v[i].x),
-                             "f"(v[i].y), "f"(v[i].z), "f"(v[i].w)
-                             : "memory");
+                const uint64_t at = r * ldc + 4u * (lane + 32u * (i % 2));
+                if (p.fusedUpdate) {
+                    updateVector(p, offset + at, v[i], true);
+                } else {
+                    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(base + at),
+                                 "f"(v[i].x), "f"(v[i].y), "f"(v[i].z), "f"(v[i].w)
+                                 : "memory");
+                }
             }
         }
     }
@@ -417,6 +477,14 @@ __device__ __forceinline__ void peerReduceRows(const Params& p, uint64_t offset,
                 acc[i].w = __fadd_rn(acc[i].w, w[i].w);
             }
         }
+        if (p.fusedUpdate) {
+#pragma unroll
+            for (uint32_t i = 0; i < 8; ++i) {
+                const uint32_t r = r0 + i / 2;
+                if (r < rows) updateVector(p, offset + r * p.ldc + 4u * (lane + 32u * (i % 2)), acc[i], false);
+            }
+            continue;
+        }
         for (uint32_t k = 0; k < p.world; ++k) {
             float* dst = p.cPeers[k] + offset;
 #pragma unroll
@@ -443,7 +511,7 @@ __device__ __forceinline__ bool reduceRows(const Params& p, uint32_t tile, uint3
     const uint32_t cols = p.n - col0 < kBN ? static_cast<uint32_t>(p.n - col0) : kBN;
     const uint64_t offset = row0 * p.ldc + col0;
     if (cols == kBN) {
-        if (p.cMc) switchReduceRows(p.cMc + offset, p.ldc, rows, lane);
+        if (p.cMc) switchReduceRows(p, offset, rows, lane);
         else peerReduceRows(p, offset, rows, lane);
         return true;
     }
@@ -453,10 +521,15 @@ __device__ __forceinline__ bool reduceRows(const Params& p, uint32_t tile, uint3
             if (p.cMc) {
                 float x;
                 asm volatile("multimem.ld_reduce.relaxed.sys.global.add.f32 %0, [%1];" : "=f"(x) : "l"(p.cMc + at) : "memory");
-                asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(p.cMc + at), "f"(x) : "memory");
+                if (p.fusedUpdate) updateScalar(p, at, x);
+                else asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(p.cMc + at), "f"(x) : "memory");
             } else {
                 float x = 0.0f;
                 for (uint32_t k = 0; k < p.world; ++k) x = __fadd_rn(x, __ldcg(p.cPeers[k] + at));
+                if (p.fusedUpdate) {
+                    updateScalar(p, at, x);
+                    continue;
+                }
                 for (uint32_t k = 0; k < p.world; ++k) __stcg(p.cPeers[k] + at, x);
             }
         }
@@ -964,6 +1037,20 @@ const char* validate(const Problem& q) {
             if (reinterpret_cast<uintptr_t>(r.cPeers[k]) % 16 || reinterpret_cast<uintptr_t>(r.flagsPeers[k]) % 4)
                 return "peer C must be 16-byte and signal words 4-byte aligned";
         }
+        const ReduceUpdate& u = r.update;
+        if (u.enabled) {
+            if (!(u.momentum >= 0.0f && u.momentum < 1.0f)) return "the fused update needs momentum in [0, 1)";
+            if (u.momentum > 0.0f && (!u.velocity || reinterpret_cast<uintptr_t>(u.velocity) % 16))
+                return "momentum needs a 16-byte aligned velocity buffer";
+            for (uint32_t k = 0; k < r.world; ++k)
+                if (!u.paramPeers[k] || !u.copyPeers[k] || reinterpret_cast<uintptr_t>(u.paramPeers[k]) % 16 ||
+                    reinterpret_cast<uintptr_t>(u.copyPeers[k]) % 8)
+                    return "the fused update needs every rank's parameters (16-byte aligned) and bf16 copy (8-byte)";
+            if (!r.cMulticast != !u.paramMulticast || !u.paramMulticast != !u.copyMulticast)
+                return "switch mode needs multicast addresses of C, the parameters and their copy";
+            if ((reinterpret_cast<uintptr_t>(u.paramMulticast) % 16) || (reinterpret_cast<uintptr_t>(u.copyMulticast) % 8))
+                return "multicast parameters must be 16-byte and their copy 8-byte aligned";
+        }
     }
     return nullptr;
 }
@@ -1010,6 +1097,19 @@ cudaError_t run(const Problem& q, int smCount, uint32_t* status, cudaStream_t st
     p.copy = static_cast<__nv_bfloat16*>(q.update.copy);
     p.lr = q.update.lr;
     p.mu = q.update.momentum;
+    const ReduceUpdate& u = q.reduce.update;
+    p.fusedUpdate = q.epilogue == kEpiAllReduceF32 && u.enabled ? 1u : 0u;
+    if (p.fusedUpdate) {
+        p.velocity = u.momentum > 0.0f ? u.velocity : nullptr;
+        p.lr = u.lr;
+        p.mu = u.momentum;
+        for (int r = 0; r < kMaxRanks; ++r) {
+            p.pPeers[r] = u.paramPeers[r];
+            p.pbPeers[r] = static_cast<__nv_bfloat16*>(u.copyPeers[r]);
+        }
+        p.pMc = u.paramMulticast;
+        p.pbMc = static_cast<__nv_bfloat16*>(u.copyMulticast);
+    }
     if (q.aMajorMN) {
         if (q.bMajorMN) return launchEpi<true, true>(q.epilogue, pair, a, b, p, stream);
         return launchEpi<true, false>(q.epilogue, pair, a, b, p, stream);

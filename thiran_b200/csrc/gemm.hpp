@@ -44,12 +44,32 @@ struct Update {
 //    multimem.st writes the total to all ranks; about (1 + 1/world) of C each
 //    way, less than peer mode from 3 ranks up.
 constexpr int kMaxRanks = 8;
+
+// Optional optimizer step fused into the all-reduce: instead of writing the
+// summed tile to every rank's C, the owner applies the update to the f32
+// parameters P (same layout as C; its own copy is every rank's, since all
+// ranks hold the same parameters) and writes the new P, and its bf16 copy,
+// to every rank. Per element, in the order of the standalone pass
+// (src/training/v0/Training.cpp:366-372): d = g (or d = v*mu + g, v = d),
+// P = P - d*lr, each operation rounded to f32. The velocity of a tile lives
+// on its owner only (ownership is fixed for a given problem and grid).
+struct ReduceUpdate {
+    bool enabled = false;
+    float* paramPeers[kMaxRanks] = {};  // P as mapped on this GPU, for every rank
+    void* copyPeers[kMaxRanks] = {};    // bf16 copy of P, for every rank
+    float* paramMulticast = nullptr;    // switch mode: multicast addresses of P and of its copy
+    void* copyMulticast = nullptr;
+    float* velocity = nullptr;          // this rank's velocities (momentum > 0)
+    float lr = 0.0f, momentum = 0.0f;
+};
+
 struct AllReduce {
     void* cMulticast = nullptr;                   // switch mode: NVLS multicast address of C
     void* cPeers[kMaxRanks] = {};                 // C as mapped on this GPU, for every rank
     std::uint32_t* flagsPeers[kMaxRanks] = {};    // signal words (4 per tile), for every rank
     std::uint32_t rank = 0, world = 1;
     std::uint32_t target = 0;                     // each signal word's value once this launch's ranks all announced
+    ReduceUpdate update;
 };
 
 // Tiles of an M x N output (signal words needed: 4 per tile).

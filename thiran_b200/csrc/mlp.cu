@@ -234,22 +234,32 @@ cudaError_t forwardBackward(const Buffers& b, const float* x, const float* t, in
                             cudaStream_t s, GemmTimer* timer, const float* fusedLr) {
     GemmTimer none;
     GemmTimer& tm = timer ? *timer : none;
-    if (fusedLr && (b.dw1Reduce.cPeers[0] || b.dw2Reduce.cPeers[0])) return cudaErrorInvalidValue;
-    // Weight-gradient GEMM epilogue: store dW, all-reduce it, or apply the
-    // optimizer step to the parameters in place.
+    const bool reduced = b.dw1Reduce.cPeers[0] || b.dw2Reduce.cPeers[0];
+    // A data-parallel fused step needs the parameters of every rank bound.
+    if (fusedLr && reduced && !(b.dw1Reduce.update.paramPeers[0] && b.dw2Reduce.update.paramPeers[0]))
+        return cudaErrorInvalidValue;
+    // Weight-gradient GEMM epilogue: store dW, all-reduce it (and, with
+    // fusedLr, apply the update in the reduction), or apply the optimizer
+    // step to the parameters in place.
     const bool momentum = b.momentum > 0.0f;
     auto weightGradient = [&](gemm::Problem& q, float* dw, float* w, float* vw, void* wb, const gemm::AllReduce& r) {
-        if (fusedLr) {
+        if (r.cPeers[0]) {
+            q.c = dw;
+            q.epilogue = gemm::kEpiAllReduceF32;
+            q.reduce = r;
+            q.reduce.update.enabled = fusedLr != nullptr;
+            if (fusedLr) {
+                q.reduce.update.velocity = momentum ? vw : nullptr;
+                q.reduce.update.lr = *fusedLr;
+                q.reduce.update.momentum = b.momentum;
+            }
+        } else if (fusedLr) {
             q.c = w;
             q.epilogue = gemm::kEpiSgdF32;
             q.update.velocity = momentum ? vw : nullptr;
             q.update.copy = wb;
             q.update.lr = *fusedLr;
             q.update.momentum = b.momentum;
-        } else if (r.cPeers[0]) {
-            q.c = dw;
-            q.epilogue = gemm::kEpiAllReduceF32;
-            q.reduce = r;
         } else {
             q.c = dw;
             q.epilogue = gemm::kEpiF32;

@@ -43,6 +43,9 @@ struct Buffers {
     // plain local store). The caller advances `target` every step.
     gemm::AllReduce dw1Reduce;
     gemm::AllReduce dw2Reduce;
+    // With the all-reduce, the parameters and their bf16 copies on every rank
+    // (paramPeers / copyPeers / multicast of dwNReduce.update), so the owner
+    // of each tile can apply the update in the reduction.
 };
 
 // Optional CUDA-event timing of the GEMM launches of a step (recorded on the

@@ -62,10 +62,15 @@ class FusedGradientAllReduce:
 
     BARRIER_TIMEOUT_MS = 60000
 
-    def __init__(self, session, dist, group=None, mode=None):
+    def __init__(self, session, dist, group=None, mode=None, update=False):
+        """`update=True` also moves W1, W2 and their bf16 copies into
+        symmetric memory (thb_mlp_bind_update), so that a step can run
+        session.forward_backward_update(): each tile's owner applies the
+        optimizer step in the reduction and writes the new weights to every
+        rank."""
         import torch
         import torch.distributed._symmetric_memory as symm_mem
-        from . import MLP_DW1, MLP_DW2
+        from . import MLP_DW1, MLP_DW2, MLP_W1, MLP_W2
         self.group = group or dist.group.WORLD
         rank, world = dist.get_rank(self.group), dist.get_world_size(self.group)
         self.mode = mode or fused_reduction_mode(world)
@@ -82,16 +87,37 @@ class FusedGradientAllReduce:
             h = symm_mem.rendezvous(t, self.group)
             self.buffers.append((which, t))
             self.handles.append(h)
-        self.available = self.mode == "peer" or all(h.multicast_ptr for h in self.handles)
+        self.update = bool(update)
+        self.param_handles = []
+        if self.update:
+            for which, shape in ((MLP_W1, (session.d_in, session.hidden)), (MLP_W2, (session.hidden, session.d_out))):
+                pair = []
+                for dtype in (torch.float32, torch.bfloat16):
+                    t = symm_mem.empty(shape, dtype=dtype, device="cuda")
+                    pair.append((t, symm_mem.rendezvous(t, self.group)))
+                self.param_handles.append((which, pair))
+        handles = self.handles + [h for _, pair in self.param_handles for _, h in pair]
+        self.available = self.mode == "peer" or all(h.multicast_ptr for h in handles)
         # Every rank's signal words are zero before any rank can announce.
         self.flag_handle.barrier(channel=0, timeout_ms=self.BARRIER_TIMEOUT_MS)
         if self.available:
             offset = 0
             flag_ptrs = [int(p) for p in self.flag_handle.buffer_ptrs]
+            switch = self.mode == "switch"
             for ((which, t), h), n in zip(zip(self.buffers, self.handles), words):
                 session.bind_reduction(which, [int(p) for p in h.buffer_ptrs], [p + 4 * offset for p in flag_ptrs],
-                                       rank, world, h.multicast_ptr if self.mode == "switch" else None)
+                                       rank, world, h.multicast_ptr if switch else None)
                 offset += n
+            if self.update:
+                # The session's current weights move into the symmetric
+                # buffers (set_weights also refreshes the bf16 copies).
+                old = [session.buffer(MLP_W1)[0], session.buffer(MLP_W2)[0]]
+                for which, ((_, hp), (_, hc)) in self.param_handles:
+                    session.bind_update(which, [int(p) for p in hp.buffer_ptrs], [int(p) for p in hc.buffer_ptrs],
+                                        hp.multicast_ptr if switch else None, hc.multicast_ptr if switch else None)
+                session.set_weight_pointers(old[0], old[1], torch.cuda.current_stream().cuda_stream)
+                torch.cuda.current_stream().synchronize()
+                self.flag_handle.barrier(channel=0, timeout_ms=self.BARRIER_TIMEOUT_MS)
         self.dist = dist
         self.bias_grads = bind_bias_gradients(session)
 
