@@ -337,12 +337,14 @@ void emitKernels(std::ostringstream& out, const FusionGroup& group, const std::s
         << "        }\n"
         << "        __syncthreads();\n"
         << "        if (thb_abort) break;\n";
+    // (Stage pointers are thb_in<j>: s<j> names the group's runtime scalars.)
     for (std::size_t j = 0; j < k; ++j)
-        out << "        const " << packet << "* s" << j << " = (const " << packet << "*)(thb_stage + ((thb_u64)st * " << k
-            << " + " << j << ") * tile);\n";
+        out << "        const " << packet << "* thb_in" << j << " = (const " << packet << "*)(thb_stage + ((thb_u64)st * "
+            << k << " + " << j << ") * tile);\n";
     out << "        " << packet << "* so = (" << packet << "*)(thb_out + (thb_u64)ob * tile);\n"
         << "        for (thb_u32 q = threadIdx.x; q < tile / " << lanes << "; q += blockDim.x) {\n";
-    for (std::size_t j = 0; j < k; ++j) out << "            const " << packet << " x" << j << " = s" << j << "[q];\n";
+    for (std::size_t j = 0; j < k; ++j)
+        out << "            const " << packet << " x" << j << " = thb_in" << j << "[q];\n";
     out << "            " << packet << " r;\n#pragma unroll\n            for (int l = 0; l < " << lanes << "; ++l) r.v[l] = "
         << body << "(";
     for (std::size_t j = 0; j < k; ++j) out << "x" << j << ".v[l], ";
