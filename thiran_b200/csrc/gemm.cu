@@ -6,11 +6,14 @@
 // (A stored [K][M], B stored [K][N]), so the transposed products of a
 // reverse-AD backward pass (dW = X^T dH) need no transpose copies.
 //
-// One persistent CTA per SM, 192 threads:
+// One persistent CTA per SM, 192 threads (320 for the epilogues below that
+// read global memory or all-reduce):
 //   warp 0      TMA producer (one lane): 4-stage ring of {A 128x64, B 256x64}
 //   warp 1      TMEM owner (alloc/dealloc 512 columns) and MMA issuer (one
 //               lane): 4 x tcgen05.mma (M=128, N=256, K=16) per stage
 //   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, fused op, stores
+//               (warps 2..9, two per TMEM lane quadrant splitting the
+//               columns, for the optimizer-step and ReLU-mask epilogues)
 //   warps 6..9  (fused all-reduce only) reducers: sum the tiles this rank
 //               owns over all ranks and write the totals to every rank
 // Two TMEM accumulators (2 x 256 columns) let the epilogue of tile i overlap
@@ -42,9 +45,15 @@ namespace thb::gemm {
 namespace {
 
 constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
-constexpr int kThreads = 192;
 // The fused all-reduce adds 4 reducer warps (warps 6..9).
-constexpr int threadsFor(int epilogue) { return epilogue == kEpiAllReduceF32 ? kThreads + 128 : kThreads; }
+// Epilogue warps: 4 (one per TMEM lane quadrant), or 8 (two per quadrant,
+// each taking half of the tile's columns) for the epilogues that also read
+// global memory per element (the optimizer step reads the parameters, the
+// ReLU mask reads H): twice the loads in flight.
+constexpr int epilogueWarps(int epilogue) { return epilogue == kEpiSgdF32 || epilogue == kEpiMaskBf16 ? 8 : 4; }
+constexpr int threadsFor(int epilogue) {
+    return 64 + 32 * epilogueWarps(epilogue) + (epilogue == kEpiAllReduceF32 ? 128 : 0);
+}
 constexpr uint32_t kABytes = kBM * kBK * 2;  // 16 KB
 
 // Stage geometry. PAIR = a cluster of two CTAs on one 256x256 tile with
@@ -567,7 +576,7 @@ __global__ void __launch_bounds__(threadsFor(EPI), 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbarInit(&tmemFull[a], 1);
-            mbarInit(&tmemEmpty[a], PAIR ? 256 : 128);
+            mbarInit(&tmemEmpty[a], (PAIR ? 2 : 1) * 32 * epilogueWarps(EPI));
         }
         mbarInit(&mmaDone, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -700,9 +709,13 @@ __global__ void __launch_bounds__(threadsFor(EPI), 1)
             commit(&mmaDone);
             if (!mbarWait(&mmaDone, 0)) abortFlag = 1;
         }
-    } else if (warp >= 2 && warp < 6) {
+    } else if (warp >= 2 && warp < 2 + epilogueWarps(EPI)) {
         // ---- epilogue ----
         const uint32_t quadrant = warp % 4;  // TMEM lanes 32*quadrant .. +31
+        // With 8 epilogue warps the two warps of a quadrant split the tile's
+        // 32-column chunks.
+        constexpr uint32_t kChunks = kBN / 32, kChunksPerWarp = kChunks * 4 / epilogueWarps(EPI);
+        const uint32_t firstChunk = (warp - 2) / 4 * kChunksPerWarp;
         const uint32_t row = quadrant * 32 + lane;
         uint32_t acc = 0, accPhase = 0;
         TileQueue& queue = queues[quadrant];
@@ -720,9 +733,9 @@ __global__ void __launch_bounds__(threadsFor(EPI), 1)
             const uint64_t grow = static_cast<uint64_t>(rowBlock) * kBM + row;
             // A pair's second row block can lie wholly past M (no rows, and
             // no column-sum rows either).
-            const uint32_t chunks = static_cast<uint64_t>(rowBlock) * kBM < p.m ? kBN / 32 : 0u;
+            const uint32_t lastChunk = static_cast<uint64_t>(rowBlock) * kBM < p.m ? firstChunk + kChunksPerWarp : 0u;
 #pragma unroll 1
-            for (uint32_t chunk = 0; chunk < chunks; ++chunk) {
+            for (uint32_t chunk = firstChunk; chunk < lastChunk; ++chunk) {
                 uint32_t r[32];
                 tmemLoad32(tmemBase + ((quadrant * 32u) << 16) + acc * kBN + chunk * 32u, r);
                 const uint64_t col0 = static_cast<uint64_t>(nb) * kBN + chunk * 32u;
@@ -866,7 +879,7 @@ __global__ void __launch_bounds__(threadsFor(EPI), 1)
             }
             fenceBefore();
             // The accumulator is free once both CTAs of a pair have read it;
-            // the leader's barrier counts all 256 epilogue threads.
+            // the leader's barrier counts the epilogue threads of both.
             if (PAIR && rank != 0) mbarArriveCluster(releaseAddress + acc * static_cast<uint32_t>(sizeof(uint64_t)));
             else mbarArrive(&tmemEmpty[acc]);
             if (++acc == 2) { acc = 0; accPhase ^= 1u; }
@@ -878,7 +891,7 @@ __global__ void __launch_bounds__(threadsFor(EPI), 1)
             }
         }
         if constexpr (EPI == kEpiAllReduceF32) (void)pushTile(queue, kNoTile, lane, &abortFlag);
-    } else if (EPI == kEpiAllReduceF32 && warp >= 6) {
+    } else if (EPI == kEpiAllReduceF32 && warp >= 2 + epilogueWarps(EPI)) {
         // ---- reducers: owned tiles, summed over ranks in the switch ----
         const uint32_t quadrant = warp % 4;
         TileQueue& queue = queues[quadrant];
