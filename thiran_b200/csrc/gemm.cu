@@ -726,16 +726,90 @@ __global__ void __launch_bounds__(threadsFor(EPI), 1)
         for (uint32_t tile = first; tile < tiles; tile += step) {
             uint32_t mb, nb;
             tileCoords(tile, p, mb, nb);
-            if (!mbarWait(&tmemFull[acc], accPhase, &abortFlag)) abortFlag = 1;
-            if (abortFlag) break;
-            fenceAfter();
             const uint32_t rowBlock = mb * blocksPerTile + rank;
             const uint64_t grow = static_cast<uint64_t>(rowBlock) * kBM + row;
             // A pair's second row block can lie wholly past M (no rows, and
             // no column-sum rows either).
             const uint32_t lastChunk = static_cast<uint64_t>(rowBlock) * kBM < p.m ? firstChunk + kChunksPerWarp : 0u;
+            // Optimizer-step read-out over whole, aligned tiles: the
+            // parameters of a chunk are loaded one chunk ahead, the first
+            // chunk's before the accumulator is ready, so their latency
+            // overlaps the MMAs and the previous chunk's work.
+            bool fastUpdate = false;
+            float4 pc[8];
+            if constexpr (EPI == kEpiSgdF32) {
+                const uint64_t colBase = static_cast<uint64_t>(nb) * kBN;
+                fastUpdate = colBase + kBN <= p.n && p.ldc % 4 == 0 &&
+                             ((reinterpret_cast<uintptr_t>(p.c) | reinterpret_cast<uintptr_t>(p.velocity)) % 16) == 0 &&
+                             reinterpret_cast<uintptr_t>(p.copy) % 8 == 0;
+                if (fastUpdate && grow < p.m && firstChunk < lastChunk) {
+                    const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.c) + grow * p.ldc +
+                                                                        colBase + firstChunk * 32u);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) pc[q] = src[q];
+                }
+            }
+            if (!mbarWait(&tmemFull[acc], accPhase, &abortFlag)) abortFlag = 1;
+            if (abortFlag) break;
+            fenceAfter();
+            if constexpr (EPI == kEpiSgdF32) {
+                if (fastUpdate) {
+                    const bool rowValid = grow < p.m;
+                    const uint64_t rowOffset = grow * p.ldc + static_cast<uint64_t>(nb) * kBN;
 #pragma unroll 1
-            for (uint32_t chunk = firstChunk; chunk < lastChunk; ++chunk) {
+                    for (uint32_t chunk = firstChunk; chunk < lastChunk; ++chunk) {
+                        uint32_t r[32];
+                        tmemLoad32(tmemBase + ((quadrant * 32u) << 16) + acc * kBN + chunk * 32u, r);
+                        const uint64_t off = rowOffset + chunk * 32u;
+                        float4 pn[8];
+                        const bool more = chunk + 1 < lastChunk;
+                        if (rowValid && more) {
+                            const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.c) + off + 32u);
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) pn[q] = src[q];
+                        }
+                        if (rowValid) {
+                            float* dst = static_cast<float*>(p.c) + off;
+                            float* vel = p.velocity ? p.velocity + off : nullptr;
+                            __nv_bfloat16* cp = p.copy ? p.copy + off : nullptr;
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) {
+                                float4 w = pc[q];
+                                const float g0 = __uint_as_float(r[4 * q]), g1 = __uint_as_float(r[4 * q + 1]);
+                                const float g2 = __uint_as_float(r[4 * q + 2]), g3 = __uint_as_float(r[4 * q + 3]);
+                                if (vel) {
+                                    float4 m = *reinterpret_cast<const float4*>(vel + 4 * q);
+                                    w.x = sgdStep(w.x, g0, &m.x, p.lr, p.mu);
+                                    w.y = sgdStep(w.y, g1, &m.y, p.lr, p.mu);
+                                    w.z = sgdStep(w.z, g2, &m.z, p.lr, p.mu);
+                                    w.w = sgdStep(w.w, g3, &m.w, p.lr, p.mu);
+                                    *reinterpret_cast<float4*>(vel + 4 * q) = m;
+                                } else {
+                                    w.x = sgdStep(w.x, g0, nullptr, p.lr, p.mu);
+                                    w.y = sgdStep(w.y, g1, nullptr, p.lr, p.mu);
+                                    w.z = sgdStep(w.z, g2, nullptr, p.lr, p.mu);
+                                    w.w = sgdStep(w.w, g3, nullptr, p.lr, p.mu);
+                                }
+                                *reinterpret_cast<float4*>(dst + 4 * q) = w;
+                                if (cp) {
+                                    const __nv_bfloat162 lo = __floats2bfloat162_rn(w.x, w.y);
+                                    const __nv_bfloat162 hi = __floats2bfloat162_rn(w.z, w.w);
+                                    uint2 packed;
+                                    packed.x = *reinterpret_cast<const uint32_t*>(&lo);
+                                    packed.y = *reinterpret_cast<const uint32_t*>(&hi);
+                                    *reinterpret_cast<uint2*>(cp + 4 * q) = packed;
+                                }
+                            }
+                        }
+                        if (more) {
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) pc[q] = pn[q];
+                        }
+                    }
+                }
+            }
+#pragma unroll 1
+            for (uint32_t chunk = firstChunk; chunk < (fastUpdate ? firstChunk : lastChunk); ++chunk) {
                 uint32_t r[32];
                 tmemLoad32(tmemBase + ((quadrant * 32u) << 16) + acc * kBN + chunk * 32u, r);
                 const uint64_t col0 = static_cast<uint64_t>(nb) * kBN + chunk * 32u;
