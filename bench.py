@@ -363,7 +363,11 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
                     "d2h_bytes_per_step": 16, "steps": e2e_steps,
                     "api": "thb_mlp_* (inputs from pinned host, next batch copied during the current step; "
                            "loss read back every step)"},
-            "gpu_launches": args.steps * 10,
+            # Per step: X cast, 5 GEMMs, loss + dY, loss-partial sum, two
+            # bias-gradient column reductions, and the optimizer: the two bias
+            # updates, plus the two weight passes unless the weights were
+            # updated inside the GEMMs (1 GPU) or the all-reduce.
+            "gpu_launches": args.steps * (12 + (2 if world > 1 and not (fused and fused.update) else 0)),
             "clocks": clocks,
             "loss": float(loss[0].item()) / (workload.batch * d_out) if world == 1 else None,
         }
