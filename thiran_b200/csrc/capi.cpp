@@ -402,6 +402,30 @@ int thb_artifact_compile(const thb_artifact* artifact, int device, thb_region** 
 
 // ---- renderer ---------------------------------------------------------------------------
 
+namespace {
+
+// Per-device state of thb_render: its stream, the uploaded geometry, the
+// prepared triangles and tile lists, the framebuffer and the preparation's
+// scratch, all reused by the next call. The workspaces live for the
+// process, like the driver context they belong to.
+struct RenderWorkspace {
+    std::mutex mutex;
+    cudaStream_t stream = nullptr;
+    DeviceBuffer positions, colors, indices, triangles, offsets, lists, color, depth, counters;
+    thb::graphics::ScratchPool pool;
+};
+
+RenderWorkspace& renderWorkspace(int device) {
+    static std::mutex guard;
+    static std::map<int, RenderWorkspace*> workspaces;
+    std::lock_guard<std::mutex> lock(guard);
+    RenderWorkspace*& w = workspaces[device];
+    if (!w) w = new RenderWorkspace();
+    return *w;
+}
+
+} // namespace
+
 int thb_render(int device, const float* positions, uint64_t vertices, const int64_t* indices, uint64_t triangles,
                const float* colors, const float* model, const float* view, const float* projection, uint64_t width,
                uint64_t height, const float* clear, float* color, float* depth, uint64_t* stats, thb_evidence* evidence,
@@ -428,18 +452,21 @@ int thb_render(int device, const float* positions, uint64_t vertices, const int6
         const std::uint64_t pixels = width * height;
         if (pixels && (!color || !depth)) fail(Category::Validation, "TH019-FRAMEBUFFER-TENSOR", "null output buffer");
         useDevice(device);
-        cudaStream_t stream = nullptr;
-        cudaCheck(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreateWithFlags");
-        struct StreamGuard {
-            cudaStream_t s;
-            ~StreamGuard() { cudaStreamDestroy(s); }
-        } guard{stream};
-        DeviceBuffer tri, offsets, lists, colorBuf, depthBuf, counters;
+        // The device's render workspace: stream and buffers kept from call to
+        // call (grown when a frame needs more), one render at a time.
+        RenderWorkspace& ws = renderWorkspace(device);
+        std::lock_guard<std::mutex> lock(ws.mutex);
+        if (!ws.stream)
+            cudaCheck(cudaStreamCreateWithFlags(&ws.stream, cudaStreamNonBlocking), "cudaStreamCreateWithFlags");
+        cudaStream_t stream = ws.stream;
+        DeviceBuffer &tri = ws.triangles, &offsets = ws.offsets, &lists = ws.lists, &colorBuf = ws.color,
+                     &depthBuf = ws.depth, &counters = ws.counters;
         auto upload = [&](DeviceBuffer& b, const void* host, std::size_t bytes) {
             if (!bytes) return;
-            b.reserve(bytes, device);
-            ++ev.allocation_count;
-            ev.allocation_bytes_requested += bytes;
+            if (b.reserve(bytes, device)) {
+                ++ev.allocation_count;
+                ev.allocation_bytes_requested += bytes;
+            }
             cudaCheck(cudaMemcpyAsync(b.ptr, host, bytes, cudaMemcpyHostToDevice, stream), "cudaMemcpyAsync(render input)");
             ++ev.host_to_device_copies;
             ev.host_to_device_bytes += bytes;
@@ -451,28 +478,32 @@ int thb_render(int device, const float* positions, uint64_t vertices, const int6
             upload(lists, p.tileLists.data(), p.tileLists.size() * sizeof(std::uint32_t));
             postClip = p.postClipTriangles;
         } else {
-            DeviceBuffer devPositions, devColors, devIndices;
-            upload(devPositions, positions, vertices * 3 * sizeof(float));
-            upload(devColors, colors, vertices * 4 * sizeof(float));
-            upload(devIndices, indices, triangles * 3 * sizeof(std::int64_t));
+            upload(ws.positions, positions, vertices * 3 * sizeof(float));
+            upload(ws.colors, colors, vertices * 4 * sizeof(float));
+            upload(ws.indices, indices, triangles * 3 * sizeof(std::int64_t));
             const gfx::DevicePrepared d = gfx::prepareOnDevice(
-                scene, static_cast<const float*>(devPositions.ptr), static_cast<const float*>(devColors.ptr),
-                static_cast<const std::int64_t*>(devIndices.ptr), device, stream, tri, offsets, lists);
+                scene, static_cast<const float*>(ws.positions.ptr), static_cast<const float*>(ws.colors.ptr),
+                static_cast<const std::int64_t*>(ws.indices.ptr), device, stream, tri, offsets, lists, ws.pool);
             if (d.failure) fail(Category::Semantic, d.failure, d.failure);
             ev.kernel_launches += d.launches;
-            ev.synchronizations += 3;
+            ev.allocation_count += d.allocations;
+            ev.synchronizations += 2;
             postClip = d.postClipTriangles;
             p.tilesX = scene.tilesX;
             p.tilesY = scene.tilesY;
             std::memcpy(p.clear, scene.clear, sizeof p.clear);
         }
-        counters.reserve(2 * sizeof(unsigned long long), device);
+        if (counters.reserve(2 * sizeof(unsigned long long), device)) ++ev.allocation_count;
         cudaCheck(cudaMemsetAsync(counters.ptr, 0, 2 * sizeof(unsigned long long), stream), "cudaMemsetAsync");
         if (pixels) {
-            colorBuf.reserve(pixels * 16, device);
-            depthBuf.reserve(pixels * 4, device);
-            ev.allocation_count += 2;
-            ev.allocation_bytes_requested += pixels * 20;
+            if (colorBuf.reserve(pixels * 16, device)) {
+                ++ev.allocation_count;
+                ev.allocation_bytes_requested += pixels * 16;
+            }
+            if (depthBuf.reserve(pixels * 4, device)) {
+                ++ev.allocation_count;
+                ev.allocation_bytes_requested += pixels * 4;
+            }
             cudaCheck(gfx::rasterize(static_cast<const gfx::RasterTriangle*>(tri.ptr),
                                      static_cast<const std::uint32_t*>(offsets.ptr),
                                      static_cast<const std::uint32_t*>(lists.ptr), p.tilesX, p.tilesY,

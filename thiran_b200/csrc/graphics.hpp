@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <memory>
 #include <string>
 #include <vector>
 
@@ -79,11 +80,18 @@ struct DevicePrepared {
     std::uint64_t count = 0;  // screen triangles after setup
     const char* failure = nullptr;  // TH019 id found on the device, or null
     std::uint64_t launches = 0;     // kernels launched
+    std::uint64_t allocations = 0;  // scratch buffers that had to grow
+};
+// Device scratch buffers kept from call to call: each call takes them in
+// the same request order and grows one only when it is too small.
+struct ScratchPool {
+    std::vector<std::unique_ptr<thb::DeviceBuffer>> buffers;
+    std::size_t next = 0;
 };
 DevicePrepared prepareOnDevice(const Scene& scene, const float* positions, const float* colors,
                                const std::int64_t* indices, int device, cudaStream_t stream,
                                thb::DeviceBuffer& triangles, thb::DeviceBuffer& tileOffsets,
-                               thb::DeviceBuffer& tileLists);
+                               thb::DeviceBuffer& tileLists, ScratchPool& pool);
 
 // Rasterizes on `stream`: color [pixels][4], depth [pixels] (device), stats
 // (device, 2 x u64: shaded pixels, depth passes; accumulated into).

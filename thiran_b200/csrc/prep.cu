@@ -307,29 +307,33 @@ void check(cudaError_t e, const char* what) {
 
 unsigned blocksFor(std::uint64_t n, std::uint64_t per) { return static_cast<unsigned>((n + per - 1) / per); }
 
-// out[i] = sum of in[0..i), meta->total = sum of in; temporaries stay alive
-// in `keep` until the caller synchronises.
+// The pool's next buffer, grown to at least `bytes` (16 at least); counts
+// the growths in `allocations`.
+void* take(ScratchPool& pool, std::size_t bytes, int device, std::uint64_t& allocations) {
+    if (pool.next == pool.buffers.size()) pool.buffers.push_back(std::make_unique<DeviceBuffer>());
+    DeviceBuffer& b = *pool.buffers[pool.next++];
+    if (b.reserve(bytes < 16 ? 16 : bytes, device)) ++allocations;
+    return b.ptr;
+}
+
+// out[i] = sum of in[0..i), meta->total = sum of in; temporaries come from
+// `pool`.
 template <class In>
 void exclusiveScan(const In* in, std::uint64_t n, std::uint64_t* out, Meta* meta, int device, cudaStream_t stream,
-                   std::vector<std::unique_ptr<DeviceBuffer>>& keep, std::uint64_t& launches, bool total = true) {
+                   ScratchPool& pool, DevicePrepared& counts, bool total = true) {
+    std::uint64_t& launches = counts.launches;
     if (n == 0) {
         if (total) check(cudaMemsetAsync(&meta->total, 0, sizeof meta->total, stream), "cudaMemsetAsync(scan)");
         return;
     }
     const unsigned blocks = blocksFor(n, kScanItems);
-    keep.push_back(std::make_unique<DeviceBuffer>());
-    DeviceBuffer& sums = *keep.back();
-    sums.reserve(static_cast<std::size_t>(blocks) * 8, device);
-    auto* s = static_cast<std::uint64_t*>(sums.ptr);
+    auto* s = static_cast<std::uint64_t*>(take(pool, static_cast<std::size_t>(blocks) * 8, device, counts.allocations));
     scanBlocks<In><<<blocks, kThreads, 0, stream>>>(in, n, out, s);
     check(cudaGetLastError(), "scan");
     ++launches;
     if (blocks > 1) {
-        keep.push_back(std::make_unique<DeviceBuffer>());
-        DeviceBuffer& scanned = *keep.back();
-        scanned.reserve(static_cast<std::size_t>(blocks) * 8, device);
-        auto* o = static_cast<std::uint64_t*>(scanned.ptr);
-        exclusiveScan<std::uint64_t>(s, blocks, o, meta, device, stream, keep, launches, false);
+        auto* o = static_cast<std::uint64_t*>(take(pool, static_cast<std::size_t>(blocks) * 8, device, counts.allocations));
+        exclusiveScan<std::uint64_t>(s, blocks, o, meta, device, stream, pool, counts, false);
         addBlockOffsets<<<blocksFor(n, kThreads), kThreads, 0, stream>>>(out, n, o);
         check(cudaGetLastError(), "scan offsets");
         ++launches;
@@ -416,15 +420,12 @@ __global__ void __launch_bounds__(kThreads) addTileStarts(std::uint32_t* __restr
 
 DevicePrepared prepareOnDevice(const Scene& scene, const float* positions, const float* colors,
                                const std::int64_t* indices, int device, cudaStream_t stream,
-                               DeviceBuffer& triangles, DeviceBuffer& tileOffsets, DeviceBuffer& tileLists) {
+                               DeviceBuffer& triangles, DeviceBuffer& tileOffsets, DeviceBuffer& tileLists,
+                               ScratchPool& pool) {
     DevicePrepared result;
     const std::uint64_t vertices = scene.vertices, inputs = scene.triangles;
-    std::vector<std::unique_ptr<DeviceBuffer>> keep;
-    auto scratch = [&](std::size_t bytes) {
-        keep.push_back(std::make_unique<DeviceBuffer>());
-        keep.back()->reserve(bytes < 16 ? 16 : bytes, device);
-        return keep.back()->ptr;
-    };
+    pool.next = 0;
+    auto scratch = [&](std::size_t bytes) { return take(pool, bytes, device, result.allocations); };
     auto* meta = static_cast<Meta*>(scratch(sizeof(Meta)));
     check(cudaMemsetAsync(meta, 0, sizeof(Meta), stream), "cudaMemsetAsync(meta)");
     Meta host{};
@@ -448,7 +449,7 @@ DevicePrepared prepareOnDevice(const Scene& scene, const float* positions, const
         check(cudaGetLastError(), "clip (count)");
         ++result.launches;
     }
-    exclusiveScan<std::uint32_t>(kept, inputs, offsets, meta, device, stream, keep, result.launches);
+    exclusiveScan<std::uint32_t>(kept, inputs, offsets, meta, device, stream, pool, result);
     check(cudaMemcpyAsync(&host, meta, sizeof host, cudaMemcpyDeviceToHost, stream), "cudaMemcpyAsync(meta)");
     check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
     // The host pipeline's failure order: transform, clip, triangle count,
@@ -505,7 +506,7 @@ DevicePrepared prepareOnDevice(const Scene& scene, const float* positions, const
     chunkPrefix<<<blocksFor(tiles, kThreads), kThreads, 0, stream>>>(cells, chunks, tiles, totals);
     check(cudaGetLastError(), "bin (chunk prefix)");
     ++result.launches;
-    exclusiveScan<std::uint64_t>(totals, tiles, starts, meta, device, stream, keep, result.launches);
+    exclusiveScan<std::uint64_t>(totals, tiles, starts, meta, device, stream, pool, result);
     check(cudaMemcpyAsync(&host, meta, sizeof host, cudaMemcpyDeviceToHost, stream), "cudaMemcpyAsync(meta)");
     check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
     if (host.total >= std::numeric_limits<std::uint32_t>::max()) {
@@ -521,8 +522,6 @@ DevicePrepared prepareOnDevice(const Scene& scene, const float* positions, const
                                                          static_cast<std::uint32_t*>(tileLists.ptr));
     check(cudaGetLastError(), "bin (fill)");
     ++result.launches;
-    // The temporaries are freed on return, after the queued work.
-    check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
     return result;
 }
 
