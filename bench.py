@@ -353,7 +353,9 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
                                       "separate pass" if fused and fused.update else
                                       "SGD pass after the gradient all-reduce")),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak,
+                         # mean DRAM bytes of the step's GEMM launches (1 GPU capture)
+                         "traffic": ncu_traffic(workload.ncu_name) if world == 1 else None,
                          "kernel": "tcgen05 GEMM (256x256 tiles on CTA pairs, cta_group::2, TMEM accumulators; "
                                    "dW GEMMs with the fused all-reduce: 128x256 tiles on single CTAs)",
                          "algorithmic_flops_per_launch": flops_rank / 5,
