@@ -31,8 +31,10 @@ struct BulkShape {
 };
 
 // Ring geometry of a group's bulk-copy entry for `arity` tensor inputs: two
-// stages of 32 KiB tiles per input while (2 * arity + 2) tiles fit in
-// 200 KiB of shared memory, smaller tiles (multiples of 4 KiB) past that.
+// stages, tiles of the largest multiple of 4 KiB up to 48 KiB for which the
+// (2 * arity + 2) tiles fit in 200 KiB of shared memory (48 KiB for one
+// input, 32 KiB for two: the 2^28 f32 chain measured 341 us per launch with
+// 48 KiB against 344 with 32 KiB, and 351-358 with 3-4 stages or 24 KiB).
 // On B200 two stages of 32 KiB ran the 8192^2 i64 region at ~238 us per
 // launch whatever the placement of its three arrays, where the 128-bit
 // vector kernel took ~270-290 us; 16 KiB tiles (2-4 stages) took ~325 us and
@@ -52,7 +54,7 @@ bool bulkShape(std::size_t arity, BulkShape& s) {
         s.stages = static_cast<std::uint32_t>(choice.first);
         s.tileBytes = static_cast<std::uint32_t>(choice.second) * 1024u;
     } else {
-        constexpr std::uint64_t kBudget = 200u * 1024u, kTile = 32768, kStep = 4096;
+        constexpr std::uint64_t kBudget = 200u * 1024u, kTile = 49152, kStep = 4096;
         s.stages = 2;
         const std::uint64_t tiles = 2 * arity + 2;
         s.tileBytes = static_cast<std::uint32_t>(std::min<std::uint64_t>(kTile, kBudget / tiles / kStep * kStep));
