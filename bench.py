@@ -143,7 +143,8 @@ class FullSum(Workload):
     rows, cols = 65536, 4096
     ncu_name = "full_sum_65536x4096"
     combine = True
-    kernel = "two-pass deterministic f64 full sum (sumAllPass1 + sumAllPass2)"
+    kernel = ("two-pass deterministic f64 full sum: sumAllBulk (48 KiB cp.async.bulk tiles, one partial per SM) "
+              "+ sumAllPass2")
     launches_per_step = 2
 
     def build(self, torch, rank, world):

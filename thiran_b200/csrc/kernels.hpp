@@ -30,9 +30,12 @@ cudaError_t sumColsF32(const float* x, float* y, std::uint64_t rows, std::uint64
 // per block of a fixed grid into `partials`, pass 2 adds them in block order.
 // `out64` (optional) receives the f64 total, `out32` (optional) its f32
 // rounding. `partials` must hold sumAllPartialCount(n, smCount) doubles.
+// Large aligned inputs stream through 48 KiB bulk-copy tiles with one
+// partial per SM; `status` (optional) gets bit 4 if a bounded wait runs out,
+// and the sum is then NaN.
 std::uint32_t sumAllPartialCount(std::uint64_t n, int smCount);
 cudaError_t sumAllF32(const float* x, std::uint64_t n, double* partials, std::uint32_t partialCount, double* out64,
-                      float* out32, int smCount, cudaStream_t stream);
+                      float* out32, int smCount, cudaStream_t stream, std::uint32_t* status = nullptr);
 
 // y[c, r] = x[r, c] for a row-major [rows, cols] matrix of 4- or 8-byte
 // elements (32x32 shared-memory tiles, coalesced on both sides).

@@ -14,7 +14,9 @@
 //    stores it (shared->global). Every mbarrier wait is bounded; on expiry
 //    the kernel raises bit 4 of its status word, drains its own copies and
 //    returns.
-// THB_ROWS=staged keeps the staged kernel for every row length it serves.
+// The full-tensor sum streams 48 KiB tiles through the bulk-copy engine
+// (0.99 of the copy peak against 0.97 for 128-bit loads).
+// THB_ROWS=staged keeps the staged kernels (and the 128-bit full-sum pass).
 //
 // The reference has no native reduction (src/backend/v0/TensorRegion.cpp:425
 // "Sum lowering deferred"); its Evaluator sums sequentially in f32
@@ -408,6 +410,81 @@ __global__ void __launch_bounds__(kSumThreads) sumAllPass1(const float* __restri
     }
 }
 
+// Pass 1 over whole 48 KiB tiles with the bulk-copy engine: one persistent
+// CTA per SM takes tiles blockIdx.x, blockIdx.x + gridDim.x, ...; thread 0
+// keeps a 3-stage ring of them in shared memory full (cp.async.bulk,
+// mbarrier completion) and all threads add their part of each tile in f64.
+// The elements past the last whole tile take plain loads. A wait that runs
+// out raises the status bit (when given) and poisons the partial with NaN.
+constexpr unsigned kSumStages = 3;
+constexpr unsigned kSumTileFloats = 12288;  // 48 KiB
+constexpr std::size_t kSumBulkSmem = static_cast<std::size_t>(kSumStages) * kSumTileFloats * sizeof(float);
+
+__global__ void __launch_bounds__(kSumThreads) sumAllBulk(const float* __restrict__ x, std::uint64_t n,
+                                                          double* __restrict__ partials,
+                                                          std::uint32_t* __restrict__ status) {
+    extern __shared__ __align__(128) float tileSmem[];
+    __shared__ __align__(8) std::uint64_t full[kSumStages];
+    __shared__ double red[kSumThreads / 32];
+    __shared__ int abortFlag;
+    const std::uint64_t tiles = n / kSumTileFloats;
+    const std::uint64_t first = blockIdx.x, step = gridDim.x;
+    constexpr unsigned kTileBytes = kSumTileFloats * sizeof(float);
+    auto issue = [&](std::uint64_t t, unsigned s) {
+        if (t >= tiles) return;
+        mbarExpect(&full[s], kTileBytes);
+        bulkLoad(tileSmem + static_cast<std::size_t>(s) * kSumTileFloats, x + t * kSumTileFloats, kTileBytes, &full[s]);
+    };
+    if (threadIdx.x == 0) {
+        abortFlag = 0;
+        for (unsigned s = 0; s < kSumStages; ++s) mbarInit(&full[s], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (unsigned s = 0; s < kSumStages; ++s) issue(first + s * step, s);
+    }
+    __syncthreads();
+    double acc = 0.0;
+    unsigned st = 0, phase = 0;
+    for (std::uint64_t t = first; t < tiles; t += step) {
+        if (threadIdx.x == 0 && !mbarWait(&full[st], phase)) {
+            abortFlag = 1;
+            // Loads still in flight land before the CTA exits.
+            unsigned s = st, ph = phase;
+            for (unsigned q = 0; q < kSumStages; ++q) {
+                if (t + q * step < tiles) (void)mbarWait(&full[s], ph);
+                if (++s == kSumStages) { s = 0; ph ^= 1u; }
+            }
+        }
+        __syncthreads();
+        if (abortFlag) break;
+        const float4* tile = reinterpret_cast<const float4*>(tileSmem + static_cast<std::size_t>(st) * kSumTileFloats);
+#pragma unroll 4
+        for (unsigned q = threadIdx.x; q < kSumTileFloats / 4; q += kSumThreads) {
+            const float4 a = tile[q];
+            acc += ((double)a.x + (double)a.y) + ((double)a.z + (double)a.w);
+        }
+        __syncthreads();  // every thread is done with the stage
+        if (threadIdx.x == 0) issue(t + kSumStages * step, st);
+        if (++st == kSumStages) { st = 0; phase ^= 1u; }
+    }
+    if (abortFlag) {
+        if (threadIdx.x == 0) {
+            if (status) atomicOr(status, kWaitStatus);
+            acc = __longlong_as_double(0x7ff8000000000000ll);  // NaN
+        }
+    } else {
+        const std::uint64_t stride = step * kSumThreads;
+        for (std::uint64_t i = tiles * kSumTileFloats + first * kSumThreads + threadIdx.x; i < n; i += stride) acc += x[i];
+    }
+    acc = warpSum(acc);
+    if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = red[0];
+        for (unsigned w = 1; w < kSumThreads / 32; ++w) t += red[w];
+        partials[blockIdx.x] = t;
+    }
+}
+
 __global__ void __launch_bounds__(kSumThreads) sumAllPass2(const double* __restrict__ partials, unsigned count,
                                                            double* __restrict__ out64, float* __restrict__ out32) {
     __shared__ double red[kSumThreads / 32];
@@ -475,13 +552,31 @@ std::uint32_t sumAllPartialCount(std::uint64_t n, int smCount) {
 }
 
 cudaError_t sumAllF32(const float* x, std::uint64_t n, double* partials, std::uint32_t partialCount, double* out64,
-                      float* out32, int, cudaStream_t stream) {
+                      float* out32, int smCount, cudaStream_t stream, std::uint32_t* status) {
     if (partialCount == 0) return cudaErrorInvalidValue;
     if (n == 0) {
         sumAllPass2<<<1, kSumThreads, 0, stream>>>(partials, 0, out64, out32);
         return cudaGetLastError();
     }
-    if (reinterpret_cast<std::uintptr_t>(x) % 16 == 0)
+    const bool aligned = reinterpret_cast<std::uintptr_t>(x) % 16 == 0;
+    // Bulk tiles once every SM has one (THB_ROWS=staged keeps the vector
+    // pass, for comparison).
+    static const bool bulk = [] {
+        const char* e = std::getenv("THB_ROWS");
+        return !(e && std::strcmp(e, "staged") == 0);
+    }();
+    const std::uint64_t tiles = n / kSumTileFloats;
+    if (aligned && bulk && smCount > 0 && tiles >= static_cast<std::uint64_t>(smCount) &&
+        partialCount >= static_cast<std::uint32_t>(smCount)) {
+        cudaError_t e = cudaFuncSetAttribute(sumAllBulk, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(kSumBulkSmem));
+        if (e != cudaSuccess) return e;
+        sumAllBulk<<<smCount, kSumThreads, kSumBulkSmem, stream>>>(x, n, partials, status);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        sumAllPass2<<<1, kSumThreads, 0, stream>>>(partials, static_cast<unsigned>(smCount), out64, out32);
+        return cudaGetLastError();
+    }
+    if (aligned)
         sumAllPass1<true><<<partialCount, kSumThreads, 0, stream>>>(x, n, partials);
     else
         sumAllPass1<false><<<partialCount, kSumThreads, 0, stream>>>(x, n, partials);

@@ -414,7 +414,7 @@ void CompiledRegion::launchReduction(const FusionGroup& group, const Value& in, 
                 ev.allocation_bytes_requested += parts * sizeof(double);
             }
             e = kernels::sumAllF32(x, in.count(), static_cast<double*>(scratch->ptr), parts, nullptr, y,
-                                   info_->smCount, stream);
+                                   info_->smCount, stream, status);
         } else if (node.axis == 1) {
             e = kernels::sumRowsF32(x, y, rows, cols, info_->smCount, stream, status);
         } else {
