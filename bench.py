@@ -208,9 +208,15 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
     fused = None
     if world > 1 and args.dp_collective != "nccl":
         from thiran_b200.distributed import FusedGradientAllReduce
+        from thiran_b200.distributed import fused_reduction_mode
         mode = {"fused": None, "fused-peer": "peer", "fused-switch": "switch"}[args.dp_collective]
+        # Measured: the owner-applied update wins in switch mode (8 ranks
+        # 2.141 vs 2.204 ms per step) and loses in peer mode (2 ranks 2.87
+        # vs 2.79 ms).
+        switch = (mode or fused_reduction_mode(world)) == "switch"
+        update = args.dp_update == "fused" or (args.dp_update == "auto" and switch)
         with torch.cuda.stream(stream):
-            fused = FusedGradientAllReduce(session, dist, mode=mode, update=args.dp_update == "fused")
+            fused = FusedGradientAllReduce(session, dist, mode=mode, update=update)
         if not fused.available:
             fused = None
     from thiran_b200.distributed import bind_bias_gradients
@@ -577,9 +583,10 @@ def main():
     p.add_argument("--dp-collective", default="fused", choices=["fused", "fused-peer", "fused-switch", "nccl"],
                    help="MLP data-parallel gradient reduction: fused into the dW GEMMs (peer loads/stores at "
                         "2 ranks, in-switch from 3; or forced), or NCCL all-reduce after the backward pass")
-    p.add_argument("--dp-update", default="pass", choices=["fused", "pass"],
-                   help="with a fused all-reduce: run the separate update pass on every rank (default; measured "
-                        "faster at 2 ranks), or apply the optimizer step in the reduction (each tile's owner)")
+    p.add_argument("--dp-update", default="auto", choices=["auto", "fused", "pass"],
+                   help="with a fused all-reduce: apply the optimizer step in the reduction (each tile's owner; "
+                        "'auto' does so in switch mode, where it measured faster) or run the separate update pass "
+                        "on every rank (faster in peer mode, 2 ranks)")
     p.add_argument("--shrink", type=int, default=1,
                    help="divide the leading extent (small cases for profiler captures; not a bench line)")
     args = p.parse_args()
