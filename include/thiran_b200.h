@@ -535,7 +535,8 @@ int thb_mlp_bind(thb_mlp* session, uint32_t which, void* device_pointer);
  * status word gets bit 4 (thb_device_check_status) and the step's gradients
  * are incomplete. The caller synchronises the ranks after forward_backward
  * and before reading dW (apply_sgd); every rank binds the same way and runs
- * the same steps. NULL `peers` restores the local store. Binding restarts the
+ * the same steps. NULL `peers` restores the local store: dW returns to the
+ * session's own buffer, so the bound ones may be freed. Binding restarts the
  * step count the signal words are checked against, so they must be zero again
  * on every rank. */
 int thb_mlp_bind_reduction(thb_mlp* session, uint32_t which, void* const* peers, void* multicast,
@@ -552,8 +553,9 @@ uint64_t thb_mlp_reduction_flag_words(thb_mlp* session, uint32_t which);
  *   Copy the weights in afterwards with thb_mlp_set_weights.
  * - With a multicast reduction, `param_multicast` and `copy_multicast` are
  *   their NVLS multicast addresses; otherwise both are NULL.
- * - NULL `param_peers` removes the binding.
- * Rebinding the reduction removes it too. */
+ * - NULL `param_peers` removes the binding, and so does rebinding the
+ *   reduction. W and bf16 W then return to the session's own buffers, and the
+ *   caller copies the weights in again with thb_mlp_set_weights. */
 int thb_mlp_bind_update(thb_mlp* session, uint32_t which, float* const* param_peers, void* param_multicast,
                         void* const* copy_peers, void* copy_multicast);
 /* thb_mlp_forward_backward with the weight updates done inside the

@@ -283,7 +283,8 @@ class MlpSession:
         bound first) apply the optimizer step (thb_mlp_bind_update):
         `param_ptrs[k]` / `copy_ptrs[k]` are rank k's f32 parameters and their
         bf16 copy as mapped on this GPU. Copy the weights in afterwards with
-        set_weights."""
+        set_weights. `param_ptrs=None` removes the binding: W returns to the
+        session's own buffers, into which set_weights copies them again."""
         params = copies = None
         if param_ptrs is not None:
             params = (C.c_void_p * len(param_ptrs))(*param_ptrs)

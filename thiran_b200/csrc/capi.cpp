@@ -30,6 +30,11 @@ struct thb_mlp {
     thb::mlp::GemmTimer timer;
     std::uint32_t reduceEpoch = 0;  // forward/backward passes since the all-reduce was bound
     bool weightsUpdated = false;    // the last pass applied the weight updates in its all-reduce
+    // The session's own W, bf16 W and dW buffers (per layer), to which
+    // removing a reduction or update binding returns.
+    float* ownW[2] = {};
+    void* ownWb[2] = {};
+    float* ownDw[2] = {};
     std::vector<std::unique_ptr<thb::DeviceBuffer>> owned;
     ~thb_mlp() {
         for (auto& e : timer.events)
@@ -116,14 +121,16 @@ std::vector<Value> bind(CompiledRegion& region, const thb_abi_arg* args, std::ui
     }
     std::uint64_t reads = 0;
     if (hostMode) {
-        std::map<const void*, void*> uploaded;
+        // Host pointer -> (device copy, bytes copied). A later argument at the
+        // same address reuses the copy only when the copy covers all of it.
+        std::map<const void*, std::pair<void*, std::size_t>> uploaded;
         for (std::uint64_t i = 0; i < argc; ++i) {
             Value& v = values[i];
             if (!v.tensor) continue;
             const void* host = v.data;
             auto found = uploaded.find(host);
-            if (found != uploaded.end() && v.bytes()) {
-                v.data = found->second;
+            if (found != uploaded.end() && v.bytes() && v.bytes() <= found->second.second) {
+                v.data = found->second.first;
                 continue;
             }
             ++reads;
@@ -139,7 +146,7 @@ std::vector<Value> bind(CompiledRegion& region, const thb_abi_arg* args, std::ui
                 ev.host_to_device_bytes += v.bytes();
                 ++ev.input_storage_uploads;
             }
-            uploaded[host] = buffer.ptr;
+            if (v.bytes() > uploaded[host].second) uploaded[host] = {buffer.ptr, v.bytes()};
             v.data = buffer.ptr;
         }
     }
@@ -1014,6 +1021,12 @@ int thb_mlp_create(int device, uint64_t batch, uint64_t globalBatch, uint64_t in
         b.dw2 = static_cast<float*>(s->alloc(hidden * out * 4));
         b.lossPartials = static_cast<double*>(s->alloc(mlp::lossPartialCount(batch, out, info.smCount) * 8));
         b.lossSum = static_cast<double*>(s->alloc(8));
+        s->ownW[0] = b.w1;
+        s->ownW[1] = b.w2;
+        s->ownWb[0] = b.w1b;
+        s->ownWb[1] = b.w2b;
+        s->ownDw[0] = b.dw1;
+        s->ownDw[1] = b.dw2;
         *session = s.release();
         return THB_STATUS_OK;
     });
@@ -1210,9 +1223,25 @@ int thb_mlp_read_timing(thb_mlp* s, double* gemmMs, uint64_t* gemmLaunches) {
     return THB_STATUS_OK;
 }
 
+namespace {
+
+// Removes layer `layer`'s update binding, if any: the layer's W and bf16 W
+// return to the session's own buffers (the caller copies the weights in with
+// thb_mlp_set_weights), so the bound ones may be freed afterwards.
+void dropUpdate(thb_mlp* s, int layer) {
+    auto& r = layer == 0 ? s->b.dw1Reduce : s->b.dw2Reduce;
+    if (!r.update.paramPeers[0]) return;
+    (layer == 0 ? s->b.w1 : s->b.w2) = s->ownW[layer];
+    (layer == 0 ? s->b.w1b : s->b.w2b) = s->ownWb[layer];
+    r.update = thb::gemm::ReduceUpdate{};
+}
+
+} // namespace
+
 int thb_mlp_bind_reduction(thb_mlp* s, uint32_t which, void* const* peers, void* multicast, uint32_t* const* flagPeers,
                            uint32_t rank, uint32_t world) {
     if (!s || (which != THB_MLP_DW1 && which != THB_MLP_DW2)) return THB_STATUS_ABI;
+    const int layer = which == THB_MLP_DW1 ? 0 : 1;
     thb::gemm::AllReduce r;
     if (peers) {
         if (!flagPeers || world == 0 || world > static_cast<uint32_t>(thb::gemm::kMaxRanks) || rank >= world ||
@@ -1228,9 +1257,13 @@ int thb_mlp_bind_reduction(thb_mlp* s, uint32_t which, void* const* peers, void*
         r.cMulticast = multicast;
         r.rank = rank;
         r.world = world;
-        (which == THB_MLP_DW1 ? s->b.dw1 : s->b.dw2) = static_cast<float*>(peers[rank]);
     }
-    (which == THB_MLP_DW1 ? s->b.dw1Reduce : s->b.dw2Reduce) = r;
+    auto& bound = which == THB_MLP_DW1 ? s->b.dw1Reduce : s->b.dw2Reduce;
+    float*& dw = which == THB_MLP_DW1 ? s->b.dw1 : s->b.dw2;
+    dropUpdate(s, layer);
+    if (peers) dw = static_cast<float*>(peers[rank]);
+    else if (bound.cPeers[0]) dw = s->ownDw[layer];  // back to the local store
+    bound = r;
     s->reduceEpoch = 0;  // fresh (zeroed) signal words
     return THB_STATUS_OK;
 }
@@ -1239,8 +1272,12 @@ int thb_mlp_bind_update(thb_mlp* s, uint32_t which, float* const* paramPeers, vo
                         void* const* copyPeers, void* copyMulticast) {
     if (!s || (which != THB_MLP_W1 && which != THB_MLP_W2)) return THB_STATUS_ABI;
     auto& r = which == THB_MLP_W1 ? s->b.dw1Reduce : s->b.dw2Reduce;
+    if (!paramPeers) {
+        dropUpdate(s, which == THB_MLP_W1 ? 0 : 1);
+        return THB_STATUS_OK;
+    }
     thb::gemm::ReduceUpdate u;
-    if (paramPeers) {
+    {
         if (!r.cPeers[0] || !copyPeers) return THB_STATUS_ABI;
         if (!r.cMulticast != !paramMulticast || !paramMulticast != !copyMulticast) return THB_STATUS_ABI;
         if (reinterpret_cast<std::uintptr_t>(paramMulticast) % 16 || reinterpret_cast<std::uintptr_t>(copyMulticast) % 16)

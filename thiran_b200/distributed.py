@@ -119,7 +119,31 @@ class FusedGradientAllReduce:
                 torch.cuda.current_stream().synchronize()
                 self.flag_handle.barrier(channel=0, timeout_ms=self.BARRIER_TIMEOUT_MS)
         self.dist = dist
+        self.session = session
         self.bias_grads = bind_bias_gradients(session)
+
+    def close(self):
+        """Unbinds the session from the symmetric buffers, so that they can
+        be freed while the session lives on: dW returns to the session's own
+        buffers, and with `update` the current weights are copied back into
+        the session's own W1 and W2. Call it on every rank, between steps.
+        With `update` and momentum, each tile's velocity lives on its owner
+        rank only, so the velocities are not carried over: set_momentum
+        restarts them from zero before a step without the fused update."""
+        import torch
+        from . import MLP_DW1, MLP_DW2, MLP_W1, MLP_W2
+        if not self.available or self.session is None:
+            return
+        weights = [pair[0][0] for _, pair in self.param_handles]
+        for which, _ in self.param_handles:
+            self.session.bind_update(which, None, None)
+        for which in (MLP_DW1, MLP_DW2):
+            self.session.bind_reduction(which, None, None, 0, 1)
+        if weights:
+            stream = torch.cuda.current_stream()
+            self.session.set_weight_pointers(weights[0].data_ptr(), weights[1].data_ptr(), stream.cuda_stream)
+            stream.synchronize()
+        self.session = None
 
     def after_backward(self):
         """Wait until every rank's owned tiles hold their totals everywhere;
