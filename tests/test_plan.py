@@ -104,6 +104,38 @@ def test_malformed_regions_rejected_before_device(mutate, code):
     assert err.value.code == "GPU-INVALID-REGION"
 
 
+def _set_output(b, value):
+    b.output = value
+
+
+# The reference's manually built negative matrix over the region
+# [2,2] i64: Input 1, Input 2, Add 3 (NativeCpuTests.cpp:198-221), one
+# mutation per verifier rule.
+@pytest.mark.parametrize("mutate,code", [
+    (lambda b: b.nodes[1].update(id=1), "TRV01"),
+    (lambda b: b.nodes[2].update(deps=[1, 99]), "TRV02"),
+    (lambda b: b.nodes[2].update(deps=[1, 3]), "TRV03"),
+    (lambda b: b.nodes[2].update(shape=[]), "TRV04"),
+    (lambda b: b.nodes[1].update(shape=[2]), "TRV05"),
+    (lambda b: b.nodes[1].update(shape=[2, 3]), "TRV06"),
+    (lambda b: b.nodes[2].update(op=thb.OP_INDEX, deps=[1], indices=[]), "TRV07"),
+    (lambda b: b.nodes[2].update(op=thb.OP_INDEX, deps=[1], indices=[1, 2]), "TRV08"),
+    (lambda b: _set_output(b, 99), "TRV09"),
+    (lambda b: b.nodes[2].update(op=thb.OP_UNSUPPORTED), "TRV10"),
+])
+def test_reference_negative_matrix(mutate, code):
+    b = thb.RegionBuilder("manual")
+    x = b.input(thb.I64, [2, 2])
+    y = b.input(thb.I64, [2, 2])
+    b.add(x, y)
+    assert b.build(3).describe(thb.DESCRIBE_PLAN)[1][0] == 1  # the base verifies
+    mutate(b)
+    spec = b.build(b.output)
+    with pytest.raises(thb.GpuError) as err:
+        spec.describe(thb.DESCRIBE_PLAN)
+    assert err.value.code == "GPU-INVALID-REGION" and code in err.value.message, err.value.message
+
+
 def test_invalid_recipe_rejected():
     op = thb.Operation("bad", [(thb.SCALAR_INPUT, 0, 0, 0, 0.0), (thb.SCALAR_ADD, 0, 5, 0, 0.0)], root=1)
     b = thb.RegionBuilder("f")
@@ -123,3 +155,59 @@ def test_reductions_are_their_own_groups():
     spec = b.build(m)
     g, counts = groups(spec)
     assert g == [[2], [3], [4]] and counts[2] == 3
+
+
+def _engine_op_region(kind):
+    """A well-formed one-op region over the engine's lowered operations
+    (Sum, RowMax, Softmax, Transpose, MatMul, BroadcastToShape,
+    ReduceToShape, ZeroLike) and its result id."""
+    b = thb.RegionBuilder(kind)
+    a = b.input(thb.F32, [4, 6])
+    if kind == "sum":
+        r = b.sum(a, 1)
+    elif kind == "row_max":
+        r = b.row_max(a)
+    elif kind == "softmax":
+        r = b.softmax(a)
+    elif kind == "transpose":
+        r = b.transpose(a)
+    elif kind == "matmul":
+        r = b.matmul(a, b.input(thb.F32, [6, 3]))
+    elif kind == "broadcast":
+        r = b.broadcast_to_shape(b.input(thb.F32, [6]), a, 0)
+    elif kind == "reduce":
+        r = b.reduce_to_shape(a, b.input(thb.F32, [4, 1]))
+    else:
+        r = b.zero_like(a)
+    return b, r
+
+
+# One malformed variant per engine operation: each breaks the operation's
+# type or extent rule (axis range, rank, inner dimension, dtype).
+@pytest.mark.parametrize("kind,mutate", [
+    ("sum", lambda n: n.update(axis=2)),
+    ("sum", lambda n: n.update(shape=[5])),
+    ("row_max", lambda n: n.update(axis=0)),
+    ("softmax", lambda n: n.update(axis=0)),
+    ("transpose", lambda n: n.update(shape=[4, 6])),
+    ("matmul", lambda n: n.update(shape=[4, 4])),
+    ("broadcast", lambda n: n.update(axis=2)),
+    ("reduce", lambda n: n.update(shape=[4])),
+    ("zero_like", lambda n: n.update(dtype=thb.I64)),
+])
+def test_engine_operations_negative_matrix(kind, mutate):
+    b, r = _engine_op_region(kind)
+    assert b.build(r).describe(thb.DESCRIBE_PLAN)[1][0] >= 1  # the well-formed region verifies
+    mutate(b.nodes[r - 1])
+    with pytest.raises(thb.GpuError) as err:
+        b.build(r).describe(thb.DESCRIBE_PLAN)
+    assert err.value.code == "GPU-INVALID-REGION" and "TRV12" in err.value.message, err.value.message
+
+
+def test_matmul_inner_dimension_mismatch_rejected():
+    b = thb.RegionBuilder("mm")
+    x = b.input(thb.F32, [4, 6])
+    w = b.input(thb.F32, [5, 3])
+    with pytest.raises(thb.GpuError) as err:
+        b.build(b.matmul(x, w)).describe(thb.DESCRIBE_PLAN)
+    assert "TRV12 malformed MatMul" in err.value.message
