@@ -1276,24 +1276,22 @@ int thb_mlp_bind_update(thb_mlp* s, uint32_t which, float* const* paramPeers, vo
         dropUpdate(s, which == THB_MLP_W1 ? 0 : 1);
         return THB_STATUS_OK;
     }
+    if (!r.cPeers[0] || !copyPeers) return THB_STATUS_ABI;
+    if (!r.cMulticast != !paramMulticast || !paramMulticast != !copyMulticast) return THB_STATUS_ABI;
+    if (reinterpret_cast<std::uintptr_t>(paramMulticast) % 16 || reinterpret_cast<std::uintptr_t>(copyMulticast) % 16)
+        return THB_STATUS_ABI;
     thb::gemm::ReduceUpdate u;
-    {
-        if (!r.cPeers[0] || !copyPeers) return THB_STATUS_ABI;
-        if (!r.cMulticast != !paramMulticast || !paramMulticast != !copyMulticast) return THB_STATUS_ABI;
-        if (reinterpret_cast<std::uintptr_t>(paramMulticast) % 16 || reinterpret_cast<std::uintptr_t>(copyMulticast) % 16)
+    for (uint32_t k = 0; k < r.world; ++k) {
+        if (!paramPeers[k] || !copyPeers[k] || reinterpret_cast<std::uintptr_t>(paramPeers[k]) % 16 ||
+            reinterpret_cast<std::uintptr_t>(copyPeers[k]) % 16)
             return THB_STATUS_ABI;
-        for (uint32_t k = 0; k < r.world; ++k) {
-            if (!paramPeers[k] || !copyPeers[k] || reinterpret_cast<std::uintptr_t>(paramPeers[k]) % 16 ||
-                reinterpret_cast<std::uintptr_t>(copyPeers[k]) % 16)
-                return THB_STATUS_ABI;
-            u.paramPeers[k] = paramPeers[k];
-            u.copyPeers[k] = copyPeers[k];
-        }
-        u.paramMulticast = static_cast<float*>(paramMulticast);
-        u.copyMulticast = copyMulticast;
-        (which == THB_MLP_W1 ? s->b.w1 : s->b.w2) = paramPeers[r.rank];
-        (which == THB_MLP_W1 ? s->b.w1b : s->b.w2b) = copyPeers[r.rank];
+        u.paramPeers[k] = paramPeers[k];
+        u.copyPeers[k] = copyPeers[k];
     }
+    u.paramMulticast = static_cast<float*>(paramMulticast);
+    u.copyMulticast = copyMulticast;
+    (which == THB_MLP_W1 ? s->b.w1 : s->b.w2) = paramPeers[r.rank];
+    (which == THB_MLP_W1 ? s->b.w1b : s->b.w2b) = copyPeers[r.rank];
     r.update = u;
     return THB_STATUS_OK;
 }
