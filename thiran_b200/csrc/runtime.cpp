@@ -77,6 +77,11 @@ DeviceBuffer::~DeviceBuffer() {
 
 bool DeviceBuffer::reserve(std::size_t want, int ordinal) {
     if (ptr && bytes >= want) return false;
+    // The buffer lands on `ordinal` whatever the calling thread's current
+    // device is; that device is restored afterwards.
+    int previous = -1;
+    cudaGetDevice(&previous);
+    if (previous != ordinal) check(cudaSetDevice(ordinal), "cudaSetDevice");
     if (ptr) {
         cudaFree(ptr);
         ptr = nullptr;
@@ -84,7 +89,13 @@ bool DeviceBuffer::reserve(std::size_t want, int ordinal) {
     }
     device = ordinal;
     const std::size_t rounded = std::max<std::size_t>(256, (want + 255) / 256 * 256);
-    check(cudaMalloc(&ptr, rounded), "cudaMalloc");
+    const cudaError_t e = cudaMalloc(&ptr, rounded);
+    if (previous >= 0 && previous != ordinal) cudaSetDevice(previous);
+    if (e != cudaSuccess) {
+        ptr = nullptr;
+        cudaGetLastError();  // an allocation failure is not left for a later launch check
+    }
+    check(e, "cudaMalloc");
     bytes = rounded;
     return true;
 }
