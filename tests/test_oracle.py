@@ -274,3 +274,55 @@ def test_renderer_failure_ids():
     with pytest.raises(orc.OracleFailure) as err:
         g.perspective(np.float32(0), 1, np.float32(.1), 100)
     assert err.value.code == "TH019-PROJECTION"
+
+
+def _training_fixture_regions():
+    """The reference's bounded training fixture (docs/spec/TRAINING_V0.md,
+    "Determinism and fixture"): prediction = x * weight + bias, loss = the
+    sum of squared errors, as a loss region and a region per parameter
+    gradient. The gradient regions follow the reverse rules the reference's
+    Autodiff.cpp emits for them: Mul -> cot*e + e*cot (2e with cot = 1),
+    bias -> ReduceToShape, MatMul -> Transpose(x) . cot."""
+    def forward(b):
+        x = b.input(thb.F32, [4, 1])
+        w = b.input(thb.F32, [1, 1])
+        bias = b.input(thb.F32, [1])
+        t = b.input(thb.F32, [4, 1])
+        xw = b.matmul(x, w)
+        e = b.sub(b.add(xw, b.broadcast_to_shape(bias, xw, 0)), t)
+        return x, bias, e
+
+    lb = thb.RegionBuilder("loss")
+    _, _, e = forward(lb)
+    loss = lb.build(lb.sum(lb.sum(lb.mul(e, e), 1), 0))
+    gb = thb.RegionBuilder("dbias")
+    _, bias, e = forward(gb)
+    dbias = gb.build(gb.reduce_to_shape(gb.add(e, e), bias))
+    gw = thb.RegionBuilder("dweight")
+    x, _, e = forward(gw)
+    dweight = gw.build(gw.matmul(gw.transpose(x), gw.add(e, e)))
+    return loss, dbias, dweight
+
+
+def test_training_fixture_known_answers():
+    """Loss 84, dLoss/dbias = [-32], dLoss/dweight = [[-68]] at the initial
+    state; one plain SGD step at lr 0.02 gives bias 0.64, weight 1.36; 200
+    full-batch steps end within 0.001 of bias 1, weight 2 (the reference's
+    predeclared convergence run)."""
+    loss, dbias, dweight = _training_fixture_regions()
+    x = np.array([[0], [1], [2], [3]], np.float32)
+    t = np.array([[1], [3], [5], [7]], np.float32)
+    p = np.zeros(2, np.float32)  # plan order [bias, weight]
+
+    def state():
+        return [x, p[1:2].reshape(1, 1).copy(), p[0:1].copy(), t]
+
+    assert orc.region_eval(loss, state()) == 84.0
+    g = np.array([orc.region_eval(dbias, state())[0], orc.region_eval(dweight, state())[0, 0]], np.float32)
+    assert g.tolist() == [-32.0, -68.0]
+    orc.sgd_update(p, g, 0.02)
+    np.testing.assert_allclose(p, [0.64, 1.36], rtol=0, atol=1e-6)
+    for _ in range(199):
+        g = np.array([orc.region_eval(dbias, state())[0], orc.region_eval(dweight, state())[0, 0]], np.float32)
+        orc.sgd_update(p, g, 0.02)
+    np.testing.assert_allclose(p, [1.0, 2.0], rtol=0, atol=1e-3)
