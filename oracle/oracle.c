@@ -188,6 +188,19 @@ static void column_sums(const float* m, float* out, uint64_t rows, uint64_t cols
     }
 }
 
+uint64_t orc_fnv1a64_f32(const float* values, uint64_t n, uint64_t basis) {
+    uint64_t hash = basis;
+    for (uint64_t k = 0; k < n; ++k) {
+        uint32_t bits;
+        memcpy(&bits, &values[k], 4);
+        for (unsigned shift = 0; shift < 32; shift += 8) {
+            hash ^= (uint8_t)(bits >> shift);
+            hash *= 1099511628211ULL;
+        }
+    }
+    return hash;
+}
+
 void orc_sgd_update(float* p, const float* g, float* v, float mu, float lr, uint64_t n) {
     for (uint64_t k = 0; k < n; ++k) {
         float d = g[k];

@@ -80,6 +80,12 @@ double orc_mlp_step(const float* x, const float* t, float* w1, float* w2, uint64
  * (SGD); then p = p - d*lr. Each operation rounds to f32. */
 void orc_sgd_update(float* p, const float* g, float* v, float mu, float lr, uint64_t n);
 
+/* FNV-1a over the little-endian bytes of n f32 bit patterns, starting from
+ * `basis`: the reference's output digests (benchmarks/th023/
+ * Qualification.cpp:176-187 starts from 1469598103934665603,
+ * src/graphics/v0/Graphics.cpp:188-200 from 14695981039346656037). */
+uint64_t orc_fnv1a64_f32(const float* values, uint64_t n, uint64_t basis);
+
 /* The same step with the optional parts of the examples/mlp.th structure and
  * the reference optimizer:
  *   biases (b1 [h], b2 [o], broadcast over rows, Evaluator.cpp:95-124):

@@ -32,6 +32,8 @@ _lib.orc_round_bf16.argtypes = [_f32p, _f32p, C.c_uint64]
 _lib.orc_mlp_step.restype = C.c_double
 _lib.orc_mlp_step.argtypes = [_f32p, _f32p, _f32p, _f32p, C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64, C.c_float,
                               _f32p, _f32p, _f32p, _f32p]
+_lib.orc_fnv1a64_f32.restype = C.c_uint64
+_lib.orc_fnv1a64_f32.argtypes = [_f32p, C.c_uint64, C.c_uint64]
 _lib.orc_sgd_update.restype = None
 _lib.orc_sgd_update.argtypes = [_f32p, _f32p, C.c_void_p, C.c_float, C.c_float, C.c_uint64]
 
@@ -193,12 +195,12 @@ def render(positions, indices, colors, model, view, projection, width, height, c
     return color, depth, stats
 
 
-def fnv_floats(values):
-    """The reference's framebuffer digest (Graphics.cpp:188-200)."""
-    h = 14695981039346656037
-    for byte in np.ascontiguousarray(values, np.float32).tobytes():
-        h = ((h ^ byte) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
-    return f"fnv1a64:{h:016x}"
+def fnv_floats(values, basis=14695981039346656037):
+    """The reference's f32 digests: the framebuffer digest (Graphics.cpp:
+    188-200) with the default basis; the qualification output digest
+    (benchmarks/th023/Qualification.cpp:176-187) with 1469598103934665603."""
+    flat = np.ascontiguousarray(values, np.float32).reshape(-1)
+    return f"fnv1a64:{_lib.orc_fnv1a64_f32(flat, flat.size, basis):016x}"
 
 
 def sgd_update(p, g, lr, v=None, momentum=0.0):

@@ -326,3 +326,38 @@ def test_training_fixture_known_answers():
         g = np.array([orc.region_eval(dbias, state())[0], orc.region_eval(dweight, state())[0, 0]], np.float32)
         orc.sgd_update(p, g, 0.02)
     np.testing.assert_allclose(p, [1.0, 2.0], rtol=0, atol=1e-3)
+
+
+def _qualification_inputs(n):
+    """The reference's deterministic qualification inputs
+    (docs/spec/PERFORMANCE_QUALIFICATION_V0.md, "Deterministic inputs"):
+    x[i] = f32((i*17) % 1009 - 504) / f32(37),
+    y[i] = f32((i*29 + 11) % 1013 - 506) / f32(41)."""
+    i = np.arange(n, dtype=np.int64)
+    x = ((i * 17) % 1009 - 504).astype(np.float32) / np.float32(37)
+    y = ((i * 29 + 11) % 1013 - 506).astype(np.float32) / np.float32(41)
+    return x, y
+
+
+def _qualification_chain():
+    """Workload A: a = x + y; b = -a; c = b .* y; d = c - x; e = d .* y."""
+    b = thb.RegionBuilder("elementwise_chain")
+    x = b.input(thb.F32, [None])
+    y = b.input(thb.F32, [None])
+    c = b.mul(b.neg(b.add(x, y)), y)
+    return b.build(b.mul(b.sub(c, x), y))
+
+
+# Input and output digests the reference recorded for its fused CPU chain
+# (benchmarks/results/TH-023-machine.json, elementwise_chain, thiran_fused).
+@pytest.mark.parametrize("n,input_digest,output_digest", [
+    (1 << 10, "fnv1a64:361d96caefeb88fd", "fnv1a64:61261595fdc3d150"),
+    (1 << 20, "fnv1a64:f2764d4c05bf9a50", "fnv1a64:32dc138129eebb43"),
+    (1 << 24, "fnv1a64:9c44e6d000b9f1cf", "fnv1a64:03e29fd051c79b66"),
+])
+def test_qualification_chain_digests(n, input_digest, output_digest):
+    basis = 1469598103934665603
+    x, y = _qualification_inputs(n)
+    assert orc.fnv_floats(np.concatenate([x, y]), basis) == input_digest
+    e = orc.region_eval(_qualification_chain(), [x, y])
+    assert orc.fnv_floats(e, basis) == output_digest
