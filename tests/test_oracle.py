@@ -361,3 +361,39 @@ def test_qualification_chain_digests(n, input_digest, output_digest):
     assert orc.fnv_floats(np.concatenate([x, y]), basis) == input_digest
     e = orc.region_eval(_qualification_chain(), [x, y])
     assert orc.fnv_floats(e, basis) == output_digest
+
+
+def _qualification_extension(builtin):
+    """Workload B: a = -x; b = research_square_linear(a) (a*a + a), or its
+    built-in equivalent s = a .* a; b = s + a; then c = b + y."""
+    b = thb.RegionBuilder("generic_extension")
+    x = b.input(thb.F32, [None])
+    y = b.input(thb.F32, [None])
+    a = b.neg(x)
+    sq = b.add(b.mul(a, a), a) if builtin else b.extension(regions.square_linear_operation(), a)
+    return b.build(b.add(sq, y))
+
+
+def _qualification_barrier():
+    """Workload C: a = x + y; b = -a; c = a .* y; d = b + c; e = d - x
+    (`a` has two consumers and materialises)."""
+    b = thb.RegionBuilder("planned")
+    x = b.input(thb.F32, [None])
+    y = b.input(thb.F32, [None])
+    a = b.add(x, y)
+    d = b.add(b.neg(a), b.mul(a, y))
+    return b.build(b.sub(d, x))
+
+
+# Output digests the reference recorded at 2^20 for workloads B
+# (generic_extension; its built-in equivalent must agree bit for bit) and C
+# (thiran_planned), benchmarks/results/TH-023-machine.json.
+@pytest.mark.parametrize("spec,output_digest", [
+    (lambda: _qualification_extension(False), "fnv1a64:726e0e9b047863a9"),
+    (lambda: _qualification_extension(True), "fnv1a64:726e0e9b047863a9"),
+    (_qualification_barrier, "fnv1a64:eacc3ead55e92def"),
+])
+def test_qualification_workload_digests(spec, output_digest):
+    x, y = _qualification_inputs(1 << 20)
+    e = orc.region_eval(spec(), [x, y])
+    assert orc.fnv_floats(e, 1469598103934665603) == output_digest
