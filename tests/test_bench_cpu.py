@@ -1,0 +1,27 @@
+"""The benchmark's reference arm runs on host cores only: its JSON line keeps
+the contract (one line, the engine arm's metric and unit, a cpu_baseline and
+an e2e record without transfers)."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.mark.parametrize("workload,unit", [("i64_region", "GB/s"), ("mlp", "TFLOP/s")])
+def test_reference_arm_line(workload, unit):
+    out = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "0",
+                          "--workload", workload], cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    line = json.loads(lines[-1])
+    assert line["impl"] == "reference" and line["unit"] == unit and line["value"] > 0
+    assert line["higher_is_better"] is True and line["n_gpus"] == 1 and line["steps"] == 1
+    assert line["cpu_baseline"]["unit"] == unit and line["cpu_baseline"]["cores"] >= 1
+    assert line["cpu_baseline"]["kind"] in ("reference", "port")
+    assert line["e2e"] == {"value": line["value"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert "workload" in line["config"]
