@@ -485,12 +485,15 @@ def time_cpu(workload, threads, rows_per_thread, repeats):
         sys.path.insert(0, os.path.join(ROOT, "tests"))
         import oracle_lib
         from thiran_b200 import regions
-        spec = regions.i64_region() if workload.name == "i64_region" else regions.f32_chain() \
-            if workload.name == "f32_chain" else regions.softmax_rows()
+        spec = {"i64_region": regions.i64_region, "f32_chain": regions.f32_chain, "softmax": regions.softmax_rows,
+                "sum": regions.full_sum}[workload.name]()
         kind = "port"
 
         def fn_port(inputs, out):
-            out[...] = oracle_lib.region_eval(spec, inputs)
+            if workload.name == "sum":  # the full sum of the flattened rows (a scalar result)
+                oracle_lib.region_eval(spec, [inputs[0].reshape(-1)])
+            else:
+                out[...] = oracle_lib.region_eval(spec, inputs)
     work = [cpu_inputs(workload, rows_per_thread) for _ in range(threads)]
     elements = sum(o.size for _, o in work)
 
@@ -550,7 +553,9 @@ def reference_arm(args, workload):
                 values.append(tflops)
         kind, cores, unit = "port", 1, "TFLOP/s"
     elif reference_entry(workload) is None:
-        gbs, kind, sample, _ = time_cpu(workload, 1, rows, args.steps)
+        # No native CPU region in the reference (its Evaluator interprets
+        # these): the oracle port, 2048 rows per call.
+        gbs, kind, sample, _ = time_cpu(workload, 1, 2048, args.steps)
         values = [gbs]
         cores = 1
     else:

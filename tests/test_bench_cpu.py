@@ -11,7 +11,8 @@ import pytest
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-@pytest.mark.parametrize("workload,unit", [("i64_region", "GB/s"), ("mlp", "TFLOP/s")])
+@pytest.mark.parametrize("workload,unit", [("i64_region", "GB/s"), ("f32_chain", "GB/s"), ("softmax", "GB/s"),
+                                           ("sum", "GB/s"), ("mlp", "TFLOP/s")])
 def test_reference_arm_line(workload, unit):
     out = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "0",
                           "--workload", workload], cwd=ROOT, capture_output=True, text=True, timeout=600)
