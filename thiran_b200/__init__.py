@@ -688,7 +688,7 @@ def _device_args(tensors) -> tuple:
             a.reserved = 0 if t.is_contiguous() else 1
             a.shape, a.data, a.count = shape, t.data_ptr() or None, t.numel()
         else:
-            is_int = isinstance(t, (int, np.integer))
+            is_int = isinstance(t, (int, np.integer)) and not isinstance(t, bool)
             scalar = C.c_int64(int(t)) if is_int else C.c_float(float(t))
             keep.append(scalar)
             a.kind, a.dtype, a.rank = KIND_SCALAR, I64 if is_int else F32, 0
