@@ -129,7 +129,9 @@ class FusedGradientAllReduce:
         the session's own W1 and W2. Call it on every rank, between steps.
         With `update` and momentum, each tile's velocity lives on its owner
         rank only, so the velocities are not carried over: set_momentum
-        restarts them from zero before a step without the fused update."""
+        restarts them from zero before a step without the fused update.
+        The bias gradients stay bound to `self.bias_grads` (an ordinary
+        device tensor), which must outlive the session's later steps."""
         import torch
         from . import MLP_DW1, MLP_DW2, MLP_W1, MLP_W2
         if not self.available or self.session is None:
