@@ -9,8 +9,10 @@
  * Pinning: oracle/ref_driver.cpp compiles the reference's own Evaluator and
  * NativeCpu emitter from its sources (oracle/Makefile) and
  * tests/golden/make_golden.py records their outputs as fixtures; the CPU test
- * suite checks this restatement against those fixtures and against the
- * known-answer vectors of the reference's tests.
+ * suite checks this restatement against those fixtures, against the
+ * known-answer vectors of the reference's tests, and against the output
+ * digests the reference recorded in its qualification run
+ * (benchmarks/results/TH-023-machine.json).
  */
 #ifndef THIRAN_ORACLE_H
 #define THIRAN_ORACLE_H
