@@ -727,7 +727,7 @@ def main():
 
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rows = 1024 if workload.name == "i64_region" else 128
+        rows = {"i64_region": 1024, "f32_chain": 128}.get(workload.name, 2048)
         gbs, kind, sample, _ = time_cpu(workload, 1, rows, 2)
         cpu_baseline = {"value": gbs, "unit": "GB/s", "cores": 1, "kind": kind,
                         "sample": f"{sample}; the reference CPU path is single-threaded"}
