@@ -71,8 +71,12 @@ enum {
      *   EXTENSION_GRADIENT: deps = primal operands..., primal result, output
      *     cotangent; axis = operand index k; evaluates the descriptor's
      *     gradient recipe k elementwise (Autodiff.cpp:231-270);
-     *   TRANSPOSE (Evaluator.cpp:200-213); MATMUL (Evaluator.cpp:125-154),
-     *     f32 operands computed as bf16 x bf16 -> f32 on the tensor cores;
+     *   TRANSPOSE (Evaluator.cpp:200-213); MATMUL (Evaluator.cpp:125-154):
+     *     i64 operands with checked multiply and add (TH-SPEC-I64-OVERFLOW);
+     *     f32 operands by node.axis: THB_MATMUL_TENSOR computes bf16 x bf16
+     *     -> f32 on the tensor cores (any K and N: operands are zero-padded
+     *     to 16-byte rows), THB_MATMUL_EXACT the Evaluator's sequential,
+     *     separately rounded f32 sums on the CUDA cores (bit-exact);
      *   BROADCAST_TO_SHAPE: deps = value, reference; axis (Evaluator.cpp:278-309);
      *   REDUCE_TO_SHAPE: deps = value, reference (Evaluator.cpp:258-277);
      *   ZERO_LIKE: deps = reference. */
@@ -83,6 +87,9 @@ enum {
     THB_OP_REDUCE_TO_SHAPE = 40,
     THB_OP_ZERO_LIKE = 41
 };
+
+/* MatMul modes of f32 operands (node.axis of a THB_OP_MATMUL node). */
+enum { THB_MATMUL_TENSOR = 0, THB_MATMUL_EXACT = 1 };
 
 /* Scalar recipe opcodes (include/extension/v0/Extension.hpp:16-17). */
 enum {
@@ -591,12 +598,19 @@ int thb_region_describe(const thb_region_desc* region, thb_plan_options options,
  * loading the library holds until exit; a reduction needing more partials
  * than that is rejected with GPU-NOALLOC-SIZE (on a B200 the sum uses at most
  * 4 x 148 = 592). Nothing is allocated: the first call on a device resolves
- * the scratch's device address once (make that first call before any stream
- * capture). Every call shares the one scratch array, and each call writes
- * every partial it later reads, so nothing needs clearing; calls that overlap
- * on the GPU (different streams, or different host threads on one device)
- * race on the scratch and must be serialised by the caller. Results are
- * identical to the region Sum path (same kernels, same grid). */
+ * the device addresses of the scratch and of a static status word once (make
+ * that first call before any stream capture; a host that resets the device
+ * with cudaDeviceReset after it must not call this entry point again). Every
+ * call shares the one scratch array, and each call writes every partial it
+ * later reads, so the partials need no clearing; the status word is cleared
+ * by each call before its launches. The call waits for `stream` and reads the
+ * status word before it returns: a bounded wait that ran out on the device
+ * returns THB_STATUS_BACKEND with GPU-KERNEL-TIMEOUT (or
+ * GPU-KERNEL-DRAIN-TIMEOUT) and the outputs are then invalid. Calls that
+ * overlap on the GPU (different streams, or different host threads on one
+ * device) race on the scratch and the status word and must be serialised by
+ * the caller. Results are identical to the region Sum path (same kernels,
+ * same grid). */
 int thb_sum_all_f32_noalloc(int device, const float* x, uint64_t n, float* out_f32, double* out_f64,
                             void* stream, char* failure, uint64_t failure_cap);
 

@@ -140,6 +140,22 @@ void orc_matmul_f32(const float* a, const float* b, float* c, uint64_t m, uint64
         }
 }
 
+int orc_matmul_i64(const int64_t* a, const int64_t* b, int64_t* c, uint64_t m, uint64_t k, uint64_t n) {
+    /* Evaluator.cpp:143-153: acc = checked(acc + checked(a * b)), k in order;
+     * returns 1 at the first overflow (the reference fails there). */
+    for (uint64_t i = 0; i < m; ++i)
+        for (uint64_t j = 0; j < n; ++j) {
+            int64_t acc = 0;
+            for (uint64_t p = 0; p < k; ++p) {
+                int64_t product;
+                if (__builtin_mul_overflow(a[i * k + p], b[p * n + j], &product)) return 1;
+                if (__builtin_add_overflow(acc, product, &acc)) return 1;
+            }
+            c[i * n + j] = acc;
+        }
+    return 0;
+}
+
 void orc_matmul_f64acc(const float* a, const float* b, float* c, uint64_t m, uint64_t k, uint64_t n) {
     double* row = (double*)malloc(sizeof(double) * (n ? n : 1));
     for (uint64_t i = 0; i < m; ++i) {
@@ -384,15 +400,24 @@ int orc_region_eval(const thb_region_desc* r, const thb_abi_arg* args, uint64_t 
             break;
         }
         case THB_OP_MATMUL: {
-            /* Evaluator.cpp:125-154: sequential-k f32, each op rounded */
+            /* Evaluator.cpp:125-154: sequential-k f32, each op rounded; i64
+             * with checked multiply and add (any overflow fails the call) */
             const value_t* d1 = &vals[position_of(r, n->dependencies[1])];
             v->shape[0] = d0->shape[0];
             v->shape[1] = d1->shape[1];
             v->count = v->shape[0] * v->shape[1];
-            v->data = malloc(4 * (v->count ? v->count : 1));
+            v->data = malloc(8 * (v->count ? v->count : 1));
             v->owned = 1;
-            orc_matmul_f32((const float*)d0->data, (const float*)d1->data, (float*)v->data, d0->shape[0], d0->shape[1],
-                           d1->shape[1]);
+            if (n->dtype == THB_DTYPE_I64) {
+                if (orc_matmul_i64((const int64_t*)d0->data, (const int64_t*)d1->data, (int64_t*)v->data,
+                                   d0->shape[0], d0->shape[1], d1->shape[1])) {
+                    set_failure(failure, cap, "TH-SPEC-I64-OVERFLOW");
+                    status = 2;
+                }
+            } else {
+                orc_matmul_f32((const float*)d0->data, (const float*)d1->data, (float*)v->data, d0->shape[0],
+                               d0->shape[1], d1->shape[1]);
+            }
             break;
         }
         case THB_OP_BROADCAST_TO_SHAPE: {

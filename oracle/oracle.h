@@ -56,6 +56,9 @@ float orc_sum_all_sequential_f32(const float* x, uint64_t n);
  * (i, j), acc = 0.0f; acc = acc + a[i,k] * b[k,j] over k in order, every
  * product and sum rounded to f32. a: [m,k] row-major, b: [k,n] row-major. */
 void orc_matmul_f32(const float* a, const float* b, float* c, uint64_t m, uint64_t k, uint64_t n);
+/* The i64 rule (Evaluator.cpp:143-153): checked multiply and add in the same
+ * order; returns 1 at the first overflow (TH-SPEC-I64-OVERFLOW), else 0. */
+int orc_matmul_i64(const int64_t* a, const int64_t* b, int64_t* c, uint64_t m, uint64_t k, uint64_t n);
 /* Same product accumulated in f64 and rounded once (used at sizes where the
  * sequential f32 order itself carries more error than the gate). */
 void orc_matmul_f64acc(const float* a, const float* b, float* c, uint64_t m, uint64_t k, uint64_t n);

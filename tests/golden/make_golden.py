@@ -151,6 +151,7 @@ fn cols(A: Tensor<f32,2>) -> Tensor<f32,1> { return sum(A, 0) }
 fn total(A: Tensor<f32,2>) -> f32 { return sum(sum(A, 1), 0) }
 """
 MATMUL = "fn mm(A: Tensor<f32,2>, B: Tensor<f32,2>) -> Tensor<f32,2> { return A * B }"
+MATMUL_I64 = "fn mm(A: Tensor<i64,2>, B: Tensor<i64,2>) -> Tensor<i64,2> { return A * B }"
 LINEAR_LOSS = """fn loss(x: Tensor<f32,2>, w1: Tensor<f32,2>, w2: Tensor<f32,2>, t: Tensor<f32,2>) -> f32 {
 let h = x * w1
 let y = h * w2
@@ -251,6 +252,23 @@ def main():
     mb = rng.standard_normal((32, 24)).astype(np.float32)
     status, value = evaluate(MATMUL, "mm", [ma, mb])
     arrays["mm_a"], arrays["mm_b"], arrays["mm_out"] = ma, mb, value
+    # Shapes whose K and N are not multiples of 8 (examples/transformer.th
+    # multiplies [2,4] by [4,4], [4,2] and [2,8]), and the i64 rule with its
+    # overflow failure.
+    oa = rng.standard_normal((37, 13)).astype(np.float32)
+    ob = rng.standard_normal((13, 5)).astype(np.float32)
+    status, value = evaluate(MATMUL, "mm", [oa, ob])
+    arrays["mm_odd_a"], arrays["mm_odd_b"], arrays["mm_odd_out"] = oa, ob, value
+    ia = rng.integers(-1000, 1001, (33, 70), dtype=np.int64)
+    ib = rng.integers(-1000, 1001, (70, 19), dtype=np.int64)
+    status, value = evaluate(MATMUL_I64, "mm", [ia, ib])
+    arrays["mm_i64_a"], arrays["mm_i64_b"], arrays["mm_i64_out"] = ia, ib, value
+    half = np.array([[1 << 62, 1 << 62]], np.int64)  # products fit, their sum is 2^63
+    status, _ = evaluate(MATMUL_I64, "mm", [half, np.array([[1], [1]], np.int64)])
+    fixtures["mm_i64_sum_overflow"] = status
+    root = np.array([[3037000500]], np.int64)  # 3037000500^2 > INT64_MAX
+    status, _ = evaluate(MATMUL_I64, "mm", [root, root])
+    fixtures["mm_i64_product_overflow"] = status
 
     # Reverse mode (src/autodiff/v0/Autodiff.cpp): extension gradient recipes
     # and the matmul / sum / broadcast rules of a linear two-layer loss.
@@ -339,6 +357,9 @@ def main():
             arrays[f"gfx_{name}_stats"] = np.array(status["stats"], np.uint64)
 
     np.savez_compressed(os.path.join(HERE, "reference_outputs.npz"), **arrays)
+    with open(os.path.join(HERE, "reference_fixtures.json"), "w") as f:
+        json.dump(fixtures, f, indent=1, sort_keys=True)
+    print("wrote", len(arrays), "arrays and", len(fixtures), "fixtures")
 
 
 def graphics_scenes():
@@ -375,9 +396,6 @@ def graphics_scenes():
         projection=g.orthographic(-1.2, 1.2, -1, 1, 0, 1).reshape(4, 4),
         width=97, height=81)
     return scenes
-    with open(os.path.join(HERE, "reference_fixtures.json"), "w") as f:
-        json.dump(fixtures, f, indent=1, sort_keys=True)
-    print("wrote", len(arrays), "arrays and", len(fixtures), "fixtures")
 
 
 if __name__ == "__main__":

@@ -2,7 +2,9 @@
 data-parallel MLP steps whose gradient all-reduce is fused into the
 weight-gradient GEMMs (peer loads/stores or in-switch reduction over NVLink)
 or done by NCCL after the backward pass equal the single-process full-batch
-step, at 2, 4 and 8 ranks. Each test runs spawned ranks over NCCL."""
+step and follow the oracle's full-batch step (biases, SGD with momentum), at
+2, 4 and 8 ranks; unbinding the fused all-reduce (close()) returns the
+session to its own buffers. Each test runs spawned ranks over NCCL."""
 import os
 import socket
 
@@ -95,9 +97,23 @@ def _mlp_rank(rank, world, port, mode, out_path):
         s.apply_sgd(LR)
     thb.check_device_status(rank)
     torch.cuda.synchronize()
+    results = dict(dw1=dw1.cpu().numpy(), dw2=dw2.cpu().numpy(), dbias=dbias.cpu().numpy(),
+                   **{k: v.cpu().numpy() for k, v in params.items()})
+    if mc:
+        # Unbind between steps: dW returns to the session's own buffers, so a
+        # further (local, unreduced) backward pass leaves the symmetric
+        # buffers untouched.
+        sym = [dw1.clone(), dw2.clone()]
+        mc.close()
+        own = [s.buffer(thb.MLP_DW1)[0], s.buffer(thb.MLP_DW2)[0]]
+        results["unbound"] = np.array(own[0] != dw1.data_ptr() and own[1] != dw2.data_ptr())
+        s.forward_backward(xs, ts)
+        thb.check_device_status(rank)
+        torch.cuda.synchronize()
+        results["untouched"] = np.array(torch.equal(sym[0], dw1) and torch.equal(sym[1], dw2))
+        dist.barrier()
     if rank == 0:
-        np.savez(out_path, dw1=dw1.cpu().numpy(), dw2=dw2.cpu().numpy(), dbias=dbias.cpu().numpy(),
-                 **{k: v.cpu().numpy() for k, v in params.items()})
+        np.savez(out_path, **results)
     s.release()
     dist.barrier()
     dist.destroy_process_group()
@@ -118,6 +134,15 @@ def single_gpu_reference():
     torch.cuda.synchronize()
     return dict(dw1=dw1.cpu().numpy(), dw2=dw2.cpu().numpy(), dbias=dbias.cpu().numpy(),
                 **{k: v.cpu().numpy() for k, v in params.items()})
+
+
+def _device_tensor(ptr, like):
+    """A torch view of `like.numel()` f32 values at device address `ptr`
+    (through the CUDA array interface; the memory stays the session's)."""
+    class _Mem:
+        __cuda_array_interface__ = {"shape": tuple(like.shape), "typestr": "<f4", "data": (ptr, False),
+                                    "version": 3, "strides": None}
+    return torch.as_tensor(_Mem(), device="cuda")
 
 
 def rel(a, b):
@@ -142,6 +167,23 @@ def test_data_parallel_mlp_matches_full_batch(tmp_path, mode, world):
         assert rel(got[k], ref[k]) <= 1e-2, k
     for k in ("w1", "w2", "b1", "b2"):
         assert rel(got[k], ref[k]) <= 1e-4, k
+    # The oracle's full-batch step (the bound of the single-GPU oracle test).
+    orc = oracle_steps()
+    for k in ("w1", "w2", "b1", "b2"):
+        assert rel(got[k], orc[k]) <= 1e-3, k
+    if mode != "nccl":
+        assert bool(got["unbound"]) and bool(got["untouched"])
+
+
+def oracle_steps():
+    """Three full-batch steps of the oracle (biases, SGD with momentum)."""
+    import oracle_lib
+    x, t, w1, w2, b1, b2 = problem()
+    ws = [w1.copy(), w2.copy(), b1.copy(), b2.copy()]
+    vel = [np.zeros_like(a) for a in (w1, b1, w2, b2)]
+    for _ in range(3):
+        oracle_lib.mlp_step_ex(x, t, ws[0], ws[1], LR, ws[2], ws[3], MOMENTUM, vel)
+    return dict(w1=ws[0], w2=ws[1], b1=ws[2], b2=ws[3])
 
 
 def _update_rank(rank, world, port, mode, out_path):
@@ -196,6 +238,17 @@ def _update_rank(rank, world, port, mode, out_path):
                 dist.all_gather(gathered, w)
                 results[f"ranks_equal_w{k + 1}"] = np.array(all(torch.equal(g, w) for g in gathered))
                 results[f"copy_matches_w{k + 1}"] = np.array(torch.equal(c, w.to(torch.bfloat16)))
+            # close(): W1 and W2 move back into the session's own buffers
+            # with the current values.
+            current = [w.clone() for w in weights]
+            mc.close()
+            own = [s.buffer(thb.MLP_W1)[0], s.buffer(thb.MLP_W2)[0]]
+            restored = all(p != w.data_ptr() for p, w in zip(own, weights))
+            for p, w in zip(own, current):
+                view = torch.empty_like(w)
+                view.copy_(_device_tensor(p, w))
+                restored = restored and torch.equal(view, w)
+            results["closed_restores_weights"] = np.array(restored)
         dist.barrier()
         s.release()
     if rank == 0:
@@ -223,6 +276,7 @@ def test_update_fused_into_the_all_reduce(tmp_path, mode, world):
         assert np.array_equal(got[f"fused_{k}"].view(np.uint32), got[f"plain_{k}"].view(np.uint32)), k
     for k in ("1", "2"):
         assert bool(got[f"ranks_equal_w{k}"]) and bool(got[f"copy_matches_w{k}"]), k
+    assert bool(got["closed_restores_weights"])
     ref = single_gpu_reference()
     for k in ("w1", "w2", "b1", "b2"):
         assert rel(got[f"fused_{k}"], ref[k]) <= 1e-4, k

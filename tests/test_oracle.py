@@ -99,6 +99,21 @@ def test_sums_against_reference_evaluator(golden):
 def test_matmul_evaluator_order_bitwise(golden):
     out = orc.matmul_f32(golden["mm_a"], golden["mm_b"])
     assert out.view(np.uint32).tolist() == golden["mm_out"].view(np.uint32).tolist()
+    odd = orc.region_eval(regions.matmul(thb.F32, exact=True), [golden["mm_odd_a"], golden["mm_odd_b"]])
+    assert odd.view(np.uint32).tolist() == golden["mm_odd_out"].view(np.uint32).tolist()
+
+
+def test_matmul_i64_checked_against_reference(golden, fixtures):
+    spec = regions.matmul(thb.I64)
+    out = orc.region_eval(spec, [golden["mm_i64_a"], golden["mm_i64_b"]])
+    np.testing.assert_array_equal(out, golden["mm_i64_out"])
+    half = np.array([[1 << 62, 1 << 62]], np.int64)
+    root = np.array([[3037000500]], np.int64)
+    for key, (a, b) in (("mm_i64_sum_overflow", (half, np.array([[1], [1]], np.int64))),
+                        ("mm_i64_product_overflow", (root, root))):
+        with pytest.raises(orc.OracleFailure) as err:
+            orc.region_eval(spec, [a, b])
+        assert err.value.code == fixtures[key] == "TH-SPEC-I64-OVERFLOW"
 
 
 def test_softmax_restatement_against_numpy():

@@ -191,6 +191,8 @@ def _engine_op_region(kind):
     ("softmax", lambda n: n.update(axis=0)),
     ("transpose", lambda n: n.update(shape=[4, 6])),
     ("matmul", lambda n: n.update(shape=[4, 4])),
+    ("matmul", lambda n: n.update(axis=2)),                 # no such f32 mode
+    ("matmul", lambda n: n.update(dtype=thb.I64)),          # i64 result of f32 operands
     ("broadcast", lambda n: n.update(axis=2)),
     ("reduce", lambda n: n.update(shape=[4])),
     ("zero_like", lambda n: n.update(dtype=thb.I64)),
@@ -208,6 +210,18 @@ def test_matmul_inner_dimension_mismatch_rejected():
     b = thb.RegionBuilder("mm")
     x = b.input(thb.F32, [4, 6])
     w = b.input(thb.F32, [5, 3])
+    with pytest.raises(thb.GpuError) as err:
+        b.build(b.matmul(x, w)).describe(thb.DESCRIBE_PLAN)
+    assert "TRV12 malformed MatMul" in err.value.message
+
+
+def test_matmul_i64_and_exact_modes_verify():
+    for dtype, exact in ((thb.I64, False), (thb.F32, True), (thb.F32, False)):
+        spec = regions.matmul(dtype, exact)
+        assert spec.describe(thb.DESCRIBE_PLAN)[1][0] >= 1
+    b = thb.RegionBuilder("mm")
+    x = b.input(thb.I64, [4, 6])
+    w = b.input(thb.F32, [6, 3])
     with pytest.raises(thb.GpuError) as err:
         b.build(b.matmul(x, w)).describe(thb.DESCRIBE_PLAN)
     assert "TRV12 malformed MatMul" in err.value.message

@@ -45,9 +45,32 @@ def test_noalloc_sum_matches_region_sum_twice(device):
     first = torch.randn(1 << 24, device="cuda", generator=g)
     second = torch.rand((1 << 22) + 3, device="cuda", generator=g) * 4 - 1  # ragged, different values
     for x in (first, second):
-        got32, got64 = noalloc_sum(torch, x, stream)
-        want = region_sum(torch, region, x, stream)
-        assert abs(got32 - want) <= RTOL * max(1.0, abs(want))
-        assert abs(got64 - want) <= RTOL * max(1.0, abs(want))
-        host = float(np.sum(x.cpu().numpy(), dtype=np.float64))
-        assert abs(got64 - host) <= RTOL * max(1.0, abs(host))
+        check_against_region(torch, region, x, stream)
+
+
+def check_against_region(torch, region, x, stream):
+    got32, got64 = noalloc_sum(torch, x, stream)
+    want = region_sum(torch, region, x, stream)
+    assert abs(got32 - want) <= RTOL * max(1.0, abs(want))
+    assert abs(got64 - want) <= RTOL * max(1.0, abs(want))
+    host = float(np.sum(x.cpu().numpy(), dtype=np.float64))
+    assert abs(got64 - host) <= RTOL * max(1.0, abs(host))
+
+
+def test_noalloc_sum_small_empty_and_unaligned(device):
+    """The paths below the bulk-tile pass: a small input (pass 1 with 128-bit
+    loads writing its partials into the static scratch), an empty input, and
+    an input that starts 4 bytes past a 16-byte boundary (scalar loads)."""
+    torch = pytest.importorskip("torch")
+    stream = torch.cuda.current_stream().cuda_stream
+    region = regions.full_sum().compile(device)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    base = torch.randn((1 << 20) + 9, device="cuda", generator=g)
+    small = base[:1000].clone()
+    unaligned = base[1:]
+    assert unaligned.data_ptr() % 16 == 4
+    for x in (small, unaligned, small):
+        check_against_region(torch, region, x, stream)
+    empty = torch.empty(0, device="cuda")
+    got32, got64 = noalloc_sum(torch, empty, stream)
+    assert got32 == 0.0 and got64 == 0.0

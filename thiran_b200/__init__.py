@@ -114,6 +114,7 @@ class DeviceInfo(C.Structure):
 
 
 MAJOR_K, MAJOR_MN = 0, 1
+MATMUL_TENSOR, MATMUL_EXACT = 0, 1  # f32 MatMul modes (node axis)
 EPI_F32, EPI_BF16, EPI_RELU_BF16, EPI_MASK_BF16 = 0, 1, 2, 3
 
 
@@ -547,8 +548,13 @@ class RegionBuilder:
         dtype, shape = self._like(a)
         return self._add(OP_TRANSPOSE, dtype, [shape[1], shape[0]], deps=[a])
 
-    def matmul(self, a, b):
-        return self._add(OP_MATMUL, F32, [self._like(a)[1][0], self._like(b)[1][1]], deps=[a, b])
+    def matmul(self, a, b, exact=False):
+        """C = A B. i64 operands: checked multiply and add. f32 operands:
+        bf16 x bf16 -> f32 on the tensor cores, or with `exact` the
+        reference Evaluator's sequential, separately rounded f32 sums."""
+        dtype = self._like(a)[0]
+        return self._add(OP_MATMUL, dtype, [self._like(a)[1][0], self._like(b)[1][1]], deps=[a, b],
+                         axis=MATMUL_EXACT if exact else MATMUL_TENSOR)
 
     def broadcast_to_shape(self, value, reference, axis):
         return self._add(OP_BROADCAST_TO_SHAPE, *self._like(reference), deps=[value, reference], axis=axis)

@@ -114,10 +114,13 @@ static __device__ __forceinline__ void thb_bulk_store(void* dst, const void* src
                  :: "l"(dst), "r"(thb_smem_addr(src)), "r"(bytes) : "memory");
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
-// True once the mbarrier phase of this parity completed; false after ~2^26
-// polls (the caller reports GPU-KERNEL-TIMEOUT).
-static __device__ __forceinline__ bool thb_wait_parity(unsigned long long* bar, unsigned parity) {
-    for (unsigned spin = 0; spin < (1u << 26); ++spin) {
+// True once the mbarrier phase of this parity completed; false after `limit`
+// polls (2^26 by default; the caller reports GPU-KERNEL-TIMEOUT). The drain
+// after a timeout polls 2^30 times (GPU-KERNEL-DRAIN-TIMEOUT when that runs
+// out too).
+static __device__ __forceinline__ bool thb_wait_parity(unsigned long long* bar, unsigned parity,
+                                                       unsigned limit = 1u << 26) {
+    for (unsigned spin = 0; spin < limit; ++spin) {
         unsigned done;
         asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
                      " selp.u32 %0, 1, 0, p;\n}\n" : "=r"(done) : "r"(thb_smem_addr(bar)), "r"(parity) : "memory");
@@ -326,10 +329,10 @@ void emitKernels(std::ostringstream& out, const FusionGroup& group, const std::s
         << "        if (threadIdx.x == 0) {\n"
         << "            if (!thb_wait_parity(&thb_full[st], phase)) {\n"
         << "                thb_abort = 1;\n"
-        << "                // Loads still in flight land before the CTA exits.\n"
+        << "                // Loads still in flight land before the CTA exits (bounded).\n"
         << "                thb_u32 s = st, p = phase;\n"
         << "                for (thb_u32 q = 0; q < stages; ++q) {\n"
-        << "                    if (t + q * step < tiles) (void)thb_wait_parity(&thb_full[s], p);\n"
+        << "                    if (t + q * step < tiles && !thb_wait_parity(&thb_full[s], p, 1u << 30)) thb_abort = 2;\n"
         << "                    if (++s == stages) { s = 0; p ^= 1u; }\n"
         << "                }\n"
         << "            }\n"
@@ -362,7 +365,7 @@ void emitKernels(std::ostringstream& out, const FusionGroup& group, const std::s
         << "    }\n"
         << "    if (threadIdx.x == 0) asm volatile(\"cp.async.bulk.wait_group 0;\" ::: \"memory\");\n"
         << "    if (thb_abort) {\n"
-        << "        flag |= 16u;\n"
+        << "        flag |= thb_abort == 2 ? 48u : 16u;\n"
         << "    } else {\n"
         << "        const thb_u64 stride = (thb_u64)gridDim.x * blockDim.x;\n"
         << "        for (thb_u64 i = tiles * tile + (thb_u64)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)\n"

@@ -49,6 +49,19 @@ cudaError_t broadcastF32(const float* src, float* y, std::uint64_t rows, std::ui
 cudaError_t fillF32(const float* deviceScalar, float value, float* y, std::uint64_t n, int smCount,
                     cudaStream_t stream);
 
+// C = A B for row-major A [m, k], B [k, n], C [m, n] on the CUDA cores, in
+// the reference Evaluator's order (src/semantic/v0/Evaluator.cpp:125-154):
+// every element sums its products for k = 0, 1, ... with separately rounded
+// f32 operations (bit-exact), or with checked i64 arithmetic, raising bit 0
+// (value 1) of `status` when any product or partial sum overflows.
+cudaError_t matmulExactF32(const float* a, const float* b, float* c, std::uint64_t m, std::uint64_t k,
+                           std::uint64_t n, cudaStream_t stream);
+cudaError_t matmulCheckedI64(const std::int64_t* a, const std::int64_t* b, std::int64_t* c, std::uint64_t m,
+                             std::uint64_t k, std::uint64_t n, std::uint32_t* status, cudaStream_t stream);
+// y [rowsPad, ldPad] bf16 = bf16(x [rows, cols] f32), zero outside x.
+cudaError_t castPadBf16(const float* x, void* y, std::uint64_t rows, std::uint64_t cols, std::uint64_t rowsPad,
+                        std::uint64_t ldPad, int smCount, cudaStream_t stream);
+
 // Largest row length the shared-memory staged softmax handles (longer rows
 // take the streaming two-pass kernel).
 constexpr std::uint64_t kMaxSmemRowCols = 8192;

@@ -7,7 +7,8 @@
 // the reduction any scratch. This entry point keeps the reduction's block
 // partials in a fixed array compiled into the library instead: kMaxPartials
 // f64 values (32 KiB) of device memory that every GPU loading the library
-// holds until the process exits.
+// holds until the process exits, plus one u32 status word the kernels raise
+// when a bounded wait runs out.
 //
 // The reduction is the same two-pass kernel pair as the region Sum path
 // (kernels::sumAllF32 in reduce.cu, same fixed grid), so both give
@@ -30,25 +31,41 @@ constexpr std::uint32_t kMaxPartials = 4096;
 // name is only a stand-in; kernels receive the device address obtained with
 // cudaGetSymbolAddress below.
 static __device__ __align__(256) double gSumScratch[kMaxPartials];
+// Status word of the call in flight: bit 4 (16) a bounded wait ran out, bit 5
+// (32) the copies in flight could not be drained after that. Cleared by every
+// call before its launches.
+static __device__ __align__(4) std::uint32_t gSumStatus;
 
 namespace {
 
-std::mutex addressMutex;
-std::map<int, double*> addresses;  // device ordinal -> device address of gSumScratch
+struct Scratch {
+    double* partials = nullptr;
+    std::uint32_t* status = nullptr;
+};
 
-// Resolves the scratch's device address once per device, with that device
-// current. Throws on failure.
-double* scratchAddress(int device) {
+std::mutex addressMutex;
+std::map<int, Scratch> addresses;  // device ordinal -> device addresses of the static arrays
+
+// Resolves the device addresses of gSumScratch and gSumStatus once per
+// device, with that device current. The addresses stay valid for the life of
+// the device's primary context: a host that resets the device
+// (cudaDeviceReset) after the first call must not call this entry point
+// again. Throws on failure.
+Scratch scratchAddress(int device) {
     std::lock_guard<std::mutex> lock(addressMutex);
     auto found = addresses.find(device);
     if (found != addresses.end()) return found->second;
-    double* ptr = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), gSumScratch);
-    if (e != cudaSuccess || !ptr)
+    Scratch s;
+    cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.partials), gSumScratch);
+    if (e != cudaSuccess || !s.partials)
         fail(Category::Runtime, "GPU-NOALLOC-SETUP",
              std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
-    addresses.emplace(device, ptr);
-    return ptr;
+    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.status), gSumStatus);
+    if (e != cudaSuccess || !s.status)
+        fail(Category::Runtime, "GPU-NOALLOC-SETUP",
+             std::string("cudaGetSymbolAddress(status): ") + cudaGetErrorString(e));
+    addresses.emplace(device, s);
+    return s;
 }
 
 } // namespace
@@ -67,11 +84,21 @@ extern "C" int thb_sum_all_f32_noalloc(int device, const float* x, uint64_t n, f
             fail(Category::Validation, "GPU-NOALLOC-SIZE",
                  "this reduction needs " + std::to_string(parts) + " block partials; the static scratch holds " +
                      std::to_string(noalloc::kMaxPartials));
-        double* scratch = noalloc::scratchAddress(device);
-        const cudaError_t e =
-            kernels::sumAllF32(x, n, scratch, parts, outF64, outF32, info.smCount, static_cast<cudaStream_t>(stream));
+        const noalloc::Scratch scratch = noalloc::scratchAddress(device);
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        cudaError_t e = cudaMemsetAsync(scratch.status, 0, sizeof(std::uint32_t), s);
+        if (e == cudaSuccess)
+            e = kernels::sumAllF32(x, n, scratch.partials, parts, outF64, outF32, info.smCount, s, scratch.status);
         if (e != cudaSuccess)
             fail(Category::Runtime, "GPU-RUNTIME", std::string("full-sum launch: ") + cudaGetErrorString(e));
+        // The call returns the result's status: wait for the stream and read
+        // the status word (into host memory; nothing is allocated).
+        std::uint32_t word = 0;
+        e = cudaMemcpyAsync(&word, scratch.status, sizeof word, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess)
+            fail(Category::Runtime, "GPU-RUNTIME", std::string("full-sum status read: ") + cudaGetErrorString(e));
+        if (word) fail(Category::Runtime, statusText(word), "a bounded wait of the full sum ran out; the outputs are invalid");
         return THB_STATUS_OK;
     } catch (const Failure& f) {
         writeText(failure, cap, f.text());

@@ -37,7 +37,9 @@ constexpr unsigned kRowThreads = 256;
 constexpr unsigned kRowWarps = kRowThreads / 32;
 constexpr unsigned kStages = 4;
 constexpr unsigned kWaitStatus = 16u;            // status bit raised on a wait timeout
+constexpr unsigned kDrainStatus = 32u;           // ... and when the copies in flight could not be drained
 constexpr std::uint64_t kSpinLimit = 1ull << 22; // bounded mbarrier polling (~seconds at most)
+constexpr std::uint64_t kDrainLimit = kSpinLimit << 4;
 
 enum class RowOp { Softmax, Max, Sum };
 
@@ -54,10 +56,12 @@ __device__ __forceinline__ void mbarExpect(std::uint64_t* bar, unsigned bytes) {
                  : "memory");
 }
 
-// Polls the barrier phase `parity`; false when the poll budget ran out.
-__device__ __forceinline__ bool mbarWait(std::uint64_t* bar, unsigned parity) {
+// Polls the barrier phase `parity`; false when the poll budget (`limit`
+// polls) ran out. After a timeout the drain of the copies still in flight
+// polls 16 times longer (kDrainLimit) before it gives up.
+__device__ __forceinline__ bool mbarWait(std::uint64_t* bar, unsigned parity, std::uint64_t limit = kSpinLimit) {
     const std::uint32_t addr = smemAddress(bar);
-    for (std::uint64_t spin = 0; spin < kSpinLimit; ++spin) {
+    for (std::uint64_t spin = 0; spin < limit; ++spin) {
         std::uint32_t done;
         asm volatile(
             "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
@@ -224,11 +228,14 @@ __global__ void __launch_bounds__(kRowThreads) rowStaged(const float* __restrict
     }
     if (threadIdx.x == 0) {
         if (abortFlag) {
-            atomicOr(status, kWaitStatus);
             // Drain loads still in flight (rows it, it+1, it+2 may have been
-            // issued) for rows this CTA will not process.
+            // issued) for rows this CTA will not process. A copy that still
+            // has not landed may write into shared memory after this CTA
+            // exits: bit 5 tells the host to trust nothing of this device.
+            bool drained = true;
             for (std::uint64_t k = it; k < it + 3 && k < mine; ++k)
-                (void)mbarWait(&full[k % kStages], static_cast<unsigned>((k / kStages) & 1u));
+                drained &= mbarWait(&full[k % kStages], static_cast<unsigned>((k / kStages) & 1u), kDrainLimit);
+            atomicOr(status, kWaitStatus | (drained ? 0u : kDrainStatus));
         }
         bulkWaitAll();
     }
@@ -416,6 +423,7 @@ __global__ void __launch_bounds__(kSumThreads) sumAllPass1(const float* __restri
 // mbarrier completion) and all threads add their part of each tile in f64.
 // The elements past the last whole tile take plain loads. A wait that runs
 // out raises the status bit (when given) and poisons the partial with NaN.
+// Callers that pass no status word see only the NaN.
 constexpr unsigned kSumStages = 3;
 constexpr unsigned kSumTileFloats = 12288;  // 48 KiB
 constexpr std::size_t kSumBulkSmem = static_cast<std::size_t>(kSumStages) * kSumTileFloats * sizeof(float);
@@ -446,11 +454,12 @@ __global__ void __launch_bounds__(kSumThreads) sumAllBulk(const float* __restric
     unsigned st = 0, phase = 0;
     for (std::uint64_t t = first; t < tiles; t += step) {
         if (threadIdx.x == 0 && !mbarWait(&full[st], phase)) {
+            // Loads still in flight land before the CTA exits (bounded; bit 5
+            // of the status word when they did not).
             abortFlag = 1;
-            // Loads still in flight land before the CTA exits.
             unsigned s = st, ph = phase;
             for (unsigned q = 0; q < kSumStages; ++q) {
-                if (t + q * step < tiles) (void)mbarWait(&full[s], ph);
+                if (t + q * step < tiles && !mbarWait(&full[s], ph, kDrainLimit)) abortFlag = 2;
                 if (++s == kSumStages) { s = 0; ph ^= 1u; }
             }
         }
@@ -468,7 +477,7 @@ __global__ void __launch_bounds__(kSumThreads) sumAllBulk(const float* __restric
     }
     if (abortFlag) {
         if (threadIdx.x == 0) {
-            if (status) atomicOr(status, kWaitStatus);
+            if (status) atomicOr(status, kWaitStatus | (abortFlag == 2 ? kDrainStatus : 0u));
             acc = __longlong_as_double(0x7ff8000000000000ll);  // NaN
         }
     } else {

@@ -454,8 +454,10 @@ std::vector<std::string> verifyRegion(const Region& region) {
         }
         case Op::MatMul: {
             const Node* a = dep(0); const Node* b = dep(1);
+            // f32 (tensor-core or exact mode) or checked i64 operands.
             bool ok = n.dependencies.size() == 2 && a && b && a->rank == 2 && b->rank == 2 && n.rank == 2 &&
-                      a->dtype == DType::F32 && b->dtype == DType::F32 && n.dtype == DType::F32;
+                      (n.dtype == DType::F32 || n.dtype == DType::I64) && a->dtype == n.dtype &&
+                      b->dtype == n.dtype && (n.axis == THB_MATMUL_TENSOR || n.axis == THB_MATMUL_EXACT);
             ok = ok && (a->extent[1] < 0 || b->extent[0] < 0 || a->extent[1] == b->extent[0]) &&
                  (n.extent[0] < 0 || a->extent[0] < 0 || n.extent[0] == a->extent[0]) &&
                  (n.extent[1] < 0 || b->extent[1] < 0 || n.extent[1] == b->extent[1]);

@@ -165,6 +165,7 @@ std::uint32_t* deviceStatus(int ordinal) {
 }
 
 std::string statusText(std::uint32_t word) {
+    if (word & 32u) return "GPU-KERNEL-DRAIN-TIMEOUT";  // copies in flight outlived the CTA
     if (word & 16u) return "GPU-KERNEL-TIMEOUT";
     if (word & 1u) return "TH-SPEC-I64-OVERFLOW";
     if (word & 2u) return "TH021-DIVIDE-BY-ZERO";
@@ -509,18 +510,40 @@ void CompiledRegion::launchKernel(const FusionGroup& group, const std::vector<co
         const Value& a = *in[0];
         const Value& b = *in[1];
         const std::uint64_t m = a.shape[0], k = a.shape[1], n = b.shape[1];
-        void* a16 = scratch(0x30000000u | group.id, m * k * 2, ev);
-        void* b16 = scratch(0x38000000u | group.id, k * n * 2, ev);
-        launched(mlp::castToBf16(static_cast<const float*>(a.data), a16, m * k, sms, stream), "matmul cast A");
-        launched(mlp::castToBf16(static_cast<const float*>(b.data), b16, k * n, sms, stream), "matmul cast B");
-        if (k == 0) {
+        if (k == 0) {  // empty sums: acc stays 0 (Evaluator.cpp:135-141)
             check(cudaMemsetAsync(out.data, 0, out.bytes(), stream), "cudaMemsetAsync(matmul k=0)");
+            ++ev.stream_submissions;
             return;
         }
+        if (node.dtype == DType::I64) {
+            launched(kernels::matmulCheckedI64(static_cast<const std::int64_t*>(a.data),
+                                               static_cast<const std::int64_t*>(b.data),
+                                               static_cast<std::int64_t*>(out.data), m, k, n, status, stream),
+                     "matmul i64 launch");
+            return;
+        }
+        if (node.axis == THB_MATMUL_EXACT) {
+            launched(kernels::matmulExactF32(static_cast<const float*>(a.data), static_cast<const float*>(b.data),
+                                             static_cast<float*>(out.data), m, k, n, stream),
+                     "matmul exact launch");
+            return;
+        }
+        // Tensor cores: bf16 operands with 16-byte row strides. K and N are
+        // padded to multiples of 8 with zeros (exact zero products).
+        const std::uint64_t kp = (k + 7) / 8 * 8, np = (n + 7) / 8 * 8;
+        void* a16 = scratch(0x30000000u | group.id, m * kp * 2, ev);
+        void* b16 = scratch(0x38000000u | group.id, kp * np * 2, ev);
+        if (kp == k) launched(mlp::castToBf16(static_cast<const float*>(a.data), a16, m * k, sms, stream), "matmul cast A");
+        else launched(kernels::castPadBf16(static_cast<const float*>(a.data), a16, m, k, m, kp, sms, stream),
+                      "matmul cast A");
+        if (kp == k && np == n)
+            launched(mlp::castToBf16(static_cast<const float*>(b.data), b16, k * n, sms, stream), "matmul cast B");
+        else launched(kernels::castPadBf16(static_cast<const float*>(b.data), b16, k, n, kp, np, sms, stream),
+                      "matmul cast B");
         gemm::Problem q;
-        q.m = m; q.n = n; q.k = k;
-        q.a = a16; q.lda = k;
-        q.b = b16; q.bMajorMN = true; q.ldb = n;
+        q.m = m; q.n = n; q.k = kp;
+        q.a = a16; q.lda = kp;
+        q.b = b16; q.bMajorMN = true; q.ldb = np;
         q.c = out.data; q.ldc = n; q.epilogue = gemm::kEpiF32;
         if (const char* bad = gemm::validate(q)) fail(Category::Unsupported, "GPU-UNSUPPORTED-SHAPE", bad);
         launched(gemm::run(q, sms, status, stream), "matmul launch");
@@ -571,9 +594,6 @@ Value CompiledRegion::run(const std::vector<Value>& inputs, cudaStream_t stream,
             const Value& b = dep(1);
             if (a.shape[1] != b.shape[0])
                 fail(Category::Semantic, "TH-SPEC-SHAPE", "matmul inner extents differ");
-            if (a.shape[1] % 8 || b.shape[1] % 8)
-                fail(Category::Unsupported, "GPU-UNSUPPORTED-SHAPE",
-                     "tensor-core matmul needs K and N multiples of 8 (16-byte rows)");
             v.shape[0] = a.shape[0]; v.shape[1] = b.shape[1];
             break;
         }

@@ -213,3 +213,38 @@ def full_sum(n=None):
     b = RegionBuilder("total")
     x = b.input(F32, [n])
     return b.build(b.sum(x, 0))
+
+
+def matmul(dtype=F32, exact=False):
+    """fn mm(A: Tensor<T,2>, B: Tensor<T,2>) -> Tensor<T,2> { return A * B }
+    (the reference runs this only in its Evaluator, Evaluator.cpp:125-154).
+    f32: tensor cores (bf16 operands), or with `exact` the Evaluator's
+    sequential f32 sums; i64: checked multiply and add."""
+    b = RegionBuilder("mm")
+    x = b.input(dtype, [None, None])
+    y = b.input(dtype, [None, None])
+    return b.build(b.matmul(b.alias(x), b.alias(y), exact=exact))
+
+
+def transformer_block(exact=True):
+    """examples/transformer.th: one attention block on X [2,4] with Wq, Wk
+    [4,4], Wv [4,8] and Wo [8,4] (inputs in that order):
+        Q = X Wq; K = X Wk; Scores = Q K^T; Attention = softmax(Scores);
+        V = X Wv; Context = Attention V; O = Context Wo + X
+    The legacy stack lowers MatMul / Transpose / Softmax / Add to torch
+    (src/backend/PythonExecutorEmitter.cpp:87-97); here every node is an
+    engine op, the matmuls exact (or on the tensor cores)."""
+    b = RegionBuilder("transformer")
+    x = b.input(F32, [None, None])
+    wq = b.input(F32, [None, None])
+    wk = b.input(F32, [None, None])
+    wv = b.input(F32, [None, None])
+    wo = b.input(F32, [None, None])
+    q = b.matmul(x, wq, exact=exact)
+    k = b.matmul(x, wk, exact=exact)
+    scores = b.matmul(q, b.transpose(k), exact=exact)
+    attention = b.softmax(scores)
+    v = b.matmul(x, wv, exact=exact)
+    context = b.matmul(attention, v, exact=exact)
+    projected = b.matmul(context, wo, exact=exact)
+    return b.build(b.add(projected, x))
