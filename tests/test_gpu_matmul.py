@@ -115,6 +115,8 @@ def test_transformer_example_region(device):
         q, k = tx[0] @ tx[1], tx[0] @ tx[2]
         ctx = torch.softmax(q @ k.T, dim=-1) @ (tx[0] @ tx[3])
         np.testing.assert_allclose(out, (ctx @ tx[4] + tx[0]).numpy(), rtol=1e-4, atol=1e-5)
-        # Tensor-core matmuls: the bf16 contract.
+        # Tensor-core matmuls: six bf16-operand products composed through a
+        # softmax (each product alone holds the per-element contract, tested
+        # above), so the block is held to 2e-2 in relative Frobenius norm.
         fast = regions.transformer_block(exact=False).compile(device).execute(inputs)
-        assert block_error(fast, want) <= 2e-2
+        assert np.linalg.norm(fast.astype(np.float64) - want) <= 2e-2 * np.linalg.norm(want.astype(np.float64))
