@@ -149,12 +149,13 @@ def test_mlp_biases_and_momentum_match_oracle(device, batch, d_in, hidden, d_out
     assert rel(B2.cpu().numpy(), ws[3]) <= 1e-3
 
 
-def test_mlp_bias_gradient_against_f32_column_sums(device):
+@pytest.mark.parametrize("batch,d_in,hidden,d_out", [(512, 128, 256, 128), (256, 128, 256, 2056)])
+def test_mlp_bias_gradient_against_f32_column_sums(device, batch, d_in, hidden, d_out):
     """db2 is exactly what the f32 loss gradient sums to (no bf16 rounding
-    sits between Y and dY's column sums), 1e-5 relative per element."""
+    sits between Y and dY's column sums), 1e-5 relative per element; the
+    second shape has more output columns than one loss block covers."""
     torch = pytest.importorskip("torch")
     rng = np.random.default_rng(5)
-    batch, d_in, hidden, d_out = 512, 128, 256, 128
     x = rng.standard_normal((batch, d_in)).astype(np.float32)
     t = rng.standard_normal((batch, d_out)).astype(np.float32)
     w1, w2 = xavier(rng, d_in, hidden), xavier(rng, hidden, d_out)

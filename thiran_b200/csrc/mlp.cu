@@ -212,7 +212,9 @@ cudaError_t lossAndGradient(const float* y, const float* t, void* dy, double* pa
     if (e != cudaSuccess) return e;
     sumPartialsKernel<<<1, kThreads, 0, s>>>(partials, colBlocks * chunks, lossSum);
     if ((e = cudaGetLastError()) != cudaSuccess || !db) return e;
-    columnReduceKernel<<<colBlocks, kThreads, 0, s>>>(colSums, chunks, cols, db);
+    // One thread per column (the loss blocks above take four columns each).
+    columnReduceKernel<<<static_cast<unsigned>((cols + kThreads - 1) / kThreads), kThreads, 0, s>>>(colSums, chunks,
+                                                                                                 cols, db);
     return cudaGetLastError();
 }
 
