@@ -470,7 +470,35 @@ int orc_region_eval(const thb_region_desc* r, const thb_abi_arg* args, uint64_t 
             v->data = calloc(v->count ? v->count : 1, 4);
             v->owned = 1;
             break;
-        case THB_OP_SOFTMAX: case THB_OP_ROW_MAX: case THB_OP_SUM: {
+        case THB_OP_SUM:
+            if (n->dtype == THB_DTYPE_I64) {
+                /* Evaluator.cpp:237-250: acc = checked(acc + v) in order */
+                const uint64_t rows = d0->rank == 2 ? d0->shape[0] : 1;
+                const uint64_t cols = d0->rank == 2 ? d0->shape[1] : d0->shape[0];
+                const int64_t* x = (const int64_t*)d0->data;
+                const uint64_t outer = n->rank == 0 ? 1 : (n->axis == 1 ? rows : cols);
+                const uint64_t inner = n->rank == 0 ? d0->count : (n->axis == 1 ? cols : rows);
+                v->count = n->rank == 0 ? 1 : outer;
+                v->shape[0] = outer;
+                v->data = malloc(8 * (v->count ? v->count : 1));
+                v->owned = 1;
+                for (uint64_t o = 0; o < outer && status == 0; ++o) {
+                    int64_t acc = 0;
+                    for (uint64_t k = 0; k < inner; ++k) {
+                        const int64_t e = n->rank == 0 ? x[k] : (n->axis == 1 ? x[o * cols + k] : x[k * cols + o]);
+                        if (__builtin_add_overflow(acc, e, &acc)) {
+                            set_failure(failure, cap, "TH-SPEC-I64-OVERFLOW");
+                            status = 2;
+                            break;
+                        }
+                    }
+                    if (n->rank == 0) v->i = acc;
+                    else ((int64_t*)v->data)[o] = acc;
+                }
+                break;
+            }
+            /* fall through: f32 sums */
+        case THB_OP_SOFTMAX: case THB_OP_ROW_MAX: {
             const uint64_t rows = d0->rank == 2 ? d0->shape[0] : 1;
             const uint64_t cols = d0->rank == 2 ? d0->shape[1] : d0->shape[0];
             v->count = 1;

@@ -146,6 +146,10 @@ CHAIN = open(os.path.join(ROOT, "oracle", "programs", "f32_chain.th")).read()
 CHAIN_LITERAL = "fn f(x: Tensor<f32,1>) -> Tensor<f32,1> {\nreturn ((x*1.5+0.25).*x - x)*0.5 + x\n}"
 I64_REGION = open(os.path.join(ROOT, "oracle", "programs", "i64_region.th")).read()
 SQUARE_LINEAR = "fn f(x: Tensor<f32,1>) -> Tensor<f32,1> {\nreturn research_square_linear(x)\n}"
+SUMS_I64 = """fn rows(A: Tensor<i64,2>) -> Tensor<i64,1> { return sum(A, 1) }
+fn cols(A: Tensor<i64,2>) -> Tensor<i64,1> { return sum(A, 0) }
+fn total(A: Tensor<i64,1>) -> i64 { return sum(A, 0) }
+"""
 SUMS = """fn rows(A: Tensor<f32,2>) -> Tensor<f32,1> { return sum(A, 1) }
 fn cols(A: Tensor<f32,2>) -> Tensor<f32,1> { return sum(A, 0) }
 fn total(A: Tensor<f32,2>) -> f32 { return sum(sum(A, 1), 0) }
@@ -247,6 +251,19 @@ def main():
     for fn in ("rows", "cols", "total"):
         status, value = evaluate(SUMS, fn, [m])
         arrays[f"sum_{fn}"] = np.asarray(value, np.float32)
+    # i64 sums (checked adds in order) and a prefix that overflows although
+    # the total would fit.
+    im = np.random.default_rng(9).integers(-(1 << 40), 1 << 40, (33, 70), dtype=np.int64)
+    arrays["sum_i64_in"] = im
+    for fn in ("rows", "cols"):
+        status, value = evaluate(SUMS_I64, fn, [im])
+        arrays[f"sum_i64_{fn}"] = np.asarray(value, np.int64)
+    status, value = evaluate(SUMS_I64, "total", [im.reshape(-1)])
+    arrays["sum_i64_total"] = np.asarray(value, np.int64)
+    edge = np.array([np.iinfo(np.int64).max, 1, -1], np.int64)
+    fixtures["sum_i64_prefix_overflow"] = evaluate(SUMS_I64, "total", [edge])[0]
+    fixtures["sum_i64_rows_prefix_overflow"] = evaluate(SUMS_I64, "rows", [edge.reshape(1, 3)])[0]
+    fixtures["sum_i64_cols_prefix_overflow"] = evaluate(SUMS_I64, "cols", [edge.reshape(3, 1)])[0]
     rng = np.random.default_rng(4)
     ma = rng.standard_normal((16, 32)).astype(np.float32)
     mb = rng.standard_normal((32, 24)).astype(np.float32)

@@ -22,6 +22,7 @@ fn imm(A: Tensor<i64,2>, B: Tensor<i64,2>) -> Tensor<i64,2> { return A * B }
 fn affine(x: Tensor<f32,2>, w: Tensor<f32,2>, b: Tensor<f32,1>) -> Tensor<f32,2> { return x * w + b }
 fn total(A: Tensor<f32,2>) -> f32 { return sum(sum(A, 1), 0) }
 fn scaled(x: Tensor<f32,1>) -> Tensor<f32,1> { return research_chain(x) * 2.0 }
+fn isum(A: Tensor<i64,2>, B: Tensor<i64,2>) -> Tensor<i64,1> { return sum(A * B, 0) }
 """
 
 # A two-layer loss (matmul, sum, elementwise) and an extension loss; their

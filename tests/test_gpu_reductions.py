@@ -88,3 +88,64 @@ def test_softmax_then_sum_region(device):
     out = region.execute([x])
     np.testing.assert_allclose(out, 1.0, rtol=1e-5)
     assert region.evidence["kernel_launches"] == 2
+
+
+def _sum_i64_region(kind):
+    b = thb.RegionBuilder("s")
+    if kind == "total":
+        x = b.input(thb.I64, [None])
+        return b.build(b.sum(x, 0))
+    x = b.input(thb.I64, [None, None])
+    return b.build(b.sum(x, 1 if kind == "rows" else 0))
+
+
+def test_sum_i64_matches_reference(device, golden):
+    m = golden["sum_i64_in"]
+    for kind in ("rows", "cols"):
+        out = _sum_i64_region(kind).compile(device).execute([m])
+        np.testing.assert_array_equal(out, golden[f"sum_i64_{kind}"])
+    assert _sum_i64_region("total").compile(device).execute([m.reshape(-1).copy()]) == int(golden["sum_i64_total"])
+
+
+@pytest.mark.parametrize("shape", [(1, 1), (7, 3), (300, 4099), (4097, 33), (1 << 22,), (1000003,), (5,)])
+def test_sum_i64_random_exact(device, shape):
+    """Large magnitudes (|v| < 2^50, totals far beyond f64's 53 bits): the
+    result is exact; where a partial sum in the reference order overflows,
+    the same failure id."""
+    rng = np.random.default_rng(sum(shape))
+    x = rng.integers(-(1 << 50), 1 << 50, shape, dtype=np.int64)
+    kinds = ("total",) if len(shape) == 1 else ("rows", "cols")
+    for kind in kinds:
+        spec = _sum_i64_region(kind)
+        try:
+            want = orc.region_eval(spec, [x])
+        except orc.OracleFailure as failure:
+            with pytest.raises(thb.GpuError) as err:
+                spec.compile(device).execute([x])
+            assert err.value.code == failure.code
+            continue
+        got = spec.compile(device).execute([x])
+        np.testing.assert_array_equal(got, want)
+
+
+def test_sum_i64_prefix_overflow(device, fixtures):
+    """The reference fails when any partial sum in its order leaves the i64
+    range, even if the total would fit ([MAX, 1, -1]); a reordered sum must
+    not hide that, and a sum whose partials stay in range must not fail
+    ([-1, MAX, 1] overflows only at the end in the reference order too, so
+    it fails; [1, -1, MAX] fits)."""
+    mx = np.iinfo(np.int64).max
+    for kind, shape in (("total", (3,)), ("rows", (1, 3)), ("cols", (3, 1))):
+        region = _sum_i64_region(kind).compile(device)
+        with pytest.raises(thb.GpuError) as err:
+            region.execute([np.array([mx, 1, -1], np.int64).reshape(shape)])
+        assert err.value.code == "TH-SPEC-I64-OVERFLOW"
+        out = region.execute([np.array([1, -1, mx], np.int64).reshape(shape)])
+        assert int(np.asarray(out).reshape(-1)[0]) == mx
+    # A long vector whose prefix crosses the edge in the middle of a block.
+    x = np.ones(1 << 20, np.int64)
+    x[5000] = mx - 4000
+    x[5001] = -(1 << 40)
+    with pytest.raises(thb.GpuError) as err:
+        _sum_i64_region("total").compile(device).execute([x])
+    assert err.value.code == fixtures["sum_i64_prefix_overflow"]

@@ -64,6 +64,14 @@ def test_i64_matmul(drivers, tmp_path):
     assert status == {"status": "error", "code": "TH-SPEC-I64-OVERFLOW", "category": "SemanticFailure"}, out
 
 
+def test_i64_column_sum_of_matmul(drivers, tmp_path):
+    rng = np.random.default_rng(8)
+    a = rng.integers(-(1 << 20), 1 << 20, (40, 17), dtype=np.int64)
+    b = rng.integers(-(1 << 20), 1 << 20, (17, 9), dtype=np.int64)
+    got, ref = gpu_and_reference(tmp_path, PROGRAM, "isum", [a, b])
+    np.testing.assert_array_equal(got, ref)
+
+
 def test_matmul_with_broadcast_bias_bitwise(drivers, tmp_path):
     rng = np.random.default_rng(3)
     x = rng.standard_normal((16, 12)).astype(np.float32)

@@ -412,3 +412,26 @@ def test_qualification_workload_digests(spec, output_digest):
     x, y = _qualification_inputs(1 << 20)
     e = orc.region_eval(spec(), [x, y])
     assert orc.fnv_floats(e, 1469598103934665603) == output_digest
+
+
+def _sum_i64_region(kind):
+    b = thb.RegionBuilder("s")
+    if kind == "total":
+        x = b.input(thb.I64, [None])
+        return b.build(b.sum(x, 0))
+    x = b.input(thb.I64, [None, None])
+    return b.build(b.sum(x, 1 if kind == "rows" else 0))
+
+
+def test_sum_i64_checked_against_reference(golden, fixtures):
+    m = golden["sum_i64_in"]
+    for kind in ("rows", "cols"):
+        np.testing.assert_array_equal(orc.region_eval(_sum_i64_region(kind), [m]), golden[f"sum_i64_{kind}"])
+    assert orc.region_eval(_sum_i64_region("total"), [m.reshape(-1).copy()]) == int(golden["sum_i64_total"])
+    edge = np.array([np.iinfo(np.int64).max, 1, -1], np.int64)
+    for kind, value in (("total", edge), ("rows", edge.reshape(1, 3)), ("cols", edge.reshape(3, 1))):
+        with pytest.raises(orc.OracleFailure) as err:
+            orc.region_eval(_sum_i64_region(kind), [value])
+        key = {"total": "sum_i64_prefix_overflow", "rows": "sum_i64_rows_prefix_overflow",
+               "cols": "sum_i64_cols_prefix_overflow"}[kind]
+        assert err.value.code == fixtures[key] == "TH-SPEC-I64-OVERFLOW"

@@ -37,6 +37,7 @@ def lowered(tmp_path, program, function, element=0, mode="exact"):
     ("affine", {"38", "39", "7"}),        # MatMul, BroadcastToShape (the rank-1 bias), Add
     ("total", {"32"}),
     ("scaled", {"10", "9"}),              # Extension, scalar Multiply as ElementMultiply
+    ("isum", {"38", "32"}),               # i64 MatMul and Sum
 ])
 def test_lowering_admits_what_the_reference_extractor_defers(driver, tmp_path, function, ops):
     out, nodes = lowered(tmp_path, PROGRAM, function)

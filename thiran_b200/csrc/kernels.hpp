@@ -58,6 +58,20 @@ cudaError_t matmulExactF32(const float* a, const float* b, float* c, std::uint64
                            std::uint64_t n, cudaStream_t stream);
 cudaError_t matmulCheckedI64(const std::int64_t* a, const std::int64_t* b, std::int64_t* c, std::uint64_t m,
                              std::uint64_t k, std::uint64_t n, std::uint32_t* status, cudaStream_t stream);
+// i64 sums with the reference's checked-add semantics
+// (src/semantic/v0/Evaluator.cpp:237-250): exact totals; bit 0 (value 1) of
+// `status` when any prefix sum in the reference's order leaves the i64
+// range. Rows: sum over the last axis; columns: over the leading axis; all:
+// every element of a vector, two passes over sumAllI64ScratchBytes() of
+// scratch.
+cudaError_t sumRowsI64(const std::int64_t* x, std::int64_t* y, std::uint64_t rows, std::uint64_t cols, int smCount,
+                       cudaStream_t stream, std::uint32_t* status);
+cudaError_t sumColsI64(const std::int64_t* x, std::int64_t* y, std::uint64_t rows, std::uint64_t cols,
+                       cudaStream_t stream, std::uint32_t* status);
+std::uint32_t sumAllI64Blocks(std::uint64_t n, int smCount);
+std::size_t sumAllI64ScratchBytes(std::uint64_t n, int smCount);
+cudaError_t sumAllI64(const std::int64_t* x, std::uint64_t n, void* scratch, std::int64_t* out, int smCount,
+                      cudaStream_t stream, std::uint32_t* status);
 // y [rowsPad, ldPad] bf16 = bf16(x [rows, cols] f32), zero outside x.
 cudaError_t castPadBf16(const float* x, void* y, std::uint64_t rows, std::uint64_t cols, std::uint64_t rowsPad,
                         std::uint64_t ldPad, int smCount, cudaStream_t stream);

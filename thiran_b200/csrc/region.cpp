@@ -399,9 +399,10 @@ std::vector<std::string> verifyRegion(const Region& region) {
         }
         case Op::Sum: {
             const Node* in = dep(0);
-            bool ok = n.dependencies.size() == 1 && in && numericTensor(*in) && in->dtype == DType::F32 &&
-                      n.dtype == DType::F32 && n.axis >= 0 && static_cast<std::uint32_t>(n.axis) < in->rank &&
-                      n.rank + 1 == in->rank;
+            // f32 (f64-accumulated) or i64 (exact, checked) operands.
+            bool ok = n.dependencies.size() == 1 && in && numericTensor(*in) &&
+                      (in->dtype == DType::F32 || in->dtype == DType::I64) && n.dtype == in->dtype && n.axis >= 0 &&
+                      static_cast<std::uint32_t>(n.axis) < in->rank && n.rank + 1 == in->rank;
             if (ok && n.rank == 1) {
                 const std::int64_t kept = in->extent[n.axis == 0 ? 1 : 0];
                 ok = n.extent[0] < 0 || kept < 0 || n.extent[0] == kept;

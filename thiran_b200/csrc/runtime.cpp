@@ -417,7 +417,24 @@ void CompiledRegion::launchReduction(const FusionGroup& group, const Value& in, 
     case Op::Softmax: e = kernels::softmaxRowsF32(x, y, rows, cols, info_->smCount, stream, status); break;
     case Op::RowMax: e = kernels::maxRowsF32(x, y, rows, cols, info_->smCount, stream, status); break;
     case Op::Sum:
-        if (in.rank == 1) {
+        if (node.dtype == DType::I64) {
+            const auto* xi = static_cast<const std::int64_t*>(in.data);
+            auto* yi = static_cast<std::int64_t*>(out.data);
+            if (in.rank == 1) {
+                const std::size_t bytes = kernels::sumAllI64ScratchBytes(in.count(), info_->smCount);
+                auto& scratch = scalars_[0x80000000u | group.id];
+                if (!scratch) scratch = std::make_unique<DeviceBuffer>();
+                if (scratch->reserve(bytes, device_)) {
+                    ++ev.allocation_count;
+                    ev.allocation_bytes_requested += bytes;
+                }
+                e = kernels::sumAllI64(xi, in.count(), scratch->ptr, yi, info_->smCount, stream, status);
+            } else if (node.axis == 1) {
+                e = kernels::sumRowsI64(xi, yi, rows, cols, info_->smCount, stream, status);
+            } else {
+                e = kernels::sumColsI64(xi, yi, rows, cols, stream, status);
+            }
+        } else if (in.rank == 1) {
             const std::uint32_t parts = kernels::sumAllPartialCount(in.count(), info_->smCount);
             auto& scratch = scalars_[0x80000000u | group.id];
             if (!scratch) scratch = std::make_unique<DeviceBuffer>();
