@@ -214,9 +214,10 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
         # 2.141 vs 2.204 ms per step) and loses in peer mode (2 ranks 2.87
         # vs 2.79 ms).
         switch = (mode or fused_reduction_mode(world)) == "switch"
-        update = args.dp_update == "fused" or (args.dp_update == "auto" and switch)
+        compact = args.dp_format == "bf16-sharded"
+        update = compact or args.dp_update == "fused" or (args.dp_update == "auto" and switch)
         with torch.cuda.stream(stream):
-            fused = FusedGradientAllReduce(session, dist, mode=mode, update=update)
+            fused = FusedGradientAllReduce(session, dist, mode=mode, update=update, compact=compact)
         if not fused.available:
             fused = None
     from thiran_b200.distributed import bind_bias_gradients
@@ -226,11 +227,15 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
         collective = ("dW all-reduce fused into the dW GEMMs: per-tile announce, owner rank sums "
                       + ("with NVLink peer loads and stores" if fused.mode == "peer"
                          else "in NVSwitch (multimem.ld_reduce + multimem.st)")
-                      + ("; optimizer step applied by each tile's owner in the reduction, new W and bf16 W "
+                      + ("; bf16 gradient tiles summed by each tile's owner with f32 accumulation, optimizer step "
+                         "applied to the owner's f32 weights (sharded by tile owner), bf16 W written to every rank"
+                         if fused.compact else
+                         "; optimizer step applied by each tile's owner in the reduction, new W and bf16 W "
                          "written to every rank" if fused.update else "; separate optimizer pass")
                       + "; bias gradients (80 KiB) by NCCL all-reduce")
     elif world > 1:
         collective = "NCCL all-reduce of dW1, dW2 and the bias gradients"
+    nvlink = nvlink_bytes_per_step(world, d_in * hidden + hidden * d_out, fused)
 
     def step(xx=x, tt=t):
         if world == 1:  # thb_mlp_step: the weight updates run in the dW GEMMs' read-out
@@ -338,6 +343,7 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (torch.Generator on device, seeded)",
             "config": dict(workload.config(world), **({"gradient_reduction": collective} if collective else {}),
+                           **({"nvlink_bytes_per_step_per_gpu": nvlink} if nvlink else {}),
                            optimizer=("SGD applied in the dW GEMMs' read-out (thb_mlp_step), biases by a separate "
                                       "pass" if world == 1 else
                                       "SGD applied by each tile's owner inside the fused all-reduce, biases by a "
@@ -367,6 +373,39 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
         print(json.dumps(line), flush=True)
     session.release()
     return 0
+
+
+
+def nvlink_bytes_per_step(world, elements, fused):
+    """Per GPU and direction, bytes of weight-gradient traffic over NVLink in
+    one data-parallel step of `elements` weights on `world` ranks (the 80 KiB
+    of bias gradients aside). Switch mode counts what crosses each GPU's
+    links (NVSwitch reads a rank's tile once per multimem.ld_reduce and
+    replicates a multimem.st), peer mode the loads and stores of other
+    ranks' memory."""
+    if world <= 1:
+        return None
+    w = float(world)
+    if fused is None:  # NCCL ring all-reduce of f32 gradients
+        out = inp = 2.0 * (w - 1) / w * 4
+        how = "NCCL ring all-reduce of f32 gradients: 2(w-1)/w x 4 B per element each way"
+    elif fused.compact:
+        if fused.mode == "switch":
+            out = inp = 2.0
+            how = "bf16 tiles read once by the switch, bf16 weights multicast: 2 B per element each way"
+        else:
+            out = inp = 4.0 * (w - 1) / w
+            how = "owner loads the other ranks' bf16 tiles and stores the bf16 weights to them: 4(w-1)/w B each way"
+    elif fused.mode == "switch":
+        reply = 6.0 if fused.update else 4.0  # new f32 + bf16 weights, or the f32 sum
+        out = 4.0 * (w - 1) / w + reply / w
+        inp = 4.0 / w + reply * (w - 1) / w
+        how = "f32 tiles read once by the switch, the f32 sum (or f32 and bf16 weights) multicast"
+    else:
+        reply = 6.0 if fused.update else 4.0
+        out = inp = 4.0 * (w - 1) / w + reply * (w - 1) / w
+        how = "owner loads the other ranks' f32 tiles and stores the sum (or the weights) to them"
+    return {"out": int(out * elements), "in": int(inp * elements), "model": how}
 
 
 # ---- clocks ------------------------------------------------------------------------
@@ -609,6 +648,9 @@ def main():
                    help="with a fused all-reduce: apply the optimizer step in the reduction (each tile's owner; "
                         "'auto' does so in switch mode, where it measured faster) or run the separate update pass "
                         "on every rank (faster in peer mode, 2 ranks)")
+    p.add_argument("--dp-format", default="bf16-sharded", choices=["bf16-sharded", "f32"],
+                   help="with a fused all-reduce: bf16 gradient tiles and f32 weights sharded by tile owner (only "
+                        "the bf16 weights are broadcast), or f32 gradients and replicated f32 weights")
     p.add_argument("--shrink", type=int, default=1,
                    help="divide the leading extent (small cases for profiler captures; not a bench line)")
     args = p.parse_args()

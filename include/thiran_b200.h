@@ -548,6 +548,28 @@ int thb_mlp_bind(thb_mlp* session, uint32_t which, void* device_pointer);
  * on every rank. */
 int thb_mlp_bind_reduction(thb_mlp* session, uint32_t which, void* const* peers, void* multicast,
                            uint32_t* const* flag_peers, uint32_t rank, uint32_t world);
+/* Gradient format of the fused all-reduce of `which` (THB_MLP_DW1 / DW2;
+ * call after thb_mlp_bind_reduction, which resets it to THB_REDUCE_F32):
+ *  - THB_REDUCE_F32: f32 tiles, the sum written to every rank (or, with the
+ *    fused update, the new f32 parameters and bf16 copy written to every
+ *    rank);
+ *  - THB_REDUCE_BF16_SHARDED: each rank stores its tile as bf16 (the peers'
+ *    dW buffers are then bf16 [rows][cols]); the tile's owner sums the
+ *    ranks' tiles with f32 accumulation, applies the optimizer step to its
+ *    own f32 parameters only and writes the bf16 copy to every rank. The f32
+ *    parameters are sharded by tile owner (thb_mlp_gather_parameters
+ *    assembles them); each element costs about 2 bytes of NVLink traffic per
+ *    direction instead of 10. Needs thb_mlp_bind_update and
+ *    thb_mlp_forward_backward_update. Engine addition: the reference has no
+ *    multi-GPU training (src/distributed/PartitionPlanner.cpp:6-32). */
+enum { THB_REDUCE_F32 = 0, THB_REDUCE_BF16_SHARDED = 1 };
+int thb_mlp_set_reduction_format(thb_mlp* session, uint32_t which, uint32_t format);
+/* With a THB_REDUCE_BF16_SHARDED reduction: copies every tile of weight
+ * `which` (THB_MLP_W1 / W2) that this rank does not own from its owner's
+ * f32 parameters (peer loads), so this rank holds them all. Every rank calls
+ * it between steps, and no rank frees or rebinds its buffers until all have
+ * finished (a barrier). */
+int thb_mlp_gather_parameters(thb_mlp* session, uint32_t which, void* stream, char* failure, uint64_t failure_cap);
 /* Signal words thb_mlp_bind_reduction needs for `which` (0 for an unknown
  * buffer or session). */
 uint64_t thb_mlp_reduction_flag_words(thb_mlp* session, uint32_t which);

@@ -280,3 +280,85 @@ def test_update_fused_into_the_all_reduce(tmp_path, mode, world):
     ref = single_gpu_reference()
     for k in ("w1", "w2", "b1", "b2"):
         assert rel(got[f"fused_{k}"], ref[k]) <= 1e-4, k
+
+
+def _compact_rank(rank, world, port, mode, out_path):
+    """Three data-parallel steps with the bf16 sharded reduction: bf16
+    gradient tiles summed by their owners in f32, the owner's f32 weights
+    updated, the bf16 copy broadcast; then the f32 weights gathered."""
+    import datetime
+    import sys
+    import torch.distributed as dist
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    import thiran_b200 as thb
+    from thiran_b200.distributed import FusedGradientAllReduce
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    x, t, w1, w2, b1, b2 = problem()
+    batch = x.shape[0]
+    local = batch // world
+    xs = torch.from_numpy(x[rank * local:(rank + 1) * local].copy()).cuda()
+    ts = torch.from_numpy(t[rank * local:(rank + 1) * local].copy()).cuda()
+    s, params = session(thb, local, batch, rank, w1, w2, b1, b2)
+    mc = FusedGradientAllReduce(s, dist, mode=mode, update=True, compact=True)
+    if not mc.available:
+        dist.destroy_process_group()
+        if rank == 0:
+            open(out_path, "w").write("unavailable")
+        return
+    for _ in range(3):
+        s.forward_backward_update(xs, ts, LR)
+        mc.after_backward()
+        s.apply_sgd(LR)
+    thb.check_device_status(rank)
+    torch.cuda.synchronize()
+    copies = [mc.param_handles[0][1][1][0].clone(), mc.param_handles[1][1][1][0].clone()]
+    weights = [w.clone() for w in mc.gather_parameters()]
+    results = {"w1": weights[0].cpu().numpy(), "w2": weights[1].cpu().numpy(),
+               "b1": params["b1"].cpu().numpy(), "b2": params["b2"].cpu().numpy()}
+    for k, (w, c) in enumerate(zip(weights, copies)):
+        gathered = [torch.empty_like(w) for _ in range(world)]
+        dist.all_gather(gathered, w)
+        results[f"ranks_equal_w{k + 1}"] = np.array(all(torch.equal(g, w) for g in gathered))
+        results[f"copy_matches_w{k + 1}"] = np.array(torch.equal(c, w.to(torch.bfloat16)))
+    mc.close()
+    own = [s.buffer(thb.MLP_W1)[0], s.buffer(thb.MLP_W2)[0]]
+    results["closed_restores_weights"] = np.array(all(torch.equal(_device_tensor(p, w), w)
+                                                      for p, w in zip(own, weights)))
+    dist.barrier()
+    s.release()
+    if rank == 0:
+        np.savez(out_path, **results)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("mode", ["peer", "switch"])
+def test_compact_sharded_reduction(tmp_path, mode, world):
+    """bf16 gradient payload and owner-sharded f32 weights: every rank ends
+    with the same gathered weights, bf16 copies equal to their rounding,
+    close() restores them into the session, and the trajectory follows the
+    single-process full-batch step and the oracle's (the bf16 rounding of
+    each rank's gradient tile moves the update by ~2^-8 of itself)."""
+    if gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    out = str(tmp_path / f"compact_{mode}{world}.npz")
+    mp.start_processes(_compact_rank, args=(world, free_port(), mode, out), nprocs=world, join=True,
+                       start_method="spawn")
+    if os.path.exists(out) and open(out, "rb").read(11) == b"unavailable":
+        pytest.skip("no NVLink multicast on this system")
+    got = dict(np.load(out))
+    for k in ("1", "2"):
+        assert bool(got[f"ranks_equal_w{k}"]) and bool(got[f"copy_matches_w{k}"]), k
+    assert bool(got["closed_restores_weights"])
+    ref = single_gpu_reference()
+    orc = oracle_steps()
+    for k in ("w1", "w2", "b1", "b2"):
+        assert rel(got[k], ref[k]) <= 1e-3, k
+        assert rel(got[k], orc[k]) <= 1e-3, k
+

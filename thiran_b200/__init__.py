@@ -115,6 +115,7 @@ class DeviceInfo(C.Structure):
 
 MAJOR_K, MAJOR_MN = 0, 1
 MATMUL_TENSOR, MATMUL_EXACT = 0, 1  # f32 MatMul modes (node axis)
+REDUCE_F32, REDUCE_BF16_SHARDED = 0, 1  # MLP gradient all-reduce formats
 EPI_F32, EPI_BF16, EPI_RELU_BF16, EPI_MASK_BF16 = 0, 1, 2, 3
 
 
@@ -195,6 +196,8 @@ SIGNATURES = {
                                       C.POINTER(C.c_void_p), C.c_void_p]),
     "thb_mlp_forward_backward_update": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_void_p,
                                                   C.c_char_p, C.c_uint64]),
+    "thb_mlp_set_reduction_format": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32]),
+    "thb_mlp_gather_parameters": (C.c_int, [C.c_void_p, C.c_uint32, C.c_void_p, C.c_char_p, C.c_uint64]),
     "thb_mlp_enable_timing": (C.c_int, [C.c_void_p, C.c_int]),
     "thb_mlp_read_timing": (C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
     "thb_sum_all_f32_noalloc": (C.c_int, [C.c_int, C.c_void_p, C.c_uint64, C.c_void_p, C.c_void_p, C.c_void_p,
@@ -274,6 +277,17 @@ class MlpSession:
         if lib().thb_mlp_bind_reduction(self.handle, which, peers, C.c_void_p(multicast_ptr), flags, rank,
                                         world) != STATUS_OK:
             raise GpuError(STATUS_ABI, "GPU-MLP-ARGUMENT: cannot bind the reduction target")
+
+    def set_reduction_format(self, which, fmt):
+        """THB_REDUCE_F32 or THB_REDUCE_BF16_SHARDED for the all-reduce of
+        `which` (MLP_DW1 / MLP_DW2), after bind_reduction."""
+        if lib().thb_mlp_set_reduction_format(self.handle, which, fmt) != STATUS_OK:
+            raise GpuError(STATUS_ABI, "GPU-MLP-ARGUMENT: cannot set the reduction format")
+
+    def gather_parameters(self, which, stream=0):
+        """Assembles this rank's f32 weights `which` (MLP_W1 / MLP_W2) from
+        their tile owners after bf16 sharded reductions."""
+        self._call("thb_mlp_gather_parameters", which, C.c_void_p(stream))
 
     def reduction_flag_words(self, which):
         """Number of u32 signal words bind_reduction needs for `which`."""

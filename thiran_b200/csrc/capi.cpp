@@ -1061,6 +1061,10 @@ int forwardBackwardCall(thb_mlp* s, const float* x, const float* t, const float*
         if (lr && !(s->b.dw1Reduce.update.paramPeers[0] && s->b.dw2Reduce.update.paramPeers[0]))
             fail(Category::Validation, "GPU-MLP-ARGUMENT",
                  "the fused update needs thb_mlp_bind_reduction and thb_mlp_bind_update for both layers");
+        if (!lr && (s->b.dw1Reduce.compact || s->b.dw2Reduce.compact))
+            fail(Category::Validation, "GPU-MLP-ARGUMENT",
+                 "a bf16 sharded reduction applies the optimizer step in the reduction: "
+                 "call thb_mlp_forward_backward_update");
         useDevice(s->device);
         // Each step's announcements raise every signal word by `world`.
         ++s->reduceEpoch;
@@ -1294,6 +1298,39 @@ int thb_mlp_bind_update(thb_mlp* s, uint32_t which, float* const* paramPeers, vo
     (which == THB_MLP_W1 ? s->b.w1b : s->b.w2b) = copyPeers[r.rank];
     r.update = u;
     return THB_STATUS_OK;
+}
+
+int thb_mlp_set_reduction_format(thb_mlp* s, uint32_t which, uint32_t format) {
+    if (!s || (which != THB_MLP_DW1 && which != THB_MLP_DW2) ||
+        (format != THB_REDUCE_F32 && format != THB_REDUCE_BF16_SHARDED))
+        return THB_STATUS_ABI;
+    auto& r = which == THB_MLP_DW1 ? s->b.dw1Reduce : s->b.dw2Reduce;
+    if (format == THB_REDUCE_BF16_SHARDED && !r.cPeers[0]) return THB_STATUS_ABI;
+    r.compact = format == THB_REDUCE_BF16_SHARDED;
+    return THB_STATUS_OK;
+}
+
+int thb_mlp_gather_parameters(thb_mlp* s, uint32_t which, void* stream, char* failure, uint64_t cap) {
+    return guarded(failure, cap, [&] {
+        if (!s || (which != THB_MLP_W1 && which != THB_MLP_W2))
+            fail(Category::Validation, "GPU-MLP-ARGUMENT", "null session or not a weight (THB_MLP_W1 / W2)");
+        const bool first = which == THB_MLP_W1;
+        const auto& r = first ? s->b.dw1Reduce : s->b.dw2Reduce;
+        if (!r.update.paramPeers[0])
+            fail(Category::Validation, "GPU-MLP-ARGUMENT", "no parameter binding (thb_mlp_bind_update) to gather from");
+        // The weight-gradient GEMM whose tile owners hold the parameters.
+        gemm::Problem q;
+        q.m = first ? s->b.in : s->b.hidden;
+        q.n = first ? s->b.hidden : s->b.out;
+        q.k = s->b.batch;
+        q.ldc = q.n;
+        q.epilogue = gemm::kEpiAllReduceF32;
+        q.reduce = r;
+        q.reduce.update.enabled = true;
+        useDevice(s->device);
+        cudaCheck(gemm::gatherOwned(q, s->smCount, static_cast<cudaStream_t>(stream)), "gather parameters");
+        return THB_STATUS_OK;
+    });
 }
 
 uint64_t thb_mlp_reduction_flag_words(thb_mlp* s, uint32_t which) {

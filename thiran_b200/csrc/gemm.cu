@@ -237,6 +237,7 @@ struct Params {
     // kEpiAllReduceF32 with the fused update: parameters and their bf16
     // copies on every rank (peer pointers; multicast in switch mode)
     uint32_t fusedUpdate;
+    uint32_t compact;               // bf16 payload, parameters sharded by tile owner (needs fusedUpdate)
     float* pPeers[kMaxRanks];
     __nv_bfloat16* pbPeers[kMaxRanks];
     float* pMc;
@@ -270,6 +271,24 @@ __device__ __forceinline__ void tileCoords(uint32_t tile, const Params& p, uint3
     const uint32_t local = tile % perGroup;
     mb = first + local % size;
     nb = local / size;
+}
+
+// Stores 32 consecutive results of a row as bf16 (16-byte vectors when the
+// chunk is whole and aligned; `left` = columns left in the row otherwise).
+__device__ __forceinline__ void storeBf16x32(__nv_bfloat16* dst, const float (&v)[32], bool full32, uint32_t left) {
+    if (full32 && reinterpret_cast<uintptr_t>(dst) % 16 == 0) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            uint4 packed;
+            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&packed);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
+            *reinterpret_cast<uint4*>(dst + q * 8) = packed;
+        }
+    } else {
+        for (uint32_t j = 0; j < 32; ++j)
+            if (j < left) dst[j] = __float2bfloat16_rn(v[j]);
+    }
 }
 
 template <int EPI>
@@ -507,6 +526,135 @@ __device__ __forceinline__ void peerReduceRows(const Params& p, uint64_t offset,
     }
 }
 
+// ---- compact form: bf16 payload, parameters sharded by tile owner ----
+
+__device__ __forceinline__ float2 unpackBf16x2(uint32_t bits) {
+    __nv_bfloat162 h;
+    *reinterpret_cast<uint32_t*>(&h) = bits;
+    return __bfloat1622float2(h);
+}
+
+__device__ __forceinline__ uint32_t packBf16x2(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// The compact update of 8 parameters at element offset `at` (32-byte
+// aligned in P, 16-byte in the bf16 copy) from their summed gradients g:
+// the owner's own f32 parameters (and velocities) are updated in place, and
+// the bf16 copy is written to every rank.
+__device__ __forceinline__ void updateCompact8(const Params& p, uint64_t at, const float (&g)[8], bool multicast) {
+    float* own = p.pPeers[p.rank] + at;
+    float4 w[2] = {__ldcg(reinterpret_cast<const float4*>(own)), __ldcg(reinterpret_cast<const float4*>(own + 4))};
+    float* wv = reinterpret_cast<float*>(w);
+    if (p.velocity) {
+        float4 m[2] = {*reinterpret_cast<const float4*>(p.velocity + at),
+                       *reinterpret_cast<const float4*>(p.velocity + at + 4)};
+        float* mv = reinterpret_cast<float*>(m);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) wv[e] = sgdStep(wv[e], g[e], &mv[e], p.lr, p.mu);
+        *reinterpret_cast<float4*>(p.velocity + at) = m[0];
+        *reinterpret_cast<float4*>(p.velocity + at + 4) = m[1];
+    } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) wv[e] = sgdStep(wv[e], g[e], nullptr, p.lr, p.mu);
+    }
+    *reinterpret_cast<float4*>(own) = w[0];
+    *reinterpret_cast<float4*>(own + 4) = w[1];
+    const uint4 b = make_uint4(packBf16x2(wv[0], wv[1]), packBf16x2(wv[2], wv[3]), packBf16x2(wv[4], wv[5]),
+                               packBf16x2(wv[6], wv[7]));
+    if (multicast) {
+        asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(p.pbMc + at), "r"(b.x),
+                     "r"(b.y), "r"(b.z), "r"(b.w)
+                     : "memory");
+    } else {
+        for (uint32_t k = 0; k < p.world; ++k) __stcg(reinterpret_cast<uint4*>(p.pbPeers[k] + at), b);
+    }
+}
+
+// Full-width rows of an owned tile in compact form: lane takes the 8
+// columns 8*lane .. 8*lane+7 of each row (one 16-byte bf16 vector per rank).
+// Switch mode keeps kCompactSwitchRows sums in flight per lane and unpacks
+// them one row at a time; peer mode sums kCompactPeerRows rows of every rank
+// in f32, in rank order. (The row counts keep the reducer inside the
+// kernel's register budget.)
+constexpr uint32_t kCompactSwitchRows = 2;
+constexpr uint32_t kCompactPeerRows = 1;
+
+__device__ __forceinline__ void unpack8(const uint4& v, float (&g)[8]) {
+    const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float2 f = unpackBf16x2(words[q]);
+        g[2 * q] = f.x;
+        g[2 * q + 1] = f.y;
+    }
+}
+
+__device__ __forceinline__ void compactReduceRows(const Params& p, uint64_t offset, uint32_t rows, uint32_t lane) {
+    if (p.cMc) {
+        const __nv_bfloat16* mc = reinterpret_cast<const __nv_bfloat16*>(p.cMc) + offset + 8u * lane;
+        for (uint32_t r0 = 0; r0 < rows; r0 += kCompactSwitchRows) {
+            uint4 v[kCompactSwitchRows];
+#pragma unroll
+            for (uint32_t i = 0; i < kCompactSwitchRows; ++i) {
+                if (r0 + i < rows)
+                    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+                                 : "=r"(v[i].x), "=r"(v[i].y), "=r"(v[i].z), "=r"(v[i].w)
+                                 : "l"(mc + (r0 + i) * p.ldc)
+                                 : "memory");
+            }
+#pragma unroll
+            for (uint32_t i = 0; i < kCompactSwitchRows; ++i) {
+                if (r0 + i < rows) {
+                    float g[8];
+                    unpack8(v[i], g);
+                    updateCompact8(p, offset + (r0 + i) * p.ldc + 8u * lane, g, true);
+                }
+            }
+        }
+        return;
+    }
+    for (uint32_t r0 = 0; r0 < rows; r0 += kCompactPeerRows) {
+        float acc[kCompactPeerRows][8];
+#pragma unroll
+        for (uint32_t i = 0; i < kCompactPeerRows; ++i)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[i][e] = 0.0f;
+        for (uint32_t k = 0; k < p.world; ++k) {
+            const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(p.cPeers[k]) + offset + 8u * lane;
+            uint4 v[kCompactPeerRows];
+#pragma unroll
+            for (uint32_t i = 0; i < kCompactPeerRows; ++i)
+                if (r0 + i < rows) v[i] = __ldcg(reinterpret_cast<const uint4*>(src + (r0 + i) * p.ldc));
+#pragma unroll
+            for (uint32_t i = 0; i < kCompactPeerRows; ++i) {
+                float g[8];
+                unpack8(v[i], g);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[i][e] = __fadd_rn(acc[i][e], g[e]);
+            }
+        }
+#pragma unroll
+        for (uint32_t i = 0; i < kCompactPeerRows; ++i)
+            if (r0 + i < rows) updateCompact8(p, offset + (r0 + i) * p.ldc + 8u * lane, acc[i], false);
+    }
+}
+
+// One element of a ragged tile edge in compact form: the ranks' bf16 values
+// summed in f32 in rank order by peer loads, the owner's parameter updated,
+// the bf16 copy stored to every rank.
+__device__ __forceinline__ void compactReduceScalar(const Params& p, uint64_t at) {
+    float x = 0.0f;
+    for (uint32_t k = 0; k < p.world; ++k)
+        x = __fadd_rn(x, __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.cPeers[k])[at]));
+    float* own = p.pPeers[p.rank] + at;
+    const float w = sgdStep(__ldcg(own), x, p.velocity ? p.velocity + at : nullptr, p.lr, p.mu);
+    *own = w;
+    const __nv_bfloat16 b = __float2bfloat16_rn(w);
+    for (uint32_t k = 0; k < p.world; ++k) p.pbPeers[k][at] = b;
+}
+
 // Sums this warp's 32 rows of an owned tile over all ranks and writes the
 // totals to every rank, once all ranks have announced them. Ragged edge
 // tiles go element by element.
@@ -521,6 +669,15 @@ __device__ __forceinline__ bool reduceRows(const Params& p, uint32_t tile, uint3
     const uint32_t rows = p.m - row0 < 32 ? static_cast<uint32_t>(p.m - row0) : 32u;
     const uint32_t cols = p.n - col0 < kBN ? static_cast<uint32_t>(p.n - col0) : kBN;
     const uint64_t offset = row0 * p.ldc + col0;
+    if (p.compact) {
+        if (cols == kBN) {
+            compactReduceRows(p, offset, rows, lane);
+        } else {
+            for (uint32_t r = 0; r < rows; ++r)
+                for (uint32_t c = lane; c < cols; c += 32) compactReduceScalar(p, offset + r * p.ldc + c);
+        }
+        return true;
+    }
     if (cols == kBN) {
         if (p.cMc) switchReduceRows(p, offset, rows, lane);
         else peerReduceRows(p, offset, rows, lane);
@@ -922,30 +1079,23 @@ __global__ void __launch_bounds__(threadsFor(EPI), 1)
                         }
                     }
                 } else if constexpr (EPI == kEpiF32 || EPI == kEpiAllReduceF32) {
-                    float* dst = static_cast<float*>(p.c) + grow * p.ldc + col0;
-                    if (full32 && reinterpret_cast<uintptr_t>(dst) % 16 == 0) {
-#pragma unroll
-                        for (int q = 0; q < 8; ++q)
-                            *reinterpret_cast<float4*>(dst + 4 * q) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                    if (EPI == kEpiAllReduceF32 && p.compact) {
+                        // Compact all-reduce: the rank's tile travels as bf16.
+                        storeBf16x32(static_cast<__nv_bfloat16*>(p.c) + grow * p.ldc + col0, v, full32, p.n - col0);
                     } else {
-                        for (int j = 0; j < 32; ++j)
-                            if (col0 + j < p.n) dst[j] = v[j];
+                        float* dst = static_cast<float*>(p.c) + grow * p.ldc + col0;
+                        if (full32 && reinterpret_cast<uintptr_t>(dst) % 16 == 0) {
+#pragma unroll
+                            for (int q = 0; q < 8; ++q)
+                                *reinterpret_cast<float4*>(dst + 4 * q) =
+                                    make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                        } else {
+                            for (int j = 0; j < 32; ++j)
+                                if (col0 + j < p.n) dst[j] = v[j];
+                        }
                     }
                 } else {
-                    __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.c) + grow * p.ldc + col0;
-                    if (full32 && reinterpret_cast<uintptr_t>(dst) % 16 == 0) {
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            uint4 packed;
-                            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&packed);
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
-                            *reinterpret_cast<uint4*>(dst + q * 8) = packed;
-                        }
-                    } else {
-                        for (int j = 0; j < 32; ++j)
-                            if (col0 + j < p.n) dst[j] = __float2bfloat16_rn(v[j]);
-                    }
+                    storeBf16x32(static_cast<__nv_bfloat16*>(p.c) + grow * p.ldc + col0, v, full32, p.n - col0);
                     if (p.c2) {
                         float* dst2 = static_cast<float*>(p.c2) + grow * p.ldc + col0;
                         for (int j = 0; j < 32; ++j)
@@ -993,6 +1143,16 @@ __global__ void __launch_bounds__(threadsFor(EPI), 1)
         else
             asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmemBase), "r"(kTmemCols) : "memory");
     }
+}
+
+// m-blocks per raster group (THB_GEMM_GROUP overrides the default 16).
+uint32_t rasterGroup() {
+    static const uint32_t group = [] {
+        const char* e = std::getenv("THB_GEMM_GROUP");
+        const long g = e ? std::atol(e) : 0;
+        return static_cast<uint32_t>(g > 0 && g <= 1024 ? g : 16);
+    }();
+    return group;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encodeFn() {
@@ -1140,6 +1300,15 @@ const char* validate(const Problem& q) {
             if ((reinterpret_cast<uintptr_t>(u.paramMulticast) % 16) || (reinterpret_cast<uintptr_t>(u.copyMulticast) % 8))
                 return "multicast parameters must be 16-byte and their copy 8-byte aligned";
         }
+        if (r.compact) {
+            if (!u.enabled) return "the compact all-reduce applies the update in the reduction";
+            if (q.ldc % 8) return "the compact all-reduce needs ldc a multiple of 8 (16-byte bf16 rows)";
+            for (uint32_t k = 0; k < r.world; ++k)
+                if (reinterpret_cast<uintptr_t>(u.copyPeers[k]) % 16)
+                    return "the compact all-reduce needs 16-byte aligned bf16 copies";
+            if (reinterpret_cast<uintptr_t>(u.copyMulticast) % 16)
+                return "the compact all-reduce needs a 16-byte aligned multicast copy";
+        }
     }
     return nullptr;
 }
@@ -1167,12 +1336,7 @@ cudaError_t run(const Problem& q, int smCount, uint32_t* status, cudaStream_t st
     // two GEMMs with N=16384 by a third against 8 (H = X W1: 614 -> 399 MB
     // per launch), and the step measured best of 2, 4, 8, 16 and 32.
     // THB_GEMM_GROUP overrides.
-    static const uint32_t group = [] {
-        const char* e = std::getenv("THB_GEMM_GROUP");
-        const long g = e ? std::atol(e) : 0;
-        return static_cast<uint32_t>(g > 0 && g <= 1024 ? g : 16);
-    }();
-    p.group = group;
+    p.group = rasterGroup();
     p.c = q.c;
     p.ldc = q.ldc;
     p.aux = static_cast<const __nv_bfloat16*>(q.aux);
@@ -1198,6 +1362,7 @@ cudaError_t run(const Problem& q, int smCount, uint32_t* status, cudaStream_t st
     p.mu = q.update.momentum;
     const ReduceUpdate& u = q.reduce.update;
     p.fusedUpdate = q.epilogue == kEpiAllReduceF32 && u.enabled ? 1u : 0u;
+    p.compact = p.fusedUpdate && q.reduce.compact ? 1u : 0u;
     if (p.fusedUpdate) {
         p.velocity = u.momentum > 0.0f ? u.velocity : nullptr;
         p.lr = u.lr;
@@ -1217,4 +1382,50 @@ cudaError_t run(const Problem& q, int smCount, uint32_t* status, cudaStream_t st
     return launchEpi<false, false>(q.epilogue, pair, a, b, p, stream);
 }
 
+namespace {
+
+// One CTA per tile of P: tiles owned by another rank are copied from the
+// owner's parameters (the same tile order and owner map as gemmKernel).
+__global__ void __launch_bounds__(256) gatherOwnedKernel(const Params p, float* __restrict__ own) {
+    const uint32_t tile = blockIdx.x;
+    const uint32_t owner = tileOwner(p, tile);
+    if (owner == p.rank) return;
+    uint32_t mb, nb;
+    tileCoords(tile, p, mb, nb);
+    const uint64_t row0 = static_cast<uint64_t>(mb) * kBM, col0 = static_cast<uint64_t>(nb) * kBN;
+    const float* src = p.pPeers[owner];
+    for (uint32_t e = threadIdx.x; e < kBM * kBN; e += blockDim.x) {
+        const uint64_t r = row0 + e / kBN, c = col0 + e % kBN;
+        if (r < p.m && c < p.n) own[r * p.ldc + c] = __ldcg(src + r * p.ldc + c);
+    }
+}
+
+} // namespace
+
+cudaError_t gatherOwned(const Problem& q, int smCount, cudaStream_t stream) {
+    const AllReduce& r = q.reduce;
+    if (q.epilogue != kEpiAllReduceF32 || !r.update.enabled || r.world == 0 || r.rank >= r.world ||
+        !r.update.paramPeers[r.rank])
+        return cudaErrorInvalidValue;
+    // The fused all-reduce runs on single CTAs (128 x 256 tiles); the map
+    // must match gemm::run's for this problem.
+    if (usePairs(q)) return cudaErrorInvalidValue;
+    Params p{};
+    p.m = static_cast<uint32_t>(q.m);
+    p.n = static_cast<uint32_t>(q.n);
+    p.mTiles = static_cast<uint32_t>((q.m + kBM - 1) / kBM);
+    p.nTiles = static_cast<uint32_t>((q.n + kBN - 1) / kBN);
+    p.group = rasterGroup();
+    p.ldc = q.ldc;
+    p.rank = r.rank;
+    p.world = r.world;
+    const uint32_t tiles = p.mTiles * p.nTiles;
+    p.grid = tiles < static_cast<uint32_t>(smCount) ? tiles : static_cast<uint32_t>(smCount);
+    for (int k = 0; k < kMaxRanks; ++k) p.pPeers[k] = r.update.paramPeers[k];
+    if (tiles == 0) return cudaSuccess;
+    gatherOwnedKernel<<<tiles, 256, 0, stream>>>(p, r.update.paramPeers[r.rank]);
+    return cudaGetLastError();
+}
+
 } // namespace thb::gemm
+

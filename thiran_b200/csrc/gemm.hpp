@@ -63,12 +63,22 @@ struct ReduceUpdate {
     float lr = 0.0f, momentum = 0.0f;
 };
 
+// Compact form of the fused update (`compact`, needs update.enabled): each
+// rank stores its tile as bf16 (C is then bf16 [M][ldc]); the owner sums the
+// ranks' bf16 tiles with f32 accumulation (multimem.ld_reduce ...
+// .acc::f32.v4.bf16x2 in switch mode, f32 sums of peer loads in rank order
+// in peer mode), applies the update to its own f32 parameters only, and
+// writes the bf16 copy to every rank. The f32 parameters are thereby sharded
+// by tile owner (every rank's copy of a tile it does not own goes stale;
+// gatherOwned assembles them), and each element costs about 2 bytes of
+// NVLink traffic per direction instead of 10.
 struct AllReduce {
     void* cMulticast = nullptr;                   // switch mode: NVLS multicast address of C
     void* cPeers[kMaxRanks] = {};                 // C as mapped on this GPU, for every rank
     std::uint32_t* flagsPeers[kMaxRanks] = {};    // signal words (4 per tile), for every rank
     std::uint32_t rank = 0, world = 1;
     std::uint32_t target = 0;                     // each signal word's value once this launch's ranks all announced
+    bool compact = false;                         // bf16 payload, parameters sharded by tile owner
     ReduceUpdate update;
 };
 
@@ -107,5 +117,12 @@ std::uint64_t colSumRows(std::uint64_t m);
 const char* validate(const Problem&);
 // Launches on `stream`; `status` receives bit 4 when a bounded wait expired.
 cudaError_t run(const Problem&, int smCount, std::uint32_t* status, cudaStream_t stream);
+
+// For a compact fused update (AllReduce::compact): copies every tile this
+// rank does not own from its owner's f32 parameters (reduce.update.
+// paramPeers[owner], plain peer loads) into this rank's, so that this rank
+// holds the full parameters again. The tile-to-owner map is the one `run`
+// uses for the same problem on `smCount` SMs.
+cudaError_t gatherOwned(const Problem&, int smCount, cudaStream_t stream);
 
 } // namespace thb::gemm

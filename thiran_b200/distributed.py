@@ -62,12 +62,16 @@ class FusedGradientAllReduce:
 
     BARRIER_TIMEOUT_MS = 60000
 
-    def __init__(self, session, dist, group=None, mode=None, update=False):
+    def __init__(self, session, dist, group=None, mode=None, update=False, compact=False):
         """`update=True` also moves W1, W2 and their bf16 copies into
         symmetric memory (thb_mlp_bind_update), so that a step can run
         session.forward_backward_update(): each tile's owner applies the
         optimizer step in the reduction and writes the new weights to every
-        rank."""
+        rank. `compact=True` (needs `update`) reduces bf16 gradient tiles
+        and keeps each tile's f32 weights on its owner only, broadcasting
+        just the bf16 copy (THB_REDUCE_BF16_SHARDED): about a fifth of the
+        NVLink bytes; gather_parameters() or close() assembles the f32
+        weights."""
         import torch
         import torch.distributed._symmetric_memory as symm_mem
         from . import MLP_DW1, MLP_DW2, MLP_W1, MLP_W2
@@ -76,6 +80,9 @@ class FusedGradientAllReduce:
         self.mode = mode or fused_reduction_mode(world)
         if self.mode not in ("peer", "switch"):
             raise ValueError(f"unknown fused all-reduce mode {self.mode!r}")
+        if compact and not update:
+            raise ValueError("the compact reduction applies the optimizer step in the reduction (update=True)")
+        self.compact = bool(compact)
         self.buffers, self.handles = [], []
         shapes = [(MLP_DW1, (session.d_in, session.hidden)), (MLP_DW2, (session.hidden, session.d_out))]
         words = [session.reduction_flag_words(which) for which, _ in shapes]
@@ -83,7 +90,7 @@ class FusedGradientAllReduce:
         self.flags.zero_()
         self.flag_handle = symm_mem.rendezvous(self.flags, self.group)
         for which, shape in shapes:
-            t = symm_mem.empty(shape, dtype=torch.float32, device="cuda")
+            t = symm_mem.empty(shape, dtype=torch.bfloat16 if self.compact else torch.float32, device="cuda")
             h = symm_mem.rendezvous(t, self.group)
             self.buffers.append((which, t))
             self.handles.append(h)
@@ -107,6 +114,9 @@ class FusedGradientAllReduce:
             for ((which, t), h), n in zip(zip(self.buffers, self.handles), words):
                 session.bind_reduction(which, [int(p) for p in h.buffer_ptrs], [p + 4 * offset for p in flag_ptrs],
                                        rank, world, h.multicast_ptr if switch else None)
+                if self.compact:
+                    from . import REDUCE_BF16_SHARDED
+                    session.set_reduction_format(which, REDUCE_BF16_SHARDED)
                 offset += n
             if self.update:
                 # The session's current weights move into the symmetric
@@ -137,6 +147,14 @@ class FusedGradientAllReduce:
         if not self.available or self.session is None:
             return
         weights = [pair[0][0] for _, pair in self.param_handles]
+        if self.compact:
+            # Each rank holds only its tiles' f32 weights: assemble them all,
+            # and let every rank finish reading its peers before any rebinds.
+            stream = torch.cuda.current_stream()
+            for which, _ in self.param_handles:
+                self.session.gather_parameters(which, stream.cuda_stream)
+            stream.synchronize()
+            self.flag_handle.barrier(channel=0, timeout_ms=self.BARRIER_TIMEOUT_MS)
         for which, _ in self.param_handles:
             self.session.bind_update(which, None, None)
         for which in (MLP_DW1, MLP_DW2):
@@ -146,6 +164,17 @@ class FusedGradientAllReduce:
             self.session.set_weight_pointers(weights[0].data_ptr(), weights[1].data_ptr(), stream.cuda_stream)
             stream.synchronize()
         self.session = None
+
+    def gather_parameters(self):
+        """With `compact`: this rank's f32 W1 and W2 (the symmetric buffers)
+        assembled from their tile owners; every rank calls it between steps."""
+        import torch
+        stream = torch.cuda.current_stream()
+        for which, _ in self.param_handles:
+            self.session.gather_parameters(which, stream.cuda_stream)
+        stream.synchronize()
+        self.flag_handle.barrier(channel=0, timeout_ms=self.BARRIER_TIMEOUT_MS)
+        return [pair[0][0] for _, pair in self.param_handles]
 
     def after_backward(self):
         """Wait until every rank's owned tiles hold their totals everywhere;
