@@ -138,3 +138,33 @@ def test_extension_gradient_recipe_on_the_engine(drivers, tmp_path):
     assert status and status["status"] == "ok", out
     got, ref = read_thb(str(tmp_path / "o_grad0.bin")), read_thb(str(tmp_path / "o_ref_grad0.bin"))
     assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("stem", ["ref_f32_chain", "ref_f32_chain_nofusion", "ref_i64_region",
+                                  "ref_i64_region_nofusion"])
+def test_reference_artifacts_through_load_and_execute(drivers, tmp_path, stem):
+    """The reference's own GPU artifacts (buildGpuAot) through the binding's
+    loadAndExecuteArtifact: the reference loader validates them, the region
+    runs on the engine, bit-exact against the oracle."""
+    import oracle_lib
+    from shim_programs import write_thb
+    from thiran_b200 import regions
+    import subprocess
+    rng = np.random.default_rng(9)
+    if "f32" in stem:
+        inputs = [rng.uniform(-1, 1, 4099).astype(np.float32)]
+        spec = regions.f32_chain()
+    else:
+        inputs = [rng.integers(-1000, 1001, (37, 129), dtype=np.int64) for _ in range(2)]
+        spec = regions.i64_region()
+    paths = []
+    for k, v in enumerate(inputs):
+        write_thb(str(tmp_path / f"in{k}.bin"), v)
+        paths.append(str(tmp_path / f"in{k}.bin"))
+    golden = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", f"{stem}.tha")
+    res = subprocess.run([DRIVER, "artifact", golden, "0", str(tmp_path / "o.bin")] + paths, capture_output=True,
+                         text=True)
+    assert '"status":"ok"' in res.stdout, res.stdout
+    got = read_thb(str(tmp_path / "o.bin"))
+    want = oracle_lib.region_eval(spec, inputs)
+    assert got.dtype == want.dtype and np.array_equal(got.view(np.uint8), want.view(np.uint8))

@@ -86,3 +86,26 @@ def test_unsupported_forms_are_diagnosed(driver, tmp_path):
     program = "fn f(x: Tensor<f32,2>) -> Tensor<f32,2> { return x[0:2, :] }"
     out, _ = lowered(tmp_path, program, "f")
     assert out.startswith("BACKEND-UNSUPPORTED"), out
+
+
+def test_artifact_path_validates_then_needs_a_device(driver, tmp_path):
+    """`thiran run --backend gpu file.tha`: the reference's loader checks the
+    container, the region then needs the engine's device."""
+    torch = pytest.importorskip("torch")
+    import numpy as np
+    from shim_programs import write_thb
+    x = np.ones(64, np.float32)
+    write_thb(str(tmp_path / "x.bin"), x)
+    golden = os.path.join(ROOT, "tests", "golden", "ref_f32_chain.tha")
+    res = subprocess.run([DRIVER, "artifact", golden, "0", str(tmp_path / "o.bin"), str(tmp_path / "x.bin")],
+                         capture_output=True, text=True)
+    if not torch.cuda.is_available():
+        assert '"code":"GPU-DRIVER-NOT-FOUND"' in res.stdout, res.stdout
+    # A corrupted payload is the loader's failure, before any device work.
+    data = bytearray(open(golden, "rb").read())
+    data[-5] ^= 0xFF
+    bad = tmp_path / "bad.tha"
+    bad.write_bytes(bytes(data))
+    res = subprocess.run([DRIVER, "artifact", str(bad), "0", str(tmp_path / "o.bin"), str(tmp_path / "x.bin")],
+                         capture_output=True, text=True)
+    assert '"status":"error"' in res.stdout and "ARTIFACT-" in res.stdout, res.stdout

@@ -565,4 +565,35 @@ GpuDeviceInfo probeNativeGpu(int device) noexcept {
     return info;
 }
 
+artifact::ArtifactExecutionResult loadAndExecuteArtifact(const std::string& path,
+                                                         const std::vector<artifact::ArtifactValue>& inputs,
+                                                         int device) noexcept {
+    artifact::ArtifactExecutionResult result;
+    try {
+        auto loaded = artifact::loadArtifact(path);
+        if (!loaded.ok()) {
+            result.error = loaded.error;
+            return result;
+        }
+        const auto& a = *loaded.artifact;
+        if (a.manifest.backend != artifact::NativeBackend::Gpu) {
+            result.error = artifact::ArtifactError{artifact::ArtifactErrorCategory::Execution, "ARTIFACT-BACKEND",
+                                                   "not a GPU artifact"};
+            return result;
+        }
+        auto run = b200::executeNativeGpu(a.region, inputs, device, a.manifest.planning);
+        result.gpuEvidence = run.evidence;
+        if (!run.ok()) {
+            result.error = artifact::ArtifactError{artifact::ArtifactErrorCategory::Execution, run.error->code,
+                                                   run.error->message};
+            return result;
+        }
+        result.value = std::move(run.value);
+    } catch (const std::exception& e) {
+        result.value.reset();
+        result.error = artifact::ArtifactError{artifact::ArtifactErrorCategory::Execution, "GPU-INTERNAL", e.what()};
+    }
+    return result;
+}
+
 } // namespace thiran::v0::backend::b200

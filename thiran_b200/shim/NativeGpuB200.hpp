@@ -5,7 +5,7 @@
 // engine's C ABI (include/thiran_b200.h), and keeps the reference's types on
 // its side of the boundary.
 //
-// Two entry points:
+// Entry points (plus probeNativeGpu and loadAndExecuteArtifact below):
 //  - lowerFunction: a function of a verified semantic module becomes an
 //    engine region. It admits what extractStrictRegion admits
 //    (src/backend/v0/TensorRegion.cpp:230-447) and also the operations the
@@ -22,6 +22,7 @@
 #pragma once
 
 #include "analysis/v0/Ownership.hpp"
+#include "artifact/v0/NativeArtifacts.hpp"
 #include "backend/v0/NativeGpu.hpp"
 #include "semantic/v0/Ir.hpp"
 #include "thiran_b200.h"
@@ -85,5 +86,19 @@ GpuExecutionResult executeNativeGpu(const TensorRegion& region, const std::vecto
 
 // probeNativeGpu (NativeGpu.hpp:102) over the engine.
 GpuDeviceInfo probeNativeGpu(int device) noexcept;
+
+// The GPU branch of artifact::loadAndExecuteArtifact
+// (include/artifact/v0/NativeArtifacts.hpp:138-139), which `thiran run
+// --backend gpu <file.tha>` reaches: the reference's loader validates the
+// container (digests, signature, region), and a GPU artifact's region runs
+// on the engine (its PTX payload is digest-checked by the loader but not
+// executed). A CPU artifact is refused with ARTIFACT-BACKEND (the reference
+// keeps running those itself). Artifacts this engine built (payload kind 3,
+// an sm_100a cubin) are outside the reference's loader; engine-aware callers
+// load them with thb_artifact_load_file. Failures come back as ArtifactError
+// with the reference's ids.
+artifact::ArtifactExecutionResult loadAndExecuteArtifact(const std::string& path,
+                                                         const std::vector<artifact::ArtifactValue>& inputs,
+                                                         int device) noexcept;
 
 } // namespace thiran::v0::backend::b200

@@ -9,6 +9,8 @@
 //       lowerFunction + executeLowered; writes the result.
 //   shim_driver native <program.th> <function> <device> <out.bin> [in.bin ...]
 //       the reference's extractStrictGpu region through b200::executeNativeGpu.
+//   shim_driver artifact <file.tha> <device> <out.bin> [in.bin ...]
+//       loadAndExecuteArtifact: the reference's loader, the region on the engine.
 //   shim_driver vjp <program.th> <function> <exact|tensor> <device> <out-prefix> <cotangent.bin> [in.bin ...]
 //       autodiff::differentiate over every parameter; the generated forward
 //       function runs on the engine one tuple element (primal, saved values)
@@ -237,6 +239,21 @@ int main(int argc, char** argv) {
             return 64;
         }
         const std::string mode = argv[1];
+        if (mode == "artifact") {
+            // shim_driver artifact <file.tha> <device> <out.bin> [in.bin ...]
+            if (argc < 5) throw std::runtime_error("artifact needs a device and an output path");
+            std::vector<b::GpuValue> inputs;
+            for (int k = 5; k < argc; ++k) inputs.push_back(readValue(argv[k]));
+            const auto r = g::loadAndExecuteArtifact(argv[2], inputs, std::stoi(argv[3]));
+            if (!r.ok()) {
+                std::cout << "{\"status\":\"error\",\"code\":\"" << r.error->code << "\"}\n";
+                return 0;
+            }
+            writeValue(argv[4], *r.value);
+            std::cout << "{\"status\":\"ok\",\"kernel_launches\":"
+                      << (r.gpuEvidence ? r.gpuEvidence->kernelLaunches : 0) << "}\n";
+            return 0;
+        }
         e::ExtensionRegistry registry;
         if (auto r = registry.registerExtension(kExtension); !r.ok()) throw std::runtime_error(r.message);
         const s::Module module = compile(readText(argv[2]), registry);
