@@ -227,3 +227,74 @@ def test_mlp_fused_update_step_is_bit_identical(device, batch, d_in, hidden, d_o
     assert plain_losses == fused_losses
     for k in plain:
         assert torch.equal(plain[k].view(torch.int32), fused_p[k].view(torch.int32)), k
+
+
+def test_compact_reduction_on_one_rank(device):
+    """The bf16 sharded reduction's kernels on a world of one (every tile
+    owned here, the ranks' bf16 tiles read back through the peer path): three
+    steps follow the single-process f32 step and the oracle, and the bf16
+    weight copies are the rounding of the f32 weights."""
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(31)
+    batch, d_in, hidden, d_out = 384, 256, 520, 136   # a ragged N tile in both layers
+    x = rng.standard_normal((batch, d_in)).astype(np.float32)
+    t = rng.standard_normal((batch, d_out)).astype(np.float32)
+    w1, w2 = xavier(rng, d_in, hidden), xavier(rng, hidden, d_out)
+    b1 = (rng.standard_normal(hidden) * 0.1).astype(np.float32)
+    b2 = (rng.standard_normal(d_out) * 0.1).astype(np.float32)
+    lr, momentum = 0.1, 0.9
+    cuda = lambda a: torch.from_numpy(a).cuda()
+    X, T = cuda(x), cuda(t)
+
+    def make():
+        s = thb.MlpSession(batch, d_in, hidden, d_out)
+        s.set_weights(cuda(w1), cuda(w2))
+        s.set_biases(cuda(b1), cuda(b2))
+        s.set_momentum(momentum)
+        return s, {"b1": s.bind(thb.MLP_B1, cuda(b1)), "b2": s.bind(thb.MLP_B2, cuda(b2))}
+
+    plain, pp = make()
+    pp["w1"] = plain.bind(thb.MLP_W1, cuda(w1))
+    pp["w2"] = plain.bind(thb.MLP_W2, cuda(w2))
+    plain.set_weights(cuda(w1), cuda(w2))
+    for _ in range(3):
+        plain.forward_backward(X, T)
+        plain.apply_sgd(lr)
+
+    s, cp = make()
+    grads = {thb.MLP_DW1: torch.empty((d_in, hidden), dtype=torch.bfloat16, device="cuda"),
+             thb.MLP_DW2: torch.empty((hidden, d_out), dtype=torch.bfloat16, device="cuda")}
+    flags = {k: torch.zeros(s.reduction_flag_words(k), dtype=torch.int32, device="cuda") for k in grads}
+    for k, g in grads.items():
+        s.bind_reduction(k, [g.data_ptr()], [flags[k].data_ptr()], 0, 1)
+        s.set_reduction_format(k, thb.REDUCE_BF16_SHARDED)
+    params = {thb.MLP_W1: (torch.empty((d_in, hidden), device="cuda"),
+                           torch.empty((d_in, hidden), dtype=torch.bfloat16, device="cuda")),
+              thb.MLP_W2: (torch.empty((hidden, d_out), device="cuda"),
+                           torch.empty((hidden, d_out), dtype=torch.bfloat16, device="cuda"))}
+    for k, (p, c) in params.items():
+        s.bind_update(k, [p.data_ptr()], [c.data_ptr()])
+    s.set_weights(cuda(w1), cuda(w2))
+    s.set_momentum(momentum)
+    with pytest.raises(thb.GpuError):  # the compact form needs the update in the reduction
+        s.forward_backward(X, T)
+    for _ in range(3):
+        s.forward_backward_update(X, T, lr)
+        s.apply_sgd(lr)
+    for k in params:
+        s.gather_parameters(k)
+    thb.check_device_status(0)
+    torch.cuda.synchronize()
+    got = {"w1": params[thb.MLP_W1][0], "w2": params[thb.MLP_W2][0], "b1": cp["b1"], "b2": cp["b2"]}
+    for k in ("w1", "w2", "b1", "b2"):
+        assert rel(got[k].cpu().numpy(), pp[k].cpu().numpy()) <= 1e-3, k
+    ws = [w1.copy(), w2.copy(), b1.copy(), b2.copy()]
+    vel = [np.zeros_like(a) for a in (w1, b1, w2, b2)]
+    for _ in range(3):
+        orc.mlp_step_ex(x, t, ws[0], ws[1], lr, ws[2], ws[3], momentum, vel)
+    for k, ref in zip(("w1", "w2", "b1", "b2"), ws):
+        assert rel(got[k].cpu().numpy(), ref) <= 1e-3, k
+    for k, (p, c) in params.items():
+        assert torch.equal(c, p.to(torch.bfloat16)), k
+    s.release()
+    plain.release()
