@@ -42,3 +42,26 @@ def test_reference_arm_under_torchrun_prints_once():
     assert out.returncode == 0, out.stderr[-2000:]
     lines = [json.loads(l) for l in out.stdout.splitlines() if l.startswith("{")]
     assert len(lines) == 1 and lines[0]["impl"] == "reference" and lines[0]["n_gpus"] == 2
+
+
+def test_nvlink_byte_model():
+    """The bytes per step the MLP line states for each gradient exchange: the
+    compact switch form moves 2 B per weight element each way, a fifth of the
+    f32 form with the update at 8 ranks; NCCL's ring 2(w-1)/w x 4 B."""
+    sys.path.insert(0, ROOT)
+    import bench
+
+    class Fused:
+        def __init__(self, mode, update, compact):
+            self.mode, self.update, self.compact = mode, update, compact
+
+    e = 2 * 4096 * 16384
+    assert bench.nvlink_bytes_per_step(1, e, None) is None
+    compact = bench.nvlink_bytes_per_step(8, e, Fused("switch", True, True))
+    assert compact["in"] == compact["out"] == 2 * e
+    f32 = bench.nvlink_bytes_per_step(8, e, Fused("switch", True, False))
+    assert f32["in"] == int((4 / 8 + 6 * 7 / 8) * e) and f32["out"] == int((4 * 7 / 8 + 6 / 8) * e)
+    nccl = bench.nvlink_bytes_per_step(8, e, None)
+    assert nccl["in"] == int(2 * 7 / 8 * 4 * e)
+    peer = bench.nvlink_bytes_per_step(2, e, Fused("peer", True, True))
+    assert peer["in"] == 2 * e
