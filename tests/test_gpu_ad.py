@@ -107,6 +107,7 @@ def test_matmul_region_against_reference(device, golden):
     bm = rng.standard_normal((512, 264)).astype(np.float32)
     out = spec.compile(device).execute([a, bm])
     assert rel(out, orc.matmul_f64acc(a, bm)) <= 2e-2
-    with pytest.raises(thb.GpuError) as err:
-        spec.compile(device).execute([np.ascontiguousarray(a[:, :500]), bm[:500].copy()])  # K % 8 != 0
-    assert err.value.code == "GPU-UNSUPPORTED-SHAPE"
+    # K % 8 != 0: the operands are zero-padded to 16-byte rows in the bf16 cast.
+    a5, b5 = np.ascontiguousarray(a[:, :500]), bm[:500].copy()
+    out = spec.compile(device).execute([a5, b5])
+    assert rel(out, orc.matmul_f64acc(a5, b5)) <= 2e-2
