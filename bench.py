@@ -214,7 +214,11 @@ def run_mlp(args, workload, torch, dist, thb, world, rank, local, barrier, max_o
         # 2.141 vs 2.204 ms per step) and loses in peer mode (2 ranks 2.87
         # vs 2.79 ms).
         switch = (mode or fused_reduction_mode(world)) == "switch"
-        compact = args.dp_format == "bf16-sharded"
+        # Measured at 2 ranks (peer mode): 2.907 ms per step compact against
+        # 2.795 ms for f32 gradients with the separate update pass, so
+        # 'auto' keeps the compact form for switch mode, where the step is
+        # bound by NVLink bytes.
+        compact = args.dp_format == "bf16-sharded" or (args.dp_format == "auto" and switch)
         update = compact or args.dp_update == "fused" or (args.dp_update == "auto" and switch)
         with torch.cuda.stream(stream):
             fused = FusedGradientAllReduce(session, dist, mode=mode, update=update, compact=compact)
@@ -670,9 +674,10 @@ def main():
                    help="with a fused all-reduce: apply the optimizer step in the reduction (each tile's owner; "
                         "'auto' does so in switch mode, where it measured faster) or run the separate update pass "
                         "on every rank (faster in peer mode, 2 ranks)")
-    p.add_argument("--dp-format", default="bf16-sharded", choices=["bf16-sharded", "f32"],
+    p.add_argument("--dp-format", default="auto", choices=["auto", "bf16-sharded", "f32"],
                    help="with a fused all-reduce: bf16 gradient tiles and f32 weights sharded by tile owner (only "
-                        "the bf16 weights are broadcast), or f32 gradients and replicated f32 weights")
+                        "the bf16 weights are broadcast), or f32 gradients and replicated f32 weights; 'auto' "
+                        "takes the bf16 form in switch mode (from 3 ranks)")
     p.add_argument("--shrink", type=int, default=1,
                    help="divide the leading extent (small cases for profiler captures; not a bench line)")
     args = p.parse_args()
