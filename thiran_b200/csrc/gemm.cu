@@ -528,48 +528,71 @@ __device__ __forceinline__ void peerReduceRows(const Params& p, uint64_t offset,
 
 // ---- compact form: bf16 payload, parameters sharded by tile owner ----
 
+// bf16 pairs in a 32-bit word (element 0 in the low half). Widening to f32
+// is exact: the bf16 bits are the f32's upper half.
 __device__ __forceinline__ float2 unpackBf16x2(uint32_t bits) {
-    __nv_bfloat162 h;
-    *reinterpret_cast<uint32_t*>(&h) = bits;
-    return __bfloat1622float2(h);
+    return make_float2(__uint_as_float(bits << 16), __uint_as_float(bits & 0xffff0000u));
 }
 
+// Round-to-nearest-even of (a, b) to a bf16 pair, a in the low half.
 __device__ __forceinline__ uint32_t packBf16x2(float a, float b) {
-    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<const uint32_t*>(&h);
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+    return r;
 }
 
-// The compact update of 8 parameters at element offset `at` (32-byte
-// aligned in P, 16-byte in the bf16 copy) from their summed gradients g:
-// the owner's own f32 parameters (and velocities) are updated in place, and
-// the bf16 copy is written to every rank.
-__device__ __forceinline__ void updateCompact8(const Params& p, uint64_t at, const float (&g)[8], bool multicast) {
+// The compact update of 4 parameters at element offset `at` (16-byte
+// aligned) from their summed gradients g: the owner's own f32 parameters (and
+// velocities) are updated in place; returns their bf16 rounding, packed.
+__device__ __forceinline__ uint2 updateCompact4(const Params& p, uint64_t at, float g0, float g1, float g2, float g3) {
     float* own = p.pPeers[p.rank] + at;
-    float4 w[2] = {__ldcg(reinterpret_cast<const float4*>(own)), __ldcg(reinterpret_cast<const float4*>(own + 4))};
-    float* wv = reinterpret_cast<float*>(w);
+    float4 w = __ldcg(reinterpret_cast<const float4*>(own));
     if (p.velocity) {
-        float4 m[2] = {*reinterpret_cast<const float4*>(p.velocity + at),
-                       *reinterpret_cast<const float4*>(p.velocity + at + 4)};
-        float* mv = reinterpret_cast<float*>(m);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) wv[e] = sgdStep(wv[e], g[e], &mv[e], p.lr, p.mu);
-        *reinterpret_cast<float4*>(p.velocity + at) = m[0];
-        *reinterpret_cast<float4*>(p.velocity + at + 4) = m[1];
+        float4 m = *reinterpret_cast<const float4*>(p.velocity + at);
+        w.x = sgdStep(w.x, g0, &m.x, p.lr, p.mu);
+        w.y = sgdStep(w.y, g1, &m.y, p.lr, p.mu);
+        w.z = sgdStep(w.z, g2, &m.z, p.lr, p.mu);
+        w.w = sgdStep(w.w, g3, &m.w, p.lr, p.mu);
+        *reinterpret_cast<float4*>(p.velocity + at) = m;
     } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) wv[e] = sgdStep(wv[e], g[e], nullptr, p.lr, p.mu);
+        w.x = sgdStep(w.x, g0, nullptr, p.lr, p.mu);
+        w.y = sgdStep(w.y, g1, nullptr, p.lr, p.mu);
+        w.z = sgdStep(w.z, g2, nullptr, p.lr, p.mu);
+        w.w = sgdStep(w.w, g3, nullptr, p.lr, p.mu);
     }
-    *reinterpret_cast<float4*>(own) = w[0];
-    *reinterpret_cast<float4*>(own + 4) = w[1];
-    const uint4 b = make_uint4(packBf16x2(wv[0], wv[1]), packBf16x2(wv[2], wv[3]), packBf16x2(wv[4], wv[5]),
-                               packBf16x2(wv[6], wv[7]));
+    *reinterpret_cast<float4*>(own) = w;
+    return make_uint2(packBf16x2(w.x, w.y), packBf16x2(w.z, w.w));
+}
+
+// The compact update of 8 parameters at `at` (32-byte aligned in P, 16-byte
+// in the bf16 copy), gradients as 4 packed bf16 pairs (the switch's sums) or
+// as 8 floats: the owner's f32 parameters are updated, the bf16 copy is
+// written to every rank.
+__device__ __forceinline__ void storeCompactCopy(const Params& p, uint64_t at, const uint2& lo, const uint2& hi,
+                                                 bool multicast) {
     if (multicast) {
-        asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(p.pbMc + at), "r"(b.x),
-                     "r"(b.y), "r"(b.z), "r"(b.w)
+        asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(p.pbMc + at), "r"(lo.x),
+                     "r"(lo.y), "r"(hi.x), "r"(hi.y)
                      : "memory");
     } else {
+        const uint4 b = make_uint4(lo.x, lo.y, hi.x, hi.y);
         for (uint32_t k = 0; k < p.world; ++k) __stcg(reinterpret_cast<uint4*>(p.pbPeers[k] + at), b);
     }
+}
+
+__device__ __forceinline__ void updateCompact8(const Params& p, uint64_t at, const uint4& sums) {
+    float2 a = unpackBf16x2(sums.x), b = unpackBf16x2(sums.y);
+    const uint2 lo = updateCompact4(p, at, a.x, a.y, b.x, b.y);
+    a = unpackBf16x2(sums.z);
+    b = unpackBf16x2(sums.w);
+    const uint2 hi = updateCompact4(p, at + 4, a.x, a.y, b.x, b.y);
+    storeCompactCopy(p, at, lo, hi, true);
+}
+
+__device__ __forceinline__ void updateCompact8(const Params& p, uint64_t at, const float (&g)[8]) {
+    const uint2 lo = updateCompact4(p, at, g[0], g[1], g[2], g[3]);
+    const uint2 hi = updateCompact4(p, at + 4, g[4], g[5], g[6], g[7]);
+    storeCompactCopy(p, at, lo, hi, false);
 }
 
 // Full-width rows of an owned tile in compact form: lane takes the 8
@@ -578,7 +601,7 @@ __device__ __forceinline__ void updateCompact8(const Params& p, uint64_t at, con
 // them one row at a time; peer mode sums kCompactPeerRows rows of every rank
 // in f32, in rank order. (The row counts keep the reducer inside the
 // kernel's register budget.)
-constexpr uint32_t kCompactSwitchRows = 2;
+constexpr uint32_t kCompactSwitchRows = 4;
 constexpr uint32_t kCompactPeerRows = 1;
 
 __device__ __forceinline__ void unpack8(const uint4& v, float (&g)[8]) {
@@ -605,13 +628,8 @@ __device__ __forceinline__ void compactReduceRows(const Params& p, uint64_t offs
                                  : "memory");
             }
 #pragma unroll
-            for (uint32_t i = 0; i < kCompactSwitchRows; ++i) {
-                if (r0 + i < rows) {
-                    float g[8];
-                    unpack8(v[i], g);
-                    updateCompact8(p, offset + (r0 + i) * p.ldc + 8u * lane, g, true);
-                }
-            }
+            for (uint32_t i = 0; i < kCompactSwitchRows; ++i)
+                if (r0 + i < rows) updateCompact8(p, offset + (r0 + i) * p.ldc + 8u * lane, v[i]);
         }
         return;
     }
@@ -637,7 +655,7 @@ __device__ __forceinline__ void compactReduceRows(const Params& p, uint64_t offs
         }
 #pragma unroll
         for (uint32_t i = 0; i < kCompactPeerRows; ++i)
-            if (r0 + i < rows) updateCompact8(p, offset + (r0 + i) * p.ldc + 8u * lane, acc[i], false);
+            if (r0 + i < rows) updateCompact8(p, offset + (r0 + i) * p.ldc + 8u * lane, acc[i]);
     }
 }
 
