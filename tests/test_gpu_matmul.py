@@ -120,3 +120,18 @@ def test_transformer_example_region(device):
         # above), so the block is held to 2e-2 in relative Frobenius norm.
         fast = regions.transformer_block(exact=False).compile(device).execute(inputs)
         assert np.linalg.norm(fast.astype(np.float64) - want) <= 2e-2 * np.linalg.norm(want.astype(np.float64))
+
+
+@pytest.mark.parametrize("m,k,n", [(0, 5, 3), (4, 0, 3), (4, 5, 0), (0, 0, 0)])
+def test_matmul_empty_extents(device, m, k, n):
+    """Empty extents: an empty result, or K = 0 giving zeros (the Evaluator's
+    accumulators start at 0), in every form."""
+    for dtype, exact in ((thb.F32, True), (thb.F32, False), (thb.I64, False)):
+        np_type = np.int64 if dtype == thb.I64 else np.float32
+        a, b = np.ones((m, k), np_type), np.ones((k, n), np_type)
+        spec = regions.matmul(dtype, exact)
+        out = spec.compile(device).execute([a, b])
+        want = orc.region_eval(spec, [a, b])
+        assert out.shape == want.shape == (m, n)
+        np.testing.assert_array_equal(out, want)
+        assert not out.any()

@@ -149,3 +149,13 @@ def test_sum_i64_prefix_overflow(device, fixtures):
     with pytest.raises(thb.GpuError) as err:
         _sum_i64_region("total").compile(device).execute([x])
     assert err.value.code == fixtures["sum_i64_prefix_overflow"]
+
+
+def test_sum_i64_empty(device):
+    """Sums over empty extents are 0 (the reference's accumulator starts at
+    0): zero columns, zero rows, an empty vector."""
+    rows = _sum_i64_region("rows").compile(device)
+    np.testing.assert_array_equal(rows.execute([np.zeros((3, 0), np.int64)]), np.zeros(3, np.int64))
+    cols = _sum_i64_region("cols").compile(device)
+    np.testing.assert_array_equal(cols.execute([np.zeros((0, 4), np.int64)]), np.zeros(4, np.int64))
+    assert _sum_i64_region("total").compile(device).execute([np.zeros(0, np.int64)]) == 0
