@@ -73,3 +73,20 @@ def test_two_gloo_ranks(tmp_path):
     result = tmp_path / "result.txt"
     mp.start_processes(_worker, args=(2, free_port(), str(result)), nprocs=2, join=True, start_method="spawn")
     assert result.read_text() == "ok"
+
+
+def test_compact_reduction_needs_the_fused_update():
+    """The bf16 sharded form keeps each tile's f32 weights on its owner, so
+    it is refused without the update in the reduction (before any buffer is
+    made)."""
+    import torch.distributed as dist
+    from thiran_b200.distributed import FusedGradientAllReduce
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(free_port()))
+    dist.init_process_group("gloo", rank=0, world_size=1)
+    try:
+        with pytest.raises(ValueError):
+            FusedGradientAllReduce(object(), dist, mode="switch", update=False, compact=True)
+        with pytest.raises(ValueError):
+            FusedGradientAllReduce(object(), dist, mode="ring")
+    finally:
+        dist.destroy_process_group()
